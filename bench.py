@@ -1,0 +1,331 @@
+#!/usr/bin/env python
+"""Rollout throughput of the B200 engine on the headline configuration.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nnodes=1 --nproc-per-node N ... bench.py --gpus N ...      (one rank per GPU)
+
+A "step" is one ``engine.generate`` call over one batch of the workload: packed prefill of the
+batch's prompts, then ``new_tokens`` decode steps with sampling and sampled-token log-probs.
+Workload (default "bf16-b64x512"): LFM2.5-1.2B architecture, random-init bf16 weights, 64 prompts of
+uniform-random ids with lengths uniform in [64, 1024], 512 sampled tokens each (temperature 1,
+full support, EOS ignored), CUDA-graph decode. With N > 1 every rank runs its own replica on its
+own 64 prompts (weak scaling, no data-path collective); rank 0 broadcasts the policy weights over
+NCCL once before the warm-up, as it does before each rollout in training.
+
+Prints ONE JSON line. ``value`` times the steps with inputs resident in HBM; ``e2e`` repeats them
+through the public API with pinned-host prompts and a device->host read of tokens, log-probs and
+lengths inside the timed region (the reference benchmark's convention). ``roofline`` is the decode
+step graph: algorithmic bytes (weights + KV history per step) over its CUDA-event duration against
+the measured HBM copy bandwidth. ``cpu_baseline`` times the CPU oracle on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "generated tokens/s"
+UNIT = "tokens/s"
+
+WORKLOADS = {
+    # name: (model, batch, prompt_low, prompt_high, new_tokens, graph options)
+    "bf16-b64x512": ("1p2b", 64, 64, 1024, 512, {}),
+    "fp8-b64x512": ("1p2b", 64, 64, 1024, 512, {"fp8_mlp": True, "fp8_kv": True}),
+    "tiny": ("tiny", 8, 8, 64, 32, {}),
+}
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured (MEASURED_PEAKS.json)"
+    return 6650.0, "fallback (earlier measurement on this pool)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index, self.lines, self.proc = gpu_index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu_index)], stdout=subprocess.PIPE, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *_):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, sm_max, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(sm_max) if sm_max else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_engine(model: str, device, options: dict, max_model_len: int, seed: int = 0):
+    import torch
+    from climbing_gym_b200 import synthetic
+    from climbing_gym_b200.engine import LFM25Engine
+
+    cfg = synthetic.tiny_config() if model == "tiny" else synthetic.lfm25_1p2b_config()
+    state = synthetic.make_state_dict_on_device(cfg, seed, device, torch.bfloat16)
+    engine = LFM25Engine.from_state_dict(cfg, state, device=device, dtype=torch.bfloat16, max_model_len=max_model_len)
+    del state
+    engine.enable_cuda_graphs(max_graphs=1, **options)
+    return engine, cfg
+
+
+def weight_bytes(engine, options: dict) -> int:
+    """Bytes of weights one decode step streams (tied embedding counted once, as the LM head)."""
+    total = 0
+    fp8 = bool(options.get("fp8_mlp"))
+    w = engine.weights
+    total += w.lm_head_weight.numel() * w.lm_head_weight.element_size()
+    total += w.embedding_norm_weight.numel() * 2
+    for layer in w.layers:
+        for t in (layer.w13_weight, layer.w2_weight):
+            total += t.numel() * (1 if fp8 else t.element_size()) + (t.size(0) * 4 if fp8 else 0)
+        total += (layer.operator_norm_weight.numel() + layer.ffn_norm_weight.numel()) * 2
+        if layer.attention is not None:
+            a = layer.attention
+            total += sum(t.numel() * t.element_size() for t in (a.qkv_weight, a.out_weight, a.q_norm_weight, a.k_norm_weight))
+        else:
+            c = layer.conv
+            total += sum(t.numel() * t.element_size() for t in (c.in_weight, c.conv_weight, c.out_weight))
+    return total
+
+
+def run_ours(args) -> dict:
+    import torch
+    import torch.distributed as dist
+    from climbing_gym_b200 import _native as nv, synthetic
+    from climbing_gym_b200.config import LFM25SamplingConfig
+    from climbing_gym_b200.engine import flatten_token_batches
+    from climbing_gym_b200.replica import broadcast_policy_weights
+
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if not torch.cuda.is_available():
+        raise RuntimeError("bench.py needs a CUDA device: the engine has no CPU path")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    model, batch, low, high, new_tokens, options = WORKLOADS[args.workload]
+    batch = args.batch or batch
+    new_tokens = args.new_tokens or new_tokens
+    engine, cfg = build_engine(model, device, options, max_model_len=high + new_tokens + 64)
+    broadcast_ms = None
+    if world > 1:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        moved = broadcast_policy_weights(engine, src=0)
+        torch.cuda.synchronize()
+        broadcast_ms = (time.perf_counter() - t0) * 1e3
+    prompts = synthetic.uniform_prompts(batch, low, high, cfg.vocab_size, seed=1000 + rank)
+    flat_host = flatten_token_batches(prompts, device="cpu")
+    ids_pinned, cu_pinned = flat_host[0].pin_memory(), flat_host[1].pin_memory()
+    ids_dev, cu_dev = ids_pinned.to(device), cu_pinned.to(device)
+    max_len = flat_host[2]
+    sampling = LFM25SamplingConfig(temperature=1.0, top_k=0, top_p=1.0, max_new_tokens=new_tokens, seed=0,
+                                   ignore_eos=True, return_logprobs=True)
+    decoder = engine._cuda_decoder
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def timed(fn, steps):
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        barrier()
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    outputs = {}
+
+    def step_resident():
+        outputs["last"] = engine.generate(ids_dev, cu_dev, max_len, repeats=1, sampling=sampling)
+
+    def step_e2e():
+        out = engine.generate(ids_pinned.to(device, non_blocking=True), cu_pinned, max_len, repeats=1, sampling=sampling)
+        outputs["host"] = (out.token_ids.cpu(), out.logprobs.cpu(), out.lengths.cpu())
+
+    for _ in range(args.warmup):
+        step_resident()
+    launches_before = nv.launch_count()
+    decoder.profile_decode, decoder.decode_profile = True, []
+    with ClockSampler(local_rank) as clocks:
+        total_ms = timed(step_resident, args.steps)
+    decoder.profile_decode = False
+    launches = nv.launch_count() - launches_before
+    decode_ms = sum(s.elapsed_time(e) for s, e, _ in decoder.decode_profile)
+    decode_replays = sum(n for _, _, n in decoder.decode_profile)
+    e2e_ms = timed(step_e2e, args.steps)
+    tokens_per_step = batch * new_tokens
+    lengths = outputs["last"].lengths
+    if int(lengths.sum()) != tokens_per_step or not bool(torch.isfinite(outputs["last"].logprobs).all()):
+        raise RuntimeError("generate returned an incomplete budget or non-finite log-probs")
+    value = world * tokens_per_step * args.steps / (total_ms / 1e3)
+    e2e_value = world * tokens_per_step * args.steps / (e2e_ms / 1e3)
+
+    # decode roofline: weights + KV history per step (algorithmic bytes), HBM-bound
+    w_bytes = weight_bytes(engine, options)
+    n_attn = engine.weights.num_attention_layers
+    kv_elem = 1 if options.get("fp8_kv") else 2
+    kv_tok = n_attn * 2 * cfg.num_key_value_heads * (cfg.head_dim * kv_elem + (4 if options.get("fp8_kv") else 0))
+    prompt_total = sum(len(p) for p in prompts)
+    # replay j (1-based) reads, per row, its prompt plus j generated tokens
+    kv_bytes_avg = kv_tok * (prompt_total + batch * (new_tokens) / 2.0)
+    bytes_per_replay = w_bytes + kv_bytes_avg
+    peak, peak_source = peaks()
+    roofline = None
+    if decode_replays:
+        step_ms = decode_ms / decode_replays
+        achieved = bytes_per_replay / (step_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "decode step graph (all kernels of one token step)",
+                    "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "peak_source": peak_source, "traffic": None, "ms_per_launch": round(step_ms, 4),
+                    "algorithmic_bytes_per_launch": int(bytes_per_replay), "launches_timed": decode_replays,
+                    "decode_share_of_step": round(decode_ms / total_ms, 4)}
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if not options else "bf16+e4m3", "data": "synthetic",
+        "config": {"workload": args.workload, "model": "LFM2.5-1.2B architecture, random init" if model == "1p2b" else "tiny hybrid",
+                   "batch_per_gpu": batch, "prompt_lengths": f"uniform[{low},{high}]", "new_tokens": new_tokens,
+                   "sampling": "temperature 1, full support, ignore_eos", "replicas": world,
+                   "l2": "working set per decode step (weights + KV) is far larger than the 126 MB L2"},
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": int(ids_pinned.numel() * 8 + cu_pinned.numel() * 4),
+                "d2h_bytes_per_step": int(tokens_per_step * 12 + batch * 4), "ms_per_step": round(e2e_ms / args.steps, 3)},
+        "gpu_launches": int(launches), "clocks": clocks.summary(), "roofline": roofline,
+    }
+    if broadcast_ms is not None:
+        result["weight_broadcast"] = {"ms": round(broadcast_ms, 2), "bytes": int(moved)}
+    if world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(model, seconds_budget=args.cpu_seconds)
+    if world > 1:
+        dist.destroy_process_group()
+    return result if rank == 0 else {}
+
+
+def cpu_baseline(model: str, *, seconds_budget: float = 25.0, steps: int = 1) -> dict:
+    """The CPU oracle (numpy restatement of the reference's eager engine) on a bounded sample of the
+    workload: 8 prompts of 64 tokens, 16 sampled tokens each, fp32 on the host cores."""
+    import numpy as np
+    from climbing_gym_b200 import synthetic
+    from oracle.lfm25_oracle import OracleConfig, OracleEngine, OracleSampling
+
+    cfg = synthetic.tiny_config() if model == "tiny" else synthetic.lfm25_1p2b_config()
+    state = synthetic.make_state_dict(cfg, seed=0)
+    ocfg = OracleConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size, mlp_hidden_size=cfg.mlp_hidden_size,
+                        num_attention_heads=cfg.num_attention_heads, num_key_value_heads=cfg.num_key_value_heads,
+                        layer_types=tuple(cfg.layer_types), rope_theta=cfg.rope_theta, norm_eps=cfg.norm_eps,
+                        conv_kernel_size=cfg.conv_kernel_size, eos_token_id=cfg.eos_token_id)
+    oracle = OracleEngine(ocfg, state, dtype="fp32", max_model_len=256)
+    del state
+    n_prompts, prompt_len, new_tokens = 8, 64, 16
+    prompts = synthetic.uniform_prompts(n_prompts, prompt_len, prompt_len, cfg.vocab_size, seed=7)
+    sampling = OracleSampling(temperature=1.0, max_new_tokens=new_tokens, seed=0, ignore_eos=True)
+    t0 = time.perf_counter()
+    done = 0
+    for _ in range(steps):
+        out = oracle.generate(prompts, 1, sampling)
+        done += int(out["lengths"].sum())
+        if time.perf_counter() - t0 > seconds_budget:
+            break
+    seconds = time.perf_counter() - t0
+    return {"value": round(done / seconds, 2), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_prompts} prompts x {prompt_len} tokens, {new_tokens} sampled tokens each, fp32 numpy oracle "
+                      f"(multi-threaded BLAS), {seconds:.1f} s", "seconds": round(seconds, 2)}
+
+
+def run_reference(args) -> dict:
+    """The reference's CPU implementation of the path, as restated by the oracle port, on host cores."""
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return {}
+    model = WORKLOADS[args.workload][0]
+    t0 = time.perf_counter()
+    base = cpu_baseline(model, seconds_budget=args.cpu_seconds * max(1, args.steps), steps=args.warmup + args.steps)
+    model_name, batch, low, high, new_tokens, _ = WORKLOADS[args.workload]
+    return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(base["seconds"] * 1e3 / max(1, args.steps), 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "model": "LFM2.5-1.2B architecture, random init" if model_name == "1p2b" else "tiny hybrid",
+                       "note": "the reference is Python and cannot travel to the GPU box; its CPU engine is timed through "
+                               "the numpy port pinned to it by tests/golden (bounded sample of the workload)"},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0, "wall_seconds": round(time.perf_counter() - t0, 1)}
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=3)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    parser.add_argument("--workload", default="bf16-b64x512", choices=sorted(WORKLOADS))
+    parser.add_argument("--batch", type=int, default=0, help="override prompts per GPU")
+    parser.add_argument("--new-tokens", type=int, default=0, help="override sampled tokens per prompt")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cpu-seconds", type=float, default=25.0)
+    args = parser.parse_args()
+    result = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if result:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

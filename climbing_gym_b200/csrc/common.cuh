@@ -1,0 +1,101 @@
+// Shared device/host helpers for the cgym_b200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/cgym_b200.h"
+
+namespace cgym {
+
+// ---- error reporting -------------------------------------------------------------------
+// One message buffer per host thread: the adapter calls from executor threads, and an error
+// string must not be overwritten by another thread between the failing call and the read.
+char* error_buffer();
+int fail(const char* fmt, ...);
+int check_launch(const char* what, int kernels = 1);
+
+#define CGYM_REQUIRE(cond, ...)             \
+  do {                                      \
+    if (!(cond)) return ::cgym::fail(__VA_ARGS__); \
+  } while (0)
+
+inline cudaStream_t as_stream(cgym_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---- element types ---------------------------------------------------------------------
+// load / store convert through fp32; store rounds to nearest even for bf16 (cvt.rn), which is
+// the cast the reference applies at every rounding point.
+template <typename T>
+struct Elem;
+template <>
+struct Elem<float> {
+  static __device__ __forceinline__ float load(const float* p) { return *p; }
+  static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+  static __device__ __forceinline__ float round(float v) { return v; }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+};
+
+// fp32 -> e4m3 code, round-to-nearest-even, saturating to +-448 (cvt.rn.satfinite.e4m3x2.f32).
+__device__ __forceinline__ uint8_t to_e4m3(float v) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+__device__ __forceinline__ float from_e4m3(uint8_t code) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
+  return __half2float(*reinterpret_cast<__half*>(&h));
+}
+
+// ---- reductions ------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// Block-wide reductions over <= 1024 threads; `scratch` holds 32 floats. All threads get the result.
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float r = (lane < nwarps) ? scratch[lane] : 0.0f;
+  return warp_sum(r);
+}
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float r = (lane < nwarps) ? scratch[lane] : -INFINITY;
+  return warp_max(r);
+}
+
+// ---- paged KV addressing ---------------------------------------------------------------
+// pool[layer][page][k|v][kv_head][token][dim]
+__host__ __device__ __forceinline__ int64_t kv_elem_offset(const cgym_kv_layout& kv, int layer, int page,
+                                                           int which, int head, int token) {
+  int64_t idx = (((static_cast<int64_t>(layer) * kv.n_pages + page) * 2 + which) * kv.n_kv_heads + head);
+  return (idx * kv.page_size + token) * kv.head_dim;
+}
+__host__ __device__ __forceinline__ int64_t kv_scale_offset(const cgym_kv_layout& kv, int layer, int page,
+                                                            int which, int head, int token) {
+  int64_t idx = (((static_cast<int64_t>(layer) * kv.n_pages + page) * 2 + which) * kv.n_kv_heads + head);
+  return idx * kv.page_size + token;
+}
+
+}  // namespace cgym

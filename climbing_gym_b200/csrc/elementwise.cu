@@ -1,0 +1,432 @@
+// HBM-bound row kernels of the LFM2.5 decode / prefill step: embedding gather, RMSNorm
+// (+residual, +e4m3 quantisation), SwiGLU (+quantisation), row quantisation, gated
+// short-convolution state update (decode) and packed causal conv (prefill), QK-norm + RoPE +
+// paged KV append, and target log-prob gathering for completion scoring.
+//
+// Every kernel is one pass over its rows: reads each input once with 16-byte-friendly
+// coalesced accesses, keeps the row in registers/shared memory, and applies the model-dtype
+// rounding at the points listed in include/cgym_b200.h.
+#include "common.cuh"
+
+namespace cgym {
+
+// ------------------------------------------------------------------------------------------
+// embedding
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void embedding_kernel(T* __restrict__ out, const T* __restrict__ table,
+                                 const int64_t* __restrict__ tokens, int hidden, int vocab) {
+  const int row = blockIdx.x;
+  int64_t tok = tokens[row];
+  if (tok < 0 || tok >= vocab) tok = 0;  // padding rows carry arbitrary ids; never index outside the table
+  const T* src = table + tok * hidden;
+  T* dst = out + static_cast<int64_t>(row) * hidden;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = src[i];
+}
+
+// ------------------------------------------------------------------------------------------
+// RMSNorm (+ residual) (+ e4m3 row quantisation)
+// ------------------------------------------------------------------------------------------
+template <typename T, bool QUANT>
+__global__ void rmsnorm_kernel(T* __restrict__ y, uint8_t* __restrict__ q, float* __restrict__ scales,
+                               T* __restrict__ sum_out, const T* __restrict__ x,
+                               const T* __restrict__ residual, const T* __restrict__ w, int hidden,
+                               float eps) {
+  extern __shared__ float row_buf[];  // hidden floats
+  __shared__ float scratch[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * hidden;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float v = Elem<T>::load(x + base + i);
+    if (residual != nullptr) {
+      v = Elem<T>::round(__fadd_rn(v, Elem<T>::load(residual + base + i)));
+      Elem<T>::store(sum_out + base + i, v);
+    }
+    row_buf[i] = v;
+    ss = fmaf(v, v, ss);
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = rsqrtf(total / static_cast<float>(hidden) + eps);
+  float amax = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float n = Elem<T>::round(__fmul_rn(row_buf[i], inv));
+    const float v = Elem<T>::round(__fmul_rn(n, Elem<T>::load(w + i)));
+    if (QUANT) {
+      row_buf[i] = v;
+      amax = fmaxf(amax, fabsf(v));
+    } else {
+      Elem<T>::store(y + base + i, v);
+    }
+  }
+  if (QUANT) {
+    amax = block_max(amax, scratch);
+    const float scale = fmaxf(amax / 448.0f, 1.0e-12f);
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+      const float s = fminf(fmaxf(__fdiv_rn(row_buf[i], scale), -448.0f), 448.0f);
+      q[base + i] = to_e4m3(s);
+    }
+    if (threadIdx.x == 0) scales[blockIdx.x] = scale;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// SwiGLU (+ quantisation)
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float swiglu_value(float gate, float up) {
+  const float act = Elem<T>::round(__fdiv_rn(gate, __fadd_rn(1.0f, expf(-gate))));
+  return Elem<T>::round(__fmul_rn(act, up));
+}
+
+template <typename T>
+__global__ void swiglu_kernel(T* __restrict__ y, const T* __restrict__ gate_up, int ffn) {
+  const int64_t row = blockIdx.y;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= ffn) return;
+  const float gate = Elem<T>::load(gate_up + row * 2 * ffn + col);
+  const float up = Elem<T>::load(gate_up + row * 2 * ffn + ffn + col);
+  Elem<T>::store(y + row * ffn + col, swiglu_value<T>(gate, up));
+}
+
+template <typename T>
+__global__ void swiglu_quant_kernel(uint8_t* __restrict__ q, float* __restrict__ scales,
+                                    const T* __restrict__ gate_up, int ffn) {
+  extern __shared__ float row_buf[];
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  float amax = 0.0f;
+  for (int i = threadIdx.x; i < ffn; i += blockDim.x) {
+    const float v = swiglu_value<T>(Elem<T>::load(gate_up + row * 2 * ffn + i),
+                                    Elem<T>::load(gate_up + row * 2 * ffn + ffn + i));
+    row_buf[i] = v;
+    amax = fmaxf(amax, fabsf(v));
+  }
+  amax = block_max(amax, scratch);
+  const float scale = fmaxf(amax / 448.0f, 1.0e-12f);
+  for (int i = threadIdx.x; i < ffn; i += blockDim.x)
+    q[row * ffn + i] = to_e4m3(fminf(fmaxf(__fdiv_rn(row_buf[i], scale), -448.0f), 448.0f));
+  if (threadIdx.x == 0) scales[row] = scale;
+}
+
+template <typename T>
+__global__ void quantize_rows_kernel(uint8_t* __restrict__ q, float* __restrict__ scales,
+                                     const T* __restrict__ x, int width) {
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  float amax = 0.0f;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) amax = fmaxf(amax, fabsf(Elem<T>::load(x + row * width + i)));
+  amax = block_max(amax, scratch);
+  const float scale = fmaxf(amax / 448.0f, 1.0e-12f);
+  for (int i = threadIdx.x; i < width; i += blockDim.x)
+    q[row * width + i] = to_e4m3(fminf(fmaxf(__fdiv_rn(Elem<T>::load(x + row * width + i), scale), -448.0f), 448.0f));
+  if (threadIdx.x == 0) scales[row] = scale;
+}
+
+// ------------------------------------------------------------------------------------------
+// gated short convolution, kernel size 3
+// ------------------------------------------------------------------------------------------
+// decode: state [n_slots][3][hidden], tap 2 is the newest
+template <typename T>
+__global__ void conv_update_kernel(T* __restrict__ y, T* __restrict__ state, const T* __restrict__ bcx,
+                                   const T* __restrict__ conv_w, const uint8_t* __restrict__ active,
+                                   const int32_t* __restrict__ slots, int hidden) {
+  const int row = blockIdx.y;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= hidden) return;
+  int slot = slots != nullptr ? slots[row] : row;
+  if (slot < 0) slot = 0;
+  const T* in = bcx + static_cast<int64_t>(row) * 3 * hidden;
+  const float b = Elem<T>::load(in + col), c = Elem<T>::load(in + hidden + col), x = Elem<T>::load(in + 2 * hidden + col);
+  const float bx = Elem<T>::round(__fmul_rn(b, x));
+  T* st = state + static_cast<int64_t>(slot) * 3 * hidden;
+  const float s0 = Elem<T>::load(st + hidden + col), s1 = Elem<T>::load(st + 2 * hidden + col);
+  const float w0 = Elem<T>::load(conv_w + col * 3), w1 = Elem<T>::load(conv_w + col * 3 + 1), w2 = Elem<T>::load(conv_w + col * 3 + 2);
+  const float p0 = Elem<T>::round(__fmul_rn(s0, w0)), p1 = Elem<T>::round(__fmul_rn(s1, w1)), p2 = Elem<T>::round(__fmul_rn(bx, w2));
+  const float conv = Elem<T>::round(__fadd_rn(__fadd_rn(p0, p1), p2));
+  if (active == nullptr || active[row]) {
+    Elem<T>::store(st + col, s0);
+    Elem<T>::store(st + hidden + col, s1);
+    Elem<T>::store(st + 2 * hidden + col, bx);
+  }
+  Elem<T>::store(y + static_cast<int64_t>(row) * hidden + col, Elem<T>::round(__fmul_rn(c, conv)));
+}
+
+__device__ __forceinline__ int find_sequence(const int32_t* cu, int n_seqs, int row) {
+  int lo = 0, hi = n_seqs - 1;  // largest s with cu[s] <= row
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= row) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// prefill: history value b*x at chunk-local time t (t < 0 reads the slot's carried taps)
+template <typename T>
+__device__ __forceinline__ float conv_history(const T* __restrict__ bcx, const T* __restrict__ st, int seq_begin,
+                                              int t, bool carried, int hidden, int col) {
+  if (t >= 0) {
+    const T* in = bcx + static_cast<int64_t>(seq_begin + t) * 3 * hidden;
+    return Elem<T>::round(__fmul_rn(Elem<T>::load(in + col), Elem<T>::load(in + 2 * hidden + col)));
+  }
+  return carried ? Elem<T>::load(st + (3 + t) * hidden + col) : 0.0f;  // t in [-3, -1] -> tap 3+t
+}
+
+template <typename T>
+__global__ void conv_prefill_kernel(T* __restrict__ y, const T* __restrict__ state, const T* __restrict__ bcx,
+                                    const T* __restrict__ conv_w, const int32_t* __restrict__ cu,
+                                    const int32_t* __restrict__ seq_slots, const int32_t* __restrict__ seq_starts,
+                                    int n_seqs, int hidden) {
+  const int row = blockIdx.y;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= hidden) return;
+  const int seq = find_sequence(cu, n_seqs, row);
+  const int begin = cu[seq], t = row - begin;
+  const bool carried = seq_starts[seq] > 0;
+  const T* st = state + static_cast<int64_t>(seq_slots[seq]) * 3 * hidden;
+  const float h0 = conv_history<T>(bcx, st, begin, t - 2, carried, hidden, col);
+  const float h1 = conv_history<T>(bcx, st, begin, t - 1, carried, hidden, col);
+  const float h2 = conv_history<T>(bcx, st, begin, t, carried, hidden, col);
+  const float w0 = Elem<T>::load(conv_w + col * 3), w1 = Elem<T>::load(conv_w + col * 3 + 1), w2 = Elem<T>::load(conv_w + col * 3 + 2);
+  // exact products, fp32 sum in tap order, one rounding
+  const float conv = Elem<T>::round(__fadd_rn(__fadd_rn(__fmul_rn(h0, w0), __fmul_rn(h1, w1)), __fmul_rn(h2, w2)));
+  const float c = Elem<T>::load(bcx + static_cast<int64_t>(row) * 3 * hidden + hidden + col);
+  Elem<T>::store(y + static_cast<int64_t>(row) * hidden + col, Elem<T>::round(__fmul_rn(c, conv)));
+}
+
+// runs after conv_prefill_kernel on the same stream: the slot's taps become the last three
+// history values of its chunk
+template <typename T>
+__global__ void conv_prefill_state_kernel(T* __restrict__ state, const T* __restrict__ bcx,
+                                          const int32_t* __restrict__ cu, const int32_t* __restrict__ seq_slots,
+                                          const int32_t* __restrict__ seq_starts, int hidden) {
+  const int seq = blockIdx.y;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= hidden) return;
+  const int begin = cu[seq], len = cu[seq + 1] - begin;
+  const bool carried = seq_starts[seq] > 0;
+  T* st = state + static_cast<int64_t>(seq_slots[seq]) * 3 * hidden;
+  float taps[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) taps[j] = conv_history<T>(bcx, st, begin, len - 3 + j, carried, hidden, col);
+#pragma unroll
+  for (int j = 0; j < 3; ++j) Elem<T>::store(st + j * hidden + col, taps[j]);
+}
+
+// ------------------------------------------------------------------------------------------
+// QK-norm + RoPE + paged KV append
+// ------------------------------------------------------------------------------------------
+// grid (rows, Hq + Hkv), block = head_dim threads. K-head blocks also move the V head.
+template <typename T, typename KV>
+__global__ void qk_rope_append_kernel(T* __restrict__ q_out, T* __restrict__ k_new, T* __restrict__ v_new,
+                                      const T* __restrict__ qkv, const T* __restrict__ q_w,
+                                      const T* __restrict__ k_w, const float* __restrict__ rope_cos,
+                                      const float* __restrict__ rope_sin, const int32_t* __restrict__ positions,
+                                      const int32_t* __restrict__ slots, const uint8_t* __restrict__ active,
+                                      cgym_kv_layout kv, int layer, int n_q_heads, float eps, int32_t* status) {
+  __shared__ float buf[256];
+  __shared__ float scratch[32];
+  const int row = blockIdx.x, head = blockIdx.y, d = threadIdx.x, D = kv.head_dim, half = D >> 1;
+  const int n_kv = kv.n_kv_heads;
+  const int width = (n_q_heads + 2 * n_kv) * D;
+  const bool is_q = head < n_q_heads;
+  const float x = Elem<T>::load(qkv + static_cast<int64_t>(row) * width + head * D + d);
+  const float ms = block_sum(x * x, scratch) / static_cast<float>(D);
+  float n = Elem<T>::round(__fmul_rn(x, rsqrtf(ms + eps)));
+  n = Elem<T>::round(__fmul_rn(n, Elem<T>::load((is_q ? q_w : k_w) + d)));
+  buf[d] = n;
+  __syncthreads();
+  const float other = buf[d < half ? d + half : d - half];
+  const int pos = positions[row];
+  const float c = Elem<T>::round(rope_cos[static_cast<int64_t>(pos) * half + (d % half)]);
+  const float s = Elem<T>::round(rope_sin[static_cast<int64_t>(pos) * half + (d % half)]);
+  const float left = Elem<T>::round(__fmul_rn(n, c)), right = Elem<T>::round(__fmul_rn(other, s));
+  const float rot = Elem<T>::round(d < half ? __fsub_rn(left, right) : __fadd_rn(left, right));
+  if (is_q) {
+    Elem<T>::store(q_out + (static_cast<int64_t>(row) * n_q_heads + head) * D + d, rot);
+    return;
+  }
+  const int kh = head - n_q_heads;
+  const float v = Elem<T>::load(qkv + static_cast<int64_t>(row) * width + (n_q_heads + n_kv + kh) * D + d);
+  if (k_new != nullptr) {
+    Elem<T>::store(k_new + (static_cast<int64_t>(row) * n_kv + kh) * D + d, rot);
+    Elem<T>::store(v_new + (static_cast<int64_t>(row) * n_kv + kh) * D + d, v);
+  }
+  if (active != nullptr && !active[row]) return;
+  const int slot = slots != nullptr ? slots[row] : row;
+  if (slot < 0) return;
+  const int block = pos / kv.page_size, tok = pos % kv.page_size;
+  const int page = block < kv.max_blocks ? kv.block_table[static_cast<int64_t>(slot) * kv.max_blocks + block] : -1;
+  if (page < 0 || page >= kv.n_pages) {  // uniform across the block
+    if (d == 0) atomicOr(status, CGYM_STATUS_BAD_PAGE);
+    return;
+  }
+  KV* pool = static_cast<KV*>(kv.kv_pool);
+  const int64_t ko = kv_elem_offset(kv, layer, page, 0, kh, tok) + d;
+  const int64_t vo = kv_elem_offset(kv, layer, page, 1, kh, tok) + d;
+  if constexpr (sizeof(KV) == 1) {
+    const float ak = block_max(fabsf(rot), scratch);
+    const float av = block_max(fabsf(v), scratch);
+    const float sk = fmaxf(ak / 448.0f, 1.0e-12f), sv = fmaxf(av / 448.0f, 1.0e-12f);
+    reinterpret_cast<uint8_t*>(pool)[ko] = to_e4m3(__fdiv_rn(rot, sk));
+    reinterpret_cast<uint8_t*>(pool)[vo] = to_e4m3(__fdiv_rn(v, sv));
+    if (d == 0) {
+      kv.kv_scales[kv_scale_offset(kv, layer, page, 0, kh, tok)] = sk;
+      kv.kv_scales[kv_scale_offset(kv, layer, page, 1, kh, tok)] = sv;
+    }
+  } else {
+    Elem<KV>::store(pool + ko, rot);
+    Elem<KV>::store(pool + vo, v);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// logit[target] - logsumexp(logits) per row
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void target_logprob_kernel(float* __restrict__ out, const T* __restrict__ logits,
+                                      const int64_t* __restrict__ targets, int vocab) {
+  __shared__ float scratch[32];
+  const T* row = logits + static_cast<int64_t>(blockIdx.x) * vocab;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, Elem<T>::load(row + i));
+  m = block_max(m, scratch);
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) s += expf(Elem<T>::load(row + i) - m);
+  s = block_sum(s, scratch);
+  if (threadIdx.x == 0) out[blockIdx.x] = Elem<T>::load(row + targets[blockIdx.x]) - (m + logf(s));
+}
+
+}  // namespace cgym
+
+using namespace cgym;
+
+#define DISPATCH_DTYPE(dtype, ...)                                   \
+  if ((dtype) == CGYM_F32) { using T = float; __VA_ARGS__; }         \
+  else if ((dtype) == CGYM_BF16) { using T = __nv_bfloat16; __VA_ARGS__; } \
+  else return fail("unsupported activation dtype %d", (dtype));
+
+extern "C" int cgym_embedding(void* out, const void* table, const int64_t* tokens, int rows, int hidden,
+                              int vocab, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && hidden > 0 && vocab > 0, "embedding: bad shape");
+  if (rows == 0) return 0;
+  DISPATCH_DTYPE(dtype, embedding_kernel<T><<<rows, 256, 0, as_stream(stream)>>>(
+      static_cast<T*>(out), static_cast<const T*>(table), tokens, hidden, vocab));
+  return check_launch("embedding");
+}
+
+extern "C" int cgym_rmsnorm(void* y, void* sum_out, const void* x, const void* residual, const void* w,
+                            int rows, int hidden, float eps, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && hidden > 0 && hidden <= 12288, "rmsnorm: hidden must be in [1, 12288]");
+  CGYM_REQUIRE(residual == nullptr || sum_out != nullptr, "rmsnorm: residual needs sum_out");
+  if (rows == 0) return 0;
+  DISPATCH_DTYPE(dtype, (rmsnorm_kernel<T, false><<<rows, 256, hidden * sizeof(float), as_stream(stream)>>>(
+      static_cast<T*>(y), nullptr, nullptr, static_cast<T*>(sum_out), static_cast<const T*>(x),
+      static_cast<const T*>(residual), static_cast<const T*>(w), hidden, eps)));
+  return check_launch("rmsnorm");
+}
+
+extern "C" int cgym_rmsnorm_quant(uint8_t* q, float* scales, void* sum_out, const void* x, const void* residual,
+                                  const void* w, int rows, int hidden, float eps, cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && hidden > 0 && hidden <= 12288, "rmsnorm_quant: hidden must be in [1, 12288]");
+  CGYM_REQUIRE(residual == nullptr || sum_out != nullptr, "rmsnorm_quant: residual needs sum_out");
+  if (rows == 0) return 0;
+  using T = __nv_bfloat16;
+  rmsnorm_kernel<T, true><<<rows, 256, hidden * sizeof(float), as_stream(stream)>>>(
+      nullptr, q, scales, static_cast<T*>(sum_out), static_cast<const T*>(x), static_cast<const T*>(residual),
+      static_cast<const T*>(w), hidden, eps);
+  return check_launch("rmsnorm_quant");
+}
+
+extern "C" int cgym_swiglu(void* y, const void* gate_up, int rows, int ffn, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && ffn > 0, "swiglu: bad shape");
+  if (rows == 0) return 0;
+  dim3 grid((ffn + 255) / 256, rows);
+  DISPATCH_DTYPE(dtype, swiglu_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(
+      static_cast<T*>(y), static_cast<const T*>(gate_up), ffn));
+  return check_launch("swiglu");
+}
+
+extern "C" int cgym_swiglu_quant(uint8_t* q, float* scales, const void* gate_up, int rows, int ffn,
+                                 cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && ffn > 0 && ffn <= 12288, "swiglu_quant: ffn must be in [1, 12288]");
+  if (rows == 0) return 0;
+  using T = __nv_bfloat16;
+  swiglu_quant_kernel<T><<<rows, 512, ffn * sizeof(float), as_stream(stream)>>>(
+      q, scales, static_cast<const T*>(gate_up), ffn);
+  return check_launch("swiglu_quant");
+}
+
+extern "C" int cgym_quantize_rows(uint8_t* q, float* scales, const void* x, int rows, int width, int dtype,
+                                  cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && width > 0 && width <= 32768, "quantize_rows: FP8 row width must be in [1, 32768]");
+  if (rows == 0) return 0;
+  DISPATCH_DTYPE(dtype, quantize_rows_kernel<T><<<rows, 256, 0, as_stream(stream)>>>(
+      q, scales, static_cast<const T*>(x), width));
+  return check_launch("quantize_rows");
+}
+
+extern "C" int cgym_conv_update(void* y, void* state, const void* bcx, const void* conv_w, const uint8_t* active,
+                                const int32_t* slots, int rows, int hidden, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && hidden > 0, "conv_update: bad shape");
+  if (rows == 0) return 0;
+  dim3 grid((hidden + 255) / 256, rows);
+  DISPATCH_DTYPE(dtype, conv_update_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(
+      static_cast<T*>(y), static_cast<T*>(state), static_cast<const T*>(bcx), static_cast<const T*>(conv_w),
+      active, slots, hidden));
+  return check_launch("conv_update");
+}
+
+extern "C" int cgym_conv_prefill(void* y, void* state, const void* bcx, const void* conv_w,
+                                 const int32_t* cu_seqlens, const int32_t* seq_slots, const int32_t* seq_starts,
+                                 int n_seqs, int total_rows, int hidden, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(n_seqs >= 0 && total_rows >= 0 && hidden > 0, "conv_prefill: bad shape");
+  if (n_seqs == 0 || total_rows == 0) return 0;
+  CGYM_REQUIRE(total_rows <= 65535 * 64, "conv_prefill: too many rows");
+  dim3 grid((hidden + 255) / 256, total_rows);
+  dim3 sgrid((hidden + 255) / 256, n_seqs);
+  DISPATCH_DTYPE(dtype, {
+    conv_prefill_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(
+        static_cast<T*>(y), static_cast<const T*>(state), static_cast<const T*>(bcx),
+        static_cast<const T*>(conv_w), cu_seqlens, seq_slots, seq_starts, n_seqs, hidden);
+    conv_prefill_state_kernel<T><<<sgrid, 256, 0, as_stream(stream)>>>(
+        static_cast<T*>(state), static_cast<const T*>(bcx), cu_seqlens, seq_slots, seq_starts, hidden);
+  });
+  return check_launch("conv_prefill", 2);
+}
+
+extern "C" int cgym_qk_norm_rope_append(void* q_out, void* k_new, void* v_new, const void* qkv,
+                                        const void* q_norm_w, const void* k_norm_w, const float* rope_cos,
+                                        const float* rope_sin, const int32_t* positions, const int32_t* slots,
+                                        const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows,
+                                        int n_q_heads, float eps, int dtype, int32_t* status,
+                                        cgym_stream_t stream) {
+  CGYM_REQUIRE(kv != nullptr && status != nullptr, "qk_norm_rope_append: kv layout and status are required");
+  const int D = kv->head_dim;
+  CGYM_REQUIRE(D == 32 || D == 64 || D == 128 || D == 256, "qk_norm_rope_append: head_dim must be 32, 64, 128 or 256");
+  CGYM_REQUIRE((kv->page_size & (kv->page_size - 1)) == 0 && kv->page_size > 0, "page_size must be a power of two");
+  CGYM_REQUIRE((k_new == nullptr) == (v_new == nullptr), "k_new and v_new go together");
+  CGYM_REQUIRE(kv->kv_dtype != CGYM_E4M3 || kv->kv_scales != nullptr, "e4m3 KV needs a scale pool");
+  if (rows == 0) return 0;
+  CGYM_REQUIRE(n_q_heads + kv->n_kv_heads <= 65535, "too many heads");
+  dim3 grid(rows, n_q_heads + kv->n_kv_heads);
+#define LAUNCH_QK(T, KV)                                                                                   \
+  qk_rope_append_kernel<T, KV><<<grid, D, 0, as_stream(stream)>>>(                                         \
+      static_cast<T*>(q_out), static_cast<T*>(k_new), static_cast<T*>(v_new), static_cast<const T*>(qkv), \
+      static_cast<const T*>(q_norm_w), static_cast<const T*>(k_norm_w), rope_cos, rope_sin, positions,    \
+      slots, active, *kv, layer, n_q_heads, eps, status)
+  if (dtype == CGYM_F32 && kv->kv_dtype == CGYM_F32) LAUNCH_QK(float, float);
+  else if (dtype == CGYM_BF16 && kv->kv_dtype == CGYM_BF16) LAUNCH_QK(__nv_bfloat16, __nv_bfloat16);
+  else if (dtype == CGYM_BF16 && kv->kv_dtype == CGYM_E4M3) LAUNCH_QK(__nv_bfloat16, uint8_t);
+  else return fail("qk_norm_rope_append: unsupported dtype pair (%d, kv %d)", dtype, kv->kv_dtype);
+#undef LAUNCH_QK
+  return check_launch("qk_norm_rope_append");
+}
+
+extern "C" int cgym_target_logprobs(float* out, const void* logits, const int64_t* targets, int rows, int vocab,
+                                    int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && vocab > 0, "target_logprobs: bad shape");
+  if (rows == 0) return 0;
+  DISPATCH_DTYPE(dtype, target_logprob_kernel<T><<<rows, 512, 0, as_stream(stream)>>>(
+      out, static_cast<const T*>(logits), targets, vocab));
+  return check_launch("target_logprobs");
+}

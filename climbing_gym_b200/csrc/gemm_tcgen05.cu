@@ -1,0 +1,377 @@
+// Blackwell tensor-core GEMM for the projections and the LM head:
+//   y[M, N] = x[M, K] . w[N, K]^T      (bf16 x bf16, or e4m3 x e4m3 with per-row / per-channel scales)
+//
+// The weight matrix is the streamed operand (decode reads every weight once per step and M is
+// small), so the kernel is "swap-AB": a CTA owns 128 output features (the MMA M dimension, one TMEM
+// lane each) and a tile of UN tokens (the MMA N dimension, one TMEM column each). Per 128-byte K
+// slice, TMA brings a [128 x 128B] weight tile and a [UN x 128B] activation tile into shared memory
+// with the 128-byte swizzle the UMMA descriptors expect; one elected thread issues tcgen05.mma
+// (fp32 accumulate in TMEM), tcgen05.commit releases the stage, and four epilogue warps read the
+// accumulator back with tcgen05.ld and write y (coalesced along N), applying scales / row mask.
+// Warp roles: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = epilogue.
+//
+// Split-K (grid.z) writes fp32 partials to a caller workspace that a second kernel sums in split
+// order, so results are deterministic. Every mbarrier wait is bounded (about two seconds of
+// %globaltimer): on expiry the CTA raises CGYM_STATUS_WAIT_TIMEOUT, drains its own TMA copies with
+// the same bound, frees its TMEM and returns.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace cgym {
+
+constexpr int UM = 128;           // output features per CTA
+constexpr int SLICE_BYTES = 128;  // K bytes per pipeline stage (one swizzle atom wide)
+constexpr int GEMM_THREADS = 192;
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ unsigned long long global_timer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// bounded wait: false when the limit expired or another role already gave up
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long start = global_timer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try(bar, parity)) return true;
+    if ((spin & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (global_timer() - start > WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// K-major, 128-byte-swizzled operand tile: rows are 128 B apart, 8-row groups 1024 B apart
+__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);   // start address
+  d |= static_cast<uint64_t>(1) << 16;                // leading byte offset (unused with swizzle)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;        // stride byte offset between 8-row groups
+  d |= static_cast<uint64_t>(1) << 46;                // descriptor version (Blackwell)
+  d |= static_cast<uint64_t>(2) << 61;                // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_fp8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmEpilogue {
+  void* y;                 // bf16 [M, N] (direct) or fp32 [splits, M, N] (partials)
+  const float* x_scales;   // per token, fp8 only
+  const float* w_scales;   // per output feature, fp8 only
+  const uint8_t* row_mask; // optional
+  int32_t* status;
+  int M, N, K;
+  int partial;             // 1: write fp32 partials
+};
+
+template <int UN, bool FP8>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                    GemmEpilogue ep) {
+  constexpr int STAGE_BYTES = (UM + UN) * SLICE_BYTES;
+  constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
+  constexpr int ELEMS_PER_SLICE = FP8 ? 128 : 64;
+  constexpr int TMEM_COLS = UN < 32 ? 32 : UN;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[STAGES];
+  __shared__ __align__(8) uint64_t bar_empty[STAGES];
+  __shared__ __align__(8) uint64_t bar_acc;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t tiles = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int n0 = blockIdx.x * UM, m0 = blockIdx.y * UN;
+  const int total_kb = (ep.K + ELEMS_PER_SLICE - 1) / ELEMS_PER_SLICE;
+  const int per_split = (total_kb + gridDim.z - 1) / gridDim.z;
+  const int kb_begin = blockIdx.z * per_split;
+  const int kb_end = min(total_kb, kb_begin + per_split);
+  const int n_kb = max(0, kb_end - kb_begin);
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bar_acc), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_acc = tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    int issued = 0;
+    for (int i = 0; i < n_kb; ++i) {
+      const int s = i % STAGES;
+      const uint32_t parity = ((i / STAGES) & 1) ^ 1;
+      if (!mbar_wait(smem_u32(&bar_empty[s]), parity, &abort_flag)) break;
+      const uint32_t full = smem_u32(&bar_full[s]);
+      mbar_expect_tx(full, STAGE_BYTES);
+      const uint32_t a_dst = tiles + s * STAGE_BYTES, b_dst = a_dst + UM * SLICE_BYTES;
+      const int k_elem = (kb_begin + i) * ELEMS_PER_SLICE;
+      tma_load_2d(a_dst, &tmap_w, full, k_elem, n0);
+      tma_load_2d(b_dst, &tmap_x, full, k_elem, m0);
+      issued = i + 1;
+    }
+    if (abort_flag) {
+      // let copies already in flight land before the CTA's shared memory is released
+      for (int i = max(0, issued - STAGES); i < issued; ++i)
+        mbar_wait(smem_u32(&bar_full[i % STAGES]), (i / STAGES) & 1, &abort_flag);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    // instruction descriptor: fp32 accumulate, K-major A and B, N = UN, M = 128
+    uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(UN >> 3) << 17) | (static_cast<uint32_t>(UM >> 4) << 24);
+    if (!FP8) idesc |= (1u << 7) | (1u << 10);  // bf16 operands (e4m3 is format 0)
+    for (int i = 0; i < n_kb; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(smem_u32(&bar_full[s]), (i / STAGES) & 1, &abort_flag)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a_src = tiles + s * STAGE_BYTES, b_src = a_src + UM * SLICE_BYTES;
+      const uint64_t da = umma_smem_desc(a_src), db = umma_smem_desc(b_src);
+#pragma unroll
+      for (int k = 0; k < SLICE_BYTES / 32; ++k) {  // one MMA consumes 32 bytes of K per row
+        const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+        if (FP8) umma_fp8(tmem_acc, da + 2 * k, db + 2 * k, idesc, acc);
+        else umma_bf16(tmem_acc, da + 2 * k, db + 2 * k, idesc, acc);
+      }
+      umma_commit(smem_u32(&bar_empty[s]));
+    }
+    umma_commit(smem_u32(&bar_acc));
+  } else if (warp >= 2) {
+    // ---- epilogue: TMEM lane = output feature, column = token ----
+    const int quarter = warp & 3;  // a warp may only touch TMEM lanes [32 * (warp % 4), +32)
+    const int n = n0 + quarter * 32 + lane;
+    bool ready = true;
+    if (n_kb > 0) ready = mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ready) {
+      const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
+#pragma unroll 1
+      for (int c = 0; c < UN / 32; ++c) {
+        uint32_t v[32];
+        if (n_kb > 0) {
+          tmem_load32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0u;
+        }
+        if (n < ep.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = m0 + c * 32 + j;
+            if (m >= ep.M) break;
+            float f = __uint_as_float(v[j]);
+            if (ep.partial) {
+              static_cast<float*>(ep.y)[(static_cast<int64_t>(blockIdx.z) * ep.M + m) * ep.N + n] = f;
+            } else {
+              if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
+              if (ep.x_scales != nullptr) f = __fmul_rn(__fmul_rn(f, ep.x_scales[m]), ws);
+              static_cast<__nv_bfloat16*>(ep.y)[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(f);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) atomicOr(ep.status, CGYM_STATUS_WAIT_TIMEOUT);
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_acc), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// sums split-K partials in split order, then scales / masks / converts
+__global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ partials,
+                                     const float* __restrict__ x_scales, const float* __restrict__ w_scales,
+                                     const uint8_t* __restrict__ row_mask, int M, int N, int splits) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(M) * N) return;
+  const int m = static_cast<int>(idx / N), n = static_cast<int>(idx % N);
+  if (row_mask != nullptr && !row_mask[m]) return;
+  float total = 0.0f;
+  for (int s = 0; s < splits; ++s) total = __fadd_rn(total, partials[static_cast<int64_t>(s) * M * N + idx]);
+  if (x_scales != nullptr) total = __fmul_rn(__fmul_rn(total, x_scales[m]), w_scales[n]);
+  y[idx] = __float2bfloat16_rn(total);
+}
+
+// ---- host side -------------------------------------------------------------------------------
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn tensor_map_encoder() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* sym = nullptr;
+    cudaDriverEntryPointQueryResult result;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &result) == cudaSuccess &&
+        result == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(sym);
+  });
+  return fn;
+}
+
+static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows, bool fp8) {
+  EncodeFn encode = tensor_map_encoder();
+  CGYM_REQUIRE(encode != nullptr, "gemm: cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * (fp8 ? 1 : 2)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(fp8 ? 128 : 64), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult rc = encode(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             const_cast<void*>(base), dims, strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CGYM_REQUIRE(rc == CUDA_SUCCESS, "gemm: cuTensorMapEncodeTiled failed with code %d", static_cast<int>(rc));
+  return 0;
+}
+
+template <int UN, bool FP8>
+static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmEpilogue& ep, dim3 grid,
+                       cudaStream_t stream) {
+  constexpr int STAGE_BYTES = (UM + UN) * SLICE_BYTES;
+  constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
+  constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static bool configured = false;  // per instantiation; the attribute is per function, set once
+  if (!configured) {
+    const cudaError_t rc = cudaFuncSetAttribute(gemm_tcgen05_kernel<UN, FP8>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    CGYM_REQUIRE(rc == cudaSuccess, "gemm: cannot reserve %d bytes of shared memory: %s", SMEM, cudaGetErrorString(rc));
+    configured = true;
+  }
+  gemm_tcgen05_kernel<UN, FP8><<<grid, GEMM_THREADS, SMEM, stream>>>(mw, mx, ep);
+  return 0;
+}
+
+bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const void* w) {
+  const int elem = fp8 ? 1 : 2;
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if ((static_cast<int64_t>(K) * elem) % 16 != 0) return false;  // TMA row pitch
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15u) return false;
+  return true;
+}
+
+int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_scales, const float* w_scales,
+                        const uint8_t* row_mask, int M, int N, int K, bool fp8, void* workspace,
+                        int64_t workspace_bytes, int32_t* status, int force_splits, cudaStream_t stream) {
+  CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
+               "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
+  CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
+  const int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
+  const int n_tiles = (N + UM - 1) / UM, m_tiles = (M + un - 1) / un;
+  const int total_kb = (K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
+  int splits = 1;
+  if (force_splits > 0) {
+    splits = force_splits;
+  } else if (workspace != nullptr && n_tiles * m_tiles <= 74 && total_kb >= 8) {
+    splits = 148 / (n_tiles * m_tiles);
+    if (splits > total_kb / 4) splits = total_kb / 4;  // at least four K slices per split
+  }
+  if (splits > total_kb) splits = total_kb;
+  if (splits < 1) splits = 1;
+  while (splits > 1 && static_cast<int64_t>(splits) * M * N * 4 > workspace_bytes) --splits;
+  // every split must own at least one K slice
+  while (splits > 1 && (splits - 1) * ((total_kb + splits - 1) / splits) >= total_kb) --splits;
+  CGYM_REQUIRE(splits == 1 || workspace != nullptr, "gemm(tcgen05): split-K needs a workspace");
+
+  CUtensorMap mw, mx;
+  if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
+  if (int rc = make_map(&mx, x, M, K, un, fp8)) return rc;
+  GemmEpilogue ep{splits > 1 ? workspace : y, x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0};
+  dim3 grid(n_tiles, m_tiles, splits);
+  int rc = 0;
+#define LAUNCH_UN(U)                                                              \
+  rc = fp8 ? launch_tile<U, true>(mw, mx, ep, grid, stream) : launch_tile<U, false>(mw, mx, ep, grid, stream)
+  if (un == 32) LAUNCH_UN(32);
+  else if (un == 64) LAUNCH_UN(64);
+  else if (un == 128) LAUNCH_UN(128);
+  else LAUNCH_UN(256);
+#undef LAUNCH_UN
+  if (rc) return rc;
+  if (splits > 1) {
+    const int64_t total = static_cast<int64_t>(M) * N;
+    splitk_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        static_cast<__nv_bfloat16*>(y), static_cast<const float*>(workspace), x_scales, w_scales, row_mask, M, N,
+        splits);
+  }
+  return check_launch("gemm_tcgen05", splits > 1 ? 2 : 1);
+}
+
+}  // namespace cgym

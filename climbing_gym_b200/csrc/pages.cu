@@ -1,0 +1,275 @@
+// GPU-resident page allocator and block tables of the paged hybrid cache.
+//
+// State lives in device memory: a free bitmap (bit = 1: page free), a per-page reference count
+// (prefix sharing), block_table[slot][block] and n_blocks[slot]. Pages are always handed out
+// lowest id first and entries are served in entry order, so the tables are a pure function of
+// the admit / step / release trace (restated on the CPU in oracle/pages.py). Everything runs on
+// the caller's stream inside the decode graph; no host round-trip is involved.
+#include "common.cuh"
+
+namespace cgym {
+
+constexpr int POOL_THREADS = 1024;
+
+// exclusive scan of one int per thread over the block; returns the exclusive prefix and the total
+__device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* scratch /*33 ints*/) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += n;
+  }
+  __syncthreads();
+  if (lane == 31) scratch[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int w = scratch[lane];
+    int winc = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, winc, o);
+      if (lane >= o) winc += n;
+    }
+    scratch[lane] = winc - w;
+    if (lane == 31) scratch[32] = winc;
+  }
+  __syncthreads();
+  *total = scratch[32];
+  return scratch[warp] + inc - v;
+}
+
+// Entries e < n ask that slot_e can hold need_e tokens. One CTA.
+//   step mode   (need_tokens == nullptr): entry = batch row, need = seq_lens[slot] + 1 for active rows;
+//                also snapshots pending -> active_out when given.
+//   reserve mode: entry e = (slot_ids[e], need_tokens[e]).
+__global__ void __launch_bounds__(POOL_THREADS)
+pages_reserve_kernel(cgym_page_pool pool, const int32_t* __restrict__ slot_ids,
+                     const int32_t* __restrict__ need_tokens, const int32_t* __restrict__ seq_lens,
+                     const uint8_t* __restrict__ active, const uint8_t* __restrict__ pending_in,
+                     uint8_t* __restrict__ active_out, int n, int32_t* __restrict__ status) {
+  __shared__ int s_excl[POOL_THREADS + 1];
+  __shared__ int s_old[POOL_THREADS];
+  __shared__ int s_slot[POOL_THREADS];
+  __shared__ int scratch[33];
+  const int e = threadIdx.x;
+  int cnt = 0, slot = -1, old = 0;
+  if (e < n) {
+    bool act = true;
+    if (pending_in != nullptr) {
+      act = pending_in[e] != 0;
+      if (active_out != nullptr) active_out[e] = act ? 1 : 0;
+    } else if (active != nullptr) {
+      act = active[e] != 0;
+    }
+    slot = slot_ids != nullptr ? slot_ids[e] : e;
+    if (act && slot >= 0 && slot < pool.n_slots) {
+      const int need = need_tokens != nullptr ? need_tokens[e] : seq_lens[slot] + 1;
+      int target = (need + pool.page_size - 1) / pool.page_size;
+      if (target > pool.max_blocks) {
+        atomicOr(status, CGYM_STATUS_CAPACITY);
+        target = pool.max_blocks;
+      }
+      old = pool.n_blocks[slot];
+      cnt = max(0, target - old);
+    } else {
+      slot = -1;
+    }
+  }
+  int total = 0;
+  const int excl = block_exclusive_scan(cnt, &total, scratch);
+  s_excl[e] = excl;
+  s_old[e] = old;
+  s_slot[e] = slot;
+  if (e == 0) s_excl[POOL_THREADS] = total;
+  __syncthreads();
+  if (total == 0) return;
+
+  const int n_words = (pool.n_pages + 31) >> 5;
+  int found = 0;  // free pages consumed so far (block-uniform)
+  for (int base = 0; base < n_words && found < total; base += POOL_THREADS) {
+    const int wi = base + threadIdx.x;
+    uint32_t word = wi < n_words ? pool.free_bitmap[wi] : 0u;
+    int chunk_total = 0;
+    const int before = block_exclusive_scan(__popc(word), &chunk_total, scratch) + found;
+    int r = before;
+    uint32_t taken = 0u;
+    while (word != 0u && r < total) {
+      const int bit = __ffs(word) - 1;
+      word &= word - 1u;
+      taken |= 1u << bit;
+      const int page = wi * 32 + bit;
+      // entry owning rank r: last e with s_excl[e] <= r (entries with cnt 0 share a prefix value
+      // with their successor, so search for the first prefix that exceeds r)
+      int lo = 0, hi = POOL_THREADS;  // find smallest idx with s_excl[idx] > r; owner = idx - 1
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (s_excl[mid] > r) hi = mid; else lo = mid + 1;
+      }
+      const int owner = lo - 1;
+      const int block = s_old[owner] + (r - s_excl[owner]);
+      pool.block_table[static_cast<int64_t>(s_slot[owner]) * pool.max_blocks + block] = page;
+      pool.refcount[page] = 1;
+      ++r;
+    }
+    if (taken != 0u) pool.free_bitmap[wi] &= ~taken;
+    found += chunk_total;
+  }
+  const int granted = min(found, total);
+  if (granted < total && threadIdx.x == 0) atomicOr(status, CGYM_STATUS_PAGE_POOL_EXHAUSTED);
+  if (e < n && cnt > 0) {
+    const int got = max(0, min(cnt, granted - excl));
+    pool.n_blocks[slot] = old + got;
+  }
+}
+
+__global__ void pages_release_kernel(cgym_page_pool pool, const uint8_t* __restrict__ release_mask,
+                                     int32_t* __restrict__ seq_lens) {
+  const int slot = blockIdx.x;
+  if (!release_mask[slot]) return;
+  const int held = pool.n_blocks[slot];
+  __syncthreads();
+  for (int b = threadIdx.x; b < held; b += blockDim.x) {
+    int32_t* entry = pool.block_table + static_cast<int64_t>(slot) * pool.max_blocks + b;
+    const int page = *entry;
+    *entry = -1;
+    if (page >= 0 && page < pool.n_pages && atomicSub(&pool.refcount[page], 1) == 1)
+      atomicOr(&pool.free_bitmap[page >> 5], 1u << (page & 31));
+  }
+  if (threadIdx.x == 0) {
+    pool.n_blocks[slot] = 0;
+    if (seq_lens != nullptr) seq_lens[slot] = 0;
+  }
+}
+
+// dst slots (empty) take src's full prefix pages by reference
+__global__ void pages_share_kernel(cgym_page_pool pool, const int32_t* __restrict__ src_slots,
+                                   const int32_t* __restrict__ dst_slots, const int32_t* __restrict__ prefix_lens) {
+  const int i = blockIdx.x;
+  const int src = src_slots[i], dst = dst_slots[i];
+  const int full = prefix_lens[i] / pool.page_size;
+  for (int b = threadIdx.x; b < full; b += blockDim.x) {
+    const int page = pool.block_table[static_cast<int64_t>(src) * pool.max_blocks + b];
+    pool.block_table[static_cast<int64_t>(dst) * pool.max_blocks + b] = page;
+    if (page >= 0) atomicAdd(&pool.refcount[page], 1);
+  }
+  if (threadIdx.x == 0) pool.n_blocks[dst] = full;
+}
+
+// private copy of the partially filled last prefix page, all layers / K and V / heads
+template <typename KV>
+__global__ void pages_copy_tail_kernel(cgym_page_pool pool, cgym_kv_layout kv, const int32_t* __restrict__ src_slots,
+                                       const int32_t* __restrict__ dst_slots, const int32_t* __restrict__ prefix_lens) {
+  const int i = blockIdx.x;
+  const int rem = prefix_lens[i] % pool.page_size;
+  if (rem == 0) return;
+  const int block = prefix_lens[i] / pool.page_size;
+  const int sp = pool.block_table[static_cast<int64_t>(src_slots[i]) * pool.max_blocks + block];
+  const int dp = pool.block_table[static_cast<int64_t>(dst_slots[i]) * pool.max_blocks + block];
+  if (sp < 0 || dp < 0 || sp == dp) return;
+  const int plane = blockIdx.y;  // (layer * 2 + which) * n_kv_heads + head
+  const int head = plane % kv.n_kv_heads, which = (plane / kv.n_kv_heads) & 1, layer = plane / (2 * kv.n_kv_heads);
+  KV* pool_data = static_cast<KV*>(kv.kv_pool);
+  const int64_t so = kv_elem_offset(kv, layer, sp, which, head, 0), doff = kv_elem_offset(kv, layer, dp, which, head, 0);
+  for (int j = threadIdx.x; j < rem * kv.head_dim; j += blockDim.x) pool_data[doff + j] = pool_data[so + j];
+  if (kv.kv_scales != nullptr) {
+    const int64_t ss = kv_scale_offset(kv, layer, sp, which, head, 0), ds = kv_scale_offset(kv, layer, dp, which, head, 0);
+    for (int j = threadIdx.x; j < rem; j += blockDim.x) kv.kv_scales[ds + j] = kv.kv_scales[ss + j];
+  }
+}
+
+template <typename KV>
+__global__ void gather_kv_dense_kernel(float* __restrict__ out, cgym_kv_layout kv, int layer, int which, int slot) {
+  const int tok = blockIdx.x;
+  const int page = kv.block_table[static_cast<int64_t>(slot) * kv.max_blocks + tok / kv.page_size];
+  const int width = kv.n_kv_heads * kv.head_dim;
+  for (int j = threadIdx.x; j < width; j += blockDim.x) {
+    const int head = j / kv.head_dim, d = j % kv.head_dim;
+    float v = 0.0f;
+    if (page >= 0) {
+      const int64_t off = kv_elem_offset(kv, layer, page, which, head, tok % kv.page_size) + d;
+      if constexpr (sizeof(KV) == 1) {
+        v = from_e4m3(static_cast<const uint8_t*>(kv.kv_pool)[off]) *
+            kv.kv_scales[kv_scale_offset(kv, layer, page, which, head, tok % kv.page_size)];
+      } else {
+        v = Elem<KV>::load(static_cast<const KV*>(kv.kv_pool) + off);
+      }
+    }
+    out[static_cast<int64_t>(tok) * width + j] = v;
+  }
+}
+
+static int check_pool(const cgym_page_pool* pool) {
+  CGYM_REQUIRE(pool != nullptr && pool->free_bitmap && pool->refcount && pool->block_table && pool->n_blocks,
+               "page pool is incomplete");
+  CGYM_REQUIRE(pool->n_pages > 0 && pool->max_blocks > 0 && pool->n_slots > 0, "page pool has an empty dimension");
+  CGYM_REQUIRE(pool->page_size > 0 && (pool->page_size & (pool->page_size - 1)) == 0,
+               "page_size must be a power of two");
+  return 0;
+}
+
+}  // namespace cgym
+
+using namespace cgym;
+
+extern "C" int cgym_step_begin(const cgym_page_pool* pool, const int32_t* seq_lens, const uint8_t* pending,
+                               uint8_t* active_out, const uint8_t* active, const int32_t* slots, int rows,
+                               int32_t* status, cgym_stream_t stream) {
+  if (int rc = check_pool(pool)) return rc;
+  CGYM_REQUIRE(seq_lens != nullptr && status != nullptr, "step_begin: seq_lens and status are required");
+  CGYM_REQUIRE(rows >= 0 && rows <= POOL_THREADS, "step_begin: at most 1024 rows per step");
+  if (rows == 0) return 0;
+  pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, slots, nullptr, seq_lens, active, pending,
+                                                                  active_out, rows, status);
+  return check_launch("step_begin");
+}
+
+extern "C" int cgym_pages_reserve(const cgym_page_pool* pool, const int32_t* slot_ids, const int32_t* need_tokens,
+                                  int n, int32_t* status, cgym_stream_t stream) {
+  if (int rc = check_pool(pool)) return rc;
+  CGYM_REQUIRE(slot_ids && need_tokens && status, "pages_reserve: slot_ids, need_tokens and status are required");
+  CGYM_REQUIRE(n >= 0, "pages_reserve: negative count");
+  for (int done = 0; done < n; done += POOL_THREADS) {
+    const int m = n - done < POOL_THREADS ? n - done : POOL_THREADS;
+    pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, slot_ids + done, need_tokens + done,
+                                                                    nullptr, nullptr, nullptr, nullptr, m, status);
+  }
+  return check_launch("pages_reserve", (n + POOL_THREADS - 1) / POOL_THREADS);
+}
+
+extern "C" int cgym_pages_release(const cgym_page_pool* pool, const uint8_t* release_mask, int32_t* seq_lens,
+                                  cgym_stream_t stream) {
+  if (int rc = check_pool(pool)) return rc;
+  CGYM_REQUIRE(release_mask != nullptr, "pages_release: mask is required");
+  pages_release_kernel<<<pool->n_slots, 128, 0, as_stream(stream)>>>(*pool, release_mask, seq_lens);
+  return check_launch("pages_release");
+}
+
+extern "C" int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout* kv, int n_layers,
+                               const int32_t* src_slots, const int32_t* dst_slots, const int32_t* prefix_lens, int n,
+                               int32_t* status, cgym_stream_t stream) {
+  if (int rc = check_pool(pool)) return rc;
+  CGYM_REQUIRE(kv && src_slots && dst_slots && prefix_lens && status, "pages_fork: missing argument");
+  CGYM_REQUIRE(n >= 0 && n <= POOL_THREADS, "pages_fork: at most 1024 children per call");
+  if (n == 0) return 0;
+  pages_share_kernel<<<n, 128, 0, as_stream(stream)>>>(*pool, src_slots, dst_slots, prefix_lens);
+  pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, dst_slots, prefix_lens, nullptr, nullptr,
+                                                                  nullptr, nullptr, n, status);
+  dim3 grid(n, n_layers * 2 * kv->n_kv_heads);
+  if (kv->kv_dtype == CGYM_F32) pages_copy_tail_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);
+  else if (kv->kv_dtype == CGYM_BF16) pages_copy_tail_kernel<__nv_bfloat16><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);
+  else if (kv->kv_dtype == CGYM_E4M3) pages_copy_tail_kernel<uint8_t><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);
+  else return fail("pages_fork: unsupported kv dtype %d", kv->kv_dtype);
+  return check_launch("pages_fork", 3);
+}
+
+extern "C" int cgym_gather_kv_dense(float* out, const cgym_kv_layout* kv, int layer, int which, int slot, int length,
+                                    cgym_stream_t stream) {
+  CGYM_REQUIRE(kv != nullptr && out != nullptr && length >= 0, "gather_kv_dense: bad arguments");
+  if (length == 0) return 0;
+  if (kv->kv_dtype == CGYM_F32) gather_kv_dense_kernel<float><<<length, 128, 0, as_stream(stream)>>>(out, *kv, layer, which, slot);
+  else if (kv->kv_dtype == CGYM_BF16) gather_kv_dense_kernel<__nv_bfloat16><<<length, 128, 0, as_stream(stream)>>>(out, *kv, layer, which, slot);
+  else if (kv->kv_dtype == CGYM_E4M3) gather_kv_dense_kernel<uint8_t><<<length, 128, 0, as_stream(stream)>>>(out, *kv, layer, which, slot);
+  else return fail("gather_kv_dense: unsupported kv dtype %d", kv->kv_dtype);
+  return check_launch("gather_kv_dense");
+}

@@ -1,0 +1,340 @@
+"""CUDA-graph decode engine over the paged cache (drop-in for the reference's LFM25CUDADecoder).
+
+Reference: src/climbing_gym/inference/lfm25_cuda.py. Same role and attribute contract
+(``generate``, ``graphs`` keyed ``(batch, capacity, masked)``, ``_get_graph``, ``refresh_weights``,
+``clear``, ``_active_session`` ...), different machinery: one captured graph per entry holds the
+WHOLE step - page allocation for rows that cross a page boundary, the 16-layer forward, the LM
+head, the fused sampler and the per-slot bookkeeping - so a decode step is one graph replay with
+no host logic between tokens. Rows are the physical slots of a paged cache; finished or empty
+rows are masked inside the kernels instead of being compacted on the host.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from collections import OrderedDict
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _native as nv
+from .config import LFM25SamplingConfig
+from .model import ForwardBuffers, LFM25Runner
+from .paged import PagedHybridCache
+from .types import LFM25GenerationOutput
+
+
+class SlotState:
+    """Per-slot request state on the device (the reference session's row tensors,
+    src/climbing_gym/inference/lfm25_session.py:147-167) plus the struct the sampler kernel reads."""
+
+    def __init__(self, n_slots: int, capacity: int, vocab: int, eos: int, seq_lens: torch.Tensor,
+                 *, stop_states: int = 8):
+        dev = seq_lens.device
+        self.n_slots, self.capacity, self.vocab = n_slots, capacity, vocab
+
+        def rows(dtype, value=0):
+            return torch.full((n_slots,), value, device=dev, dtype=dtype)
+
+        self.tokens = torch.zeros((n_slots, capacity), device=dev, dtype=torch.int64)
+        self.logprobs = torch.zeros((n_slots, capacity), device=dev, dtype=torch.float32)
+        self.lengths, self.limits = rows(torch.int32), rows(torch.int32)
+        self.reasons = rows(torch.int8)
+        self.alive, self.pending, self.ignore_eos = rows(torch.uint8), rows(torch.uint8), rows(torch.uint8)
+        self.input_tokens = rows(torch.int64)
+        self.stop_states, self.stop_offsets = rows(torch.int64), rows(torch.int64)
+        self.rng_positions, self.seeds, self.rng_offsets = rows(torch.int64), rows(torch.int64), rows(torch.int64)
+        self.temperatures = rows(torch.float32)
+        self.force_eos_at = rows(torch.int32, -1)
+        self.active = rows(torch.uint8)  # snapshot of `pending` taken at the start of each step
+        # stop-table arena: table 0 is all zeros (no stops); more tables are appended in place
+        self.stop_table = torch.zeros(stop_states * vocab, device=dev, dtype=torch.int32)
+        self.stop_table_used = vocab
+        self.seq_lens = seq_lens
+        self.struct = nv.SlotState(
+            nv.ptr(self.tokens), nv.ptr(self.logprobs), nv.ptr(self.lengths), nv.ptr(self.limits),
+            nv.ptr(self.reasons), nv.ptr(self.alive), nv.ptr(self.pending), nv.ptr(self.input_tokens),
+            nv.ptr(self.stop_states), nv.ptr(self.stop_offsets), nv.ptr(self.stop_table), nv.ptr(self.ignore_eos),
+            nv.ptr(self.rng_positions), nv.ptr(self.seeds), nv.ptr(self.temperatures), nv.ptr(self.rng_offsets),
+            nv.ptr(self.force_eos_at), nv.ptr(seq_lens), capacity, eos)
+
+    def reset(self) -> None:
+        for t in (self.lengths, self.limits, self.reasons, self.alive, self.pending, self.ignore_eos,
+                  self.input_tokens, self.stop_states, self.stop_offsets, self.rng_positions, self.seeds,
+                  self.rng_offsets, self.temperatures, self.active, self.tokens, self.logprobs):
+            t.zero_()
+        self.force_eos_at.fill_(-1)
+        self.stop_table_used = self.vocab
+
+    def add_stop_table(self, table: torch.Tensor) -> int:
+        """Append a [states, vocab] int32 table to the arena; returns its element offset."""
+        flat = table.reshape(-1).to(device=self.stop_table.device, dtype=torch.int32)
+        offset = self.stop_table_used
+        if offset + flat.numel() > self.stop_table.numel():
+            raise ValueError("stop tables exceed the session's reserved stop-state arena")
+        self.stop_table[offset:offset + flat.numel()].copy_(flat)
+        self.stop_table_used = offset + flat.numel()
+        return offset
+
+    def configure(self, slots, *, limits, seeds, temperatures, ignore_eos, stop_offsets, rng_offsets,
+                  rng_positions=None, stop_states=None, force_eos_at=None) -> None:
+        """Arm rows for a new request: one small scatter per field, no per-slot host writes."""
+        dev = self.lengths.device
+        index = torch.as_tensor(slots, dtype=torch.int64, device=dev)
+        n = index.numel()
+
+        def put(dst, values, dtype):
+            if isinstance(values, (list, tuple)):
+                src = torch.tensor(values, dtype=dtype, device=dev)
+            else:
+                src = torch.full((n,), values, dtype=dtype, device=dev)
+            dst.index_copy_(0, index, src)
+
+        put(self.lengths, 0, torch.int32)
+        put(self.reasons, 0, torch.int8)
+        put(self.limits, limits, torch.int32)
+        put(self.seeds, seeds, torch.int64)
+        put(self.temperatures, temperatures, torch.float32)
+        put(self.ignore_eos, ignore_eos, torch.uint8)
+        put(self.stop_offsets, stop_offsets, torch.int64)
+        put(self.rng_offsets, rng_offsets, torch.int64)
+        put(self.rng_positions, 0 if rng_positions is None else rng_positions, torch.int64)
+        put(self.stop_states, 0 if stop_states is None else stop_states, torch.int64)
+        put(self.force_eos_at, -1 if force_eos_at is None else force_eos_at, torch.int32)
+        put(self.alive, 1, torch.uint8)
+        put(self.pending, 0, torch.uint8)
+
+
+@dataclass
+class _DecodeGraph:
+    cache: PagedHybridCache
+    input_tokens: torch.Tensor
+    logits: torch.Tensor
+    graph: object
+    active: torch.Tensor
+    state: SlotState
+    bufs: ForwardBuffers
+    compact_graphs: dict = field(default_factory=dict)
+
+
+class B200Decoder:
+    supported_conv_kernel_sizes = (3,)
+
+    def __init__(self, engine, *, max_graphs: int = 2, bf16_weight_packing: bool = True,
+                 max_prefill_tokens: int = 4096, finish_check_interval: int = 32,
+                 skip_finished_attention: bool = True, fp8_mlp: bool = False, fp8_kv: bool = False,
+                 adaptive_batching: bool = False, fp8_lm_head: bool = False, page_size: int = 64,
+                 use_cuda_graphs: bool = True):
+        if engine.device.type != "cuda" or engine.dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("LFM2.5 CUDA graphs require CUDA and bfloat16 (or float32) weights")
+        cfg = engine.config
+        if cfg.conv_kernel_size not in self.supported_conv_kernel_sizes or cfg.conv_bias:
+            raise ValueError(f"Native CUDA graphs require bias-free convolutions of width {self.supported_conv_kernel_sizes}")
+        if cfg.head_dim not in (32, 64, 128, 256):
+            raise ValueError("LFM2.5 CUDA graphs require head_dim in {32, 64, 128, 256}")
+        if max_graphs <= 0:
+            raise ValueError("max_graphs must be > 0")
+        if max_prefill_tokens <= 0:
+            raise ValueError("max_prefill_tokens must be positive")
+        if type(finish_check_interval) is not int or finish_check_interval <= 0:
+            raise ValueError("finish_check_interval must be a positive integer")
+        if (fp8_mlp or fp8_kv or fp8_lm_head) and engine.dtype != torch.bfloat16:
+            raise ValueError("Native FP8 paths require bfloat16 weights")
+        if not nv.load().cgym_device_supported():
+            raise ValueError("The cgym_b200 kernels require an NVIDIA B200 (compute capability 10.x)")
+        self.engine = engine
+        self.max_graphs = max_graphs
+        self.max_prefill_tokens = max_prefill_tokens
+        self.finish_check_interval = finish_check_interval
+        self.skip_finished_attention = bool(skip_finished_attention)
+        self.bf16_weight_packing = bool(bf16_weight_packing) and engine.dtype == torch.bfloat16
+        self.packed_weights: dict = {}  # the lossless batch-1 bf16 stream of the reference has no B200 analogue
+        self.fp8_mlp, self.fp8_kv = bool(fp8_mlp), bool(fp8_kv)
+        self.adaptive_batching, self.fp8_lm_head = bool(adaptive_batching), bool(fp8_lm_head)
+        self.page_size = page_size
+        self.use_cuda_graphs = use_cuda_graphs
+        self.runner = LFM25Runner(engine.weights, engine._rope_cos, engine._rope_sin, fp8_mlp=self.fp8_mlp,
+                                  fp8_lm_head=self.fp8_lm_head)
+        self.graphs: OrderedDict = OrderedDict()
+        self._active_session = None
+        self._capture_stream = torch.cuda.Stream(device=engine.device)
+        self.debug_force_eos_at = None  # test hook: per-row generated position forced to EOS
+        # when set, generate() brackets its decode-graph replays with CUDA events on the launching
+        # stream and appends (start, end, replays) here; resolved by the caller after a synchronize
+        self.profile_decode = False
+        self.decode_profile: list = []
+
+    @property
+    def fp8_weights(self) -> dict:
+        return self.runner.fp8_weights
+
+    def clear(self) -> None:
+        if self._active_session is not None:
+            self._active_session.close()
+        self.graphs.clear()
+        self.packed_weights.clear()
+        self.runner.fp8_weights.clear()
+
+    def refresh_weights(self) -> None:
+        self.runner.refresh_fp8()
+
+    # ---- graph entries ------------------------------------------------------------------------------
+    def _step(self, entry: _DecodeGraph) -> None:
+        """The whole decode step for every slot of the entry (what the graph captures)."""
+        cache, state = entry.cache, entry.state
+        n = cache.n_slots
+        stream = nv.stream_ptr(self.engine.device)
+        nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(state.pending), nv.ptr(state.active),
+                None, None, n, nv.ptr(cache.status), stream)
+        self.runner.decode_step(entry.bufs, cache, state.input_tokens, state.active, entry.logits)
+        nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(state.struct), nv.ptr(state.active), None, None,
+                n, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype), stream)
+
+    def _sample_only(self, entry: _DecodeGraph) -> None:
+        """First token of freshly prefetched rows: sample from the prefill logits, no forward."""
+        state = entry.state
+        nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(state.struct), None, None, None,
+                entry.cache.n_slots, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype),
+                nv.stream_ptr(self.engine.device))
+
+    @torch.inference_mode()
+    def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False) -> _DecodeGraph:
+        engine = self.engine
+        alignment = 32 if batch_size >= 64 else 128
+        alignment = max(alignment, self.page_size)
+        capacity = min(engine.max_model_len, -(-cache_len // alignment) * alignment)
+        key = (batch_size, capacity, masked)
+        if key in self.graphs:
+            self.graphs.move_to_end(key)
+            return self.graphs[key]
+        if len(self.graphs) >= self.max_graphs:
+            self.graphs.popitem(last=False)
+        self.runner.prepare_fp8()
+        cache = engine._empty_cache(max_slots=batch_size, max_seq_len=capacity, fp8_kv=self.fp8_kv,
+                                    page_size=self.page_size)
+        state = SlotState(batch_size, capacity, engine.config.vocab_size, int(engine.config.eos_token_id), cache.seq_lens)
+        logits = torch.zeros((batch_size, engine.config.vocab_size), device=engine.device, dtype=engine.dtype)
+        splits = 1
+        if batch_size * engine.config.num_key_value_heads < 148:
+            splits = min(16, max(1, -(-148 // (batch_size * engine.config.num_key_value_heads))))
+        bufs = ForwardBuffers(engine.weights, batch_size, fp8=self.fp8_mlp or self.fp8_lm_head, attn_splits=splits)
+        entry = _DecodeGraph(cache, state.input_tokens, logits, None, state.active, state, bufs)
+        # All rows are dead (alive = pending = 0) while warming up and capturing, so neither run
+        # touches KV pages, conv taps, logits or bookkeeping.
+        stream, current = self._capture_stream, torch.cuda.current_stream(engine.device)
+        stream.wait_stream(current)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                self._step(entry)
+        current.wait_stream(stream)
+        torch.cuda.synchronize(engine.device)
+        if self.use_cuda_graphs:
+            graph = torch.cuda.CUDAGraph()
+            before = nv.load().cgym_launch_count()
+            with torch.cuda.graph(graph, stream=stream):
+                self._step(entry)
+            current.wait_stream(stream)
+            entry.graph = _StepGraph(graph, int(nv.load().cgym_launch_count() - before))
+        else:
+            entry.graph = _EagerStep(self, entry)
+        self.graphs[key] = entry
+        return entry
+
+    def _select_graph(self, entry, live_slots):
+        return entry.graph, entry.input_tokens.numel()
+
+    # ---- batch generate -------------------------------------------------------------------------------
+    @torch.inference_mode()
+    def generate(self, input_ids, cu_seqlens, max_seqlen: int, repeats: int, sampling: LFM25SamplingConfig):
+        if self._active_session is not None:
+            raise RuntimeError("Close the native generation session before calling generate")
+        if repeats <= 0:
+            raise ValueError("repeats must be > 0")
+        engine = self.engine
+        cache_len = int(max_seqlen) + sampling.max_new_tokens
+        if cache_len > engine.max_model_len:
+            raise ValueError(f"max_seq_len={cache_len} exceeds engine max_model_len={engine.max_model_len}")
+        if sampling.top_k or sampling.top_p != 1.0 or sampling.repetition_penalty != 1.0:
+            raise NotImplementedError("filtered sampling (top-k / top-p / repetition penalty) is not on the fused path")
+        if sampling.stop_token_sequences or sampling.behavior_topk:
+            raise NotImplementedError("stop_token_sequences / behavior_topk are not on the fused path")
+        flat_ids, prompt_lengths = engine._split_lengths(input_ids, cu_seqlens, max_seqlen)
+        n_prompts, batch = len(prompt_lengths), len(prompt_lengths) * repeats
+        entry = self._get_graph(batch, cache_len, masked=self.adaptive_batching)
+        cache, state, dev = entry.cache, entry.state, engine.device
+        cache.release(torch.ones(batch, device=dev, dtype=torch.uint8))
+        cache.conv_state.zero_()
+        state.reset()
+        sources = [p * repeats for p in range(n_prompts)]
+        engine._prefill_packed(cache, sources, prompt_lengths, [0] * n_prompts, entry.logits, self.max_prefill_tokens,
+                               flat_tokens=flat_ids)
+        if repeats > 1:
+            src = torch.tensor([p * repeats for p in range(n_prompts) for _ in range(repeats - 1)], device=dev, dtype=torch.int32)
+            dst = torch.tensor([p * repeats + r for p in range(n_prompts) for r in range(1, repeats)], device=dev, dtype=torch.int32)
+            lens = torch.tensor([prompt_lengths[p] for p in range(n_prompts) for _ in range(repeats - 1)], device=dev, dtype=torch.int32)
+            cache.fork(src, dst, lens)
+            entry.logits[dst.long()] = entry.logits[src.long()]
+        stop_offset = 0
+        if sampling.stop_table is not None or sampling.stop_token_ids:
+            stop_offset = state.add_stop_table(build_token_stop_table(sampling, engine.config.vocab_size, dev))
+        vocab = engine.config.vocab_size
+        state.configure(list(range(batch)), limits=sampling.max_new_tokens, seeds=int(sampling.seed) & 0x7FFFFFFFFFFFFFFF,
+                        temperatures=float(sampling.temperature), ignore_eos=int(sampling.ignore_eos),
+                        stop_offsets=stop_offset, rng_offsets=[row * vocab for row in range(batch)],
+                        force_eos_at=self.debug_force_eos_at)
+        fixed_length = sampling.ignore_eos and not sampling.stop_token_ids and sampling.stop_table is None
+        interval = self.finish_check_interval if batch >= 16 else 1
+        self._sample_only(entry)
+        timing = self.profile_decode
+        if timing:
+            start_event, end_event = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start_event.record()
+        replays = 0
+        for step in range(1, sampling.max_new_tokens):
+            if not fixed_length and step % interval == 0 and not bool(state.alive.any().item()):
+                break
+            entry.graph.replay()
+            replays += 1
+        if timing:
+            end_event.record()
+            self.decode_profile.append((start_event, end_event, replays))
+        cache.check_status()
+        n_new = sampling.max_new_tokens
+        shape = (n_prompts, repeats)
+        reasons = state.reasons.clone()
+        reasons.masked_fill_(reasons == 0, 3)
+        return LFM25GenerationOutput(
+            token_ids=state.tokens[:, :n_new].reshape(*shape, n_new).clone(),
+            lengths=state.lengths.reshape(shape).clone(),
+            logprobs=state.logprobs[:, :n_new].reshape(*shape, n_new).clone() if sampling.return_logprobs else None,
+            finish_reasons=reasons.reshape(shape))
+
+
+class _StepGraph:
+    """A captured step plus the number of this library's kernels inside it (for launch accounting)."""
+
+    def __init__(self, graph, kernels: int):
+        self.graph, self.kernels = graph, kernels
+
+    def replay(self) -> None:
+        self.graph.replay()
+        nv.note_graph_replay(self.kernels)
+
+
+class _EagerStep:
+    """Graph stand-in that launches the step kernels directly (debugging / profiling aid)."""
+
+    def __init__(self, decoder: B200Decoder, entry: _DecodeGraph):
+        self.decoder, self.entry = decoder, entry
+
+    def replay(self) -> None:
+        self.decoder._step(self.entry)
+
+
+def build_token_stop_table(sampling: LFM25SamplingConfig, vocab: int, device) -> torch.Tensor:
+    """Stop ids folded into a (copy of the) stop table as ``matched`` entries, as the reference
+    session does (src/climbing_gym/inference/lfm25_session.py:228-241)."""
+    table = (torch.zeros((1, vocab), dtype=torch.int32, device=device) if sampling.stop_table is None
+             else sampling.stop_table.to(device).clone())
+    if sampling.stop_token_ids:
+        table[:, list(sampling.stop_token_ids)] = 65536
+    return table

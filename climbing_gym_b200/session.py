@@ -1,0 +1,327 @@
+"""Resumable fixed-slot generation with continuous request admission.
+
+API, result types, validation messages and statistics keys follow the reference session
+(src/climbing_gym/inference/lfm25_session.py:59-533): ``admit`` takes the lowest free slots,
+``poll(steps)`` advances every live row at most ``steps`` tokens and returns the rows that
+finished, ``resume`` continues a finished row from its exact cached prefix (its last sampled
+token is still "pending", i.e. not yet in the cache), ``release`` frees the slot.
+
+What differs underneath:
+* a poll step is one replay of the decoder's step graph - page allocation, forward, LM head,
+  sampler and bookkeeping all run on the device; the host touches nothing per token;
+* ``release`` returns the slot's pages to the device-side pool (eviction), ``admit`` prefetches
+  packed variable-length prompt rows straight into freshly reserved pages;
+* ``resume`` feeds the pending token plus the new suffix through one packed prefill chunk that
+  continues from the cached prefix, instead of one decode-graph replay per token.
+"""
+from __future__ import annotations
+
+from contextlib import contextmanager
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+
+from .config import LFM25SamplingConfig
+from .decoder import build_token_stop_table
+from .types import BehaviorTopK
+
+
+@dataclass(frozen=True, slots=True)
+class LFM25ContinuationHandle:
+    """A single-use lease on one session slot; invalid after release/close."""
+
+    session: object
+    slot: int
+    version: int
+    prefix_token_ids: tuple
+
+
+@dataclass(frozen=True, slots=True)
+class LFM25SessionResult:
+    handle: LFM25ContinuationHandle
+    prompt_token_ids: tuple
+    token_ids: tuple
+    logprobs: tuple | None
+    finish_reason: int
+    behavior_topk: BehaviorTopK | None = None
+
+
+@dataclass
+class _Request:
+    prompt: tuple
+    sampling: LFM25SamplingConfig
+    version: int
+    delivered: bool = False
+    handle: LFM25ContinuationHandle | None = None
+
+
+class LFM25GenerationSession:
+    @torch.inference_mode()
+    def __init__(self, decoder, *, max_batch_size: int, max_new_tokens: int, cache_len: int | None = None,
+                 behavior_topk: int = 0, profile_timings: bool = False):
+        if decoder._active_session is not None:
+            raise RuntimeError("A native generation session is already open")
+        if type(max_batch_size) is not int or max_batch_size <= 0:
+            raise ValueError("max_batch_size must be a positive integer")
+        if type(max_new_tokens) is not int or max_new_tokens <= 0:
+            raise ValueError("max_new_tokens must be a positive integer")
+        self.decoder, self.engine = decoder, decoder.engine
+        self.batch_size, self.max_new_tokens = max_batch_size, max_new_tokens
+        if type(behavior_topk) is not int or not 0 <= behavior_topk <= min(128, self.engine.config.vocab_size):
+            raise ValueError("behavior_topk must be an integer between 0 and min(vocab, 128)")
+        if behavior_topk:
+            raise NotImplementedError("behavior_topk heads are not on the fused path")
+        self.behavior_topk = behavior_topk
+        self.entry = decoder._get_graph(max_batch_size, cache_len or self.engine.max_model_len, masked=True)
+        self.state, self.cache = self.entry.state, self.entry.cache
+        self.cache.release(torch.ones(max_batch_size, device=self.engine.device, dtype=torch.uint8))
+        self.cache.conv_state.zero_()
+        self.state.reset()
+        self.requests: list[_Request | None] = [None] * max_batch_size
+        self.versions = [0] * max_batch_size
+        self.closed = False
+        self.policy_version = self.engine.policy_version
+        self._timing_events = []
+        self.profile_timings = profile_timings
+        self._stop_tables: dict = {}
+        self.stats = dict(prefilled_tokens=0, resumed_prefix_tokens=0, appended_tokens=0, admitted_requests=0,
+                          resumed_requests=0, decode_steps=0, slot_refills=0, peak_live_slots=0, decode_row_steps=0,
+                          reserved_row_steps=0, adaptive_graph_captures=0, decode_batches={}, forked_requests=0,
+                          copied_prefix_tokens=0, snapshot_prefilled_tokens=0, snapshot_count=0, peak_snapshots=0,
+                          peak_snapshot_bytes=0)
+        decoder._active_session = self
+
+    # views the reference's tests and examples read
+    @property
+    def lengths(self): return self.state.lengths
+    @property
+    def reasons(self): return self.state.reasons
+    @property
+    def alive(self): return self.state.alive
+    @property
+    def pending(self): return self.state.pending
+    @property
+    def rng_positions(self): return self.state.rng_positions
+    @property
+    def stop_states(self): return self.state.stop_states
+    @property
+    def tokens(self): return self.state.tokens
+    @property
+    def logprobs(self): return self.state.logprobs
+
+    def _check_open(self):
+        if self.closed or self.decoder._active_session is not self or self.engine._cuda_decoder is not self.decoder:
+            raise RuntimeError("Native generation session is closed")
+        if self.engine.policy_version != self.policy_version:
+            raise ValueError("Session cache belongs to another policy version")
+
+    @contextmanager
+    def _timed(self, phase):
+        if not self.profile_timings:
+            yield
+            return
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        try:
+            yield
+        finally:
+            end.record()
+            self._timing_events.append((phase, start, end))
+
+    def timing_stats(self):
+        if self._timing_events:
+            self._timing_events[-1][2].synchronize()
+        result = {}
+        for phase, start, end in self._timing_events:
+            key = phase + "_gpu_seconds"
+            result[key] = result.get(key, 0.0) + start.elapsed_time(end) / 1000
+        return result
+
+    def _validate(self, prompt, sampling):
+        vocab = self.engine.config.vocab_size
+        if sampling.behavior_topk > self.behavior_topk:
+            raise ValueError("Request behavior head exceeds the session reservation")
+        if not prompt:
+            raise ValueError("Empty prompts are not supported")
+        if any(type(t) is not int or not 0 <= t < vocab for t in prompt):
+            raise ValueError("Prompt token outside the model vocabulary")
+        if len(prompt) + sampling.max_new_tokens > self.cache.max_seq_len:
+            raise ValueError("Request exceeds reserved session context capacity")
+        if sampling.max_new_tokens > self.max_new_tokens:
+            raise ValueError("Request exceeds the session generation buffer")
+        if sampling.top_k or sampling.top_p != 1.0 or sampling.repetition_penalty != 1.0:
+            raise ValueError("Sessions support greedy/full-support sampling without repetition penalties")
+        if sampling.stop_token_sequences:
+            raise ValueError("Sessions use stop_token_ids or stop_table; encode string stops with build_stop_table")
+        if any(not 0 <= t < vocab for t in sampling.stop_token_ids):
+            raise ValueError("Stop token outside the model vocabulary")
+        table = sampling.stop_table
+        if table is not None and (table.ndim != 2 or table.size(1) != vocab or table.dtype != torch.int32):
+            raise ValueError("stop_table must be an int32 state-by-vocabulary table")
+
+    def _stop_offset(self, sampling) -> int:
+        if sampling.stop_table is None and not sampling.stop_token_ids:
+            return 0
+        key = (id(sampling.stop_table), sampling.stop_token_ids)
+        if key not in self._stop_tables:
+            table = build_token_stop_table(sampling, self.engine.config.vocab_size, self.engine.device)
+            # keep the source table alive so a later table cannot reuse its id()
+            self._stop_tables[key] = (self.state.add_stop_table(table), sampling.stop_table)
+        return self._stop_tables[key][0]
+
+    def _configure(self, slots, prompts, samplings, *, rng_positions=None, stop_states=None):
+        for slot, prompt, sampling in zip(slots, prompts, samplings):
+            self.versions[slot] += 1
+            self.requests[slot] = _Request(tuple(prompt), sampling, self.versions[slot])
+        self.state.configure(
+            list(slots), limits=[s.max_new_tokens for s in samplings],
+            seeds=[s.seed & 0x7FFFFFFFFFFFFFFF for s in samplings],
+            temperatures=[float(s.temperature) for s in samplings], ignore_eos=[int(s.ignore_eos) for s in samplings],
+            stop_offsets=[self._stop_offset(s) for s in samplings], rng_offsets=0,
+            rng_positions=rng_positions, stop_states=stop_states)
+
+    @torch.inference_mode()
+    def admit(self, prompts: Sequence[Sequence[int]], samplings: Sequence[LFM25SamplingConfig], *,
+              slots: Sequence[int] | None = None) -> list[int]:
+        self._check_open()
+        if len(prompts) != len(samplings):
+            raise ValueError("One sampling configuration is required per prompt")
+        free = [i for i, request in enumerate(self.requests) if request is None]
+        slots = list(free[:len(prompts)] if slots is None else slots)
+        if len(slots) != len(prompts) or len(set(slots)) != len(slots) or any(i not in free for i in slots):
+            raise ValueError("Admission requires distinct free session slots")
+        work = sorted(zip(slots, prompts, samplings), key=lambda item: item[0])
+        for _, prompt, sampling in work:
+            self._validate(prompt, sampling)
+        if not work:
+            return slots
+        ordered_slots = [slot for slot, _, _ in work]
+        with self._timed("prefill"):
+            self.engine._prefill_packed(self.cache, ordered_slots, [list(p) for _, p, _ in work], [0] * len(work),
+                                        self.entry.logits, self.decoder.max_prefill_tokens)
+        for slot, prompt, _ in work:
+            self.stats["slot_refills"] += int(self.versions[slot] > 0)
+            self.stats["prefilled_tokens"] += len(prompt)
+            self.stats["admitted_requests"] += 1
+        self._configure(ordered_slots, [p for _, p, _ in work], [s for _, _, s in work])
+        self.stats["peak_live_slots"] = max(self.stats["peak_live_slots"], sum(r is not None for r in self.requests))
+        return slots
+
+    def _request_for(self, handle):
+        self._check_open()
+        if handle.session is not self or not 0 <= handle.slot < self.batch_size:
+            raise ValueError("Continuation handle belongs to another session")
+        request = self.requests[handle.slot]
+        if request is None or request.version != handle.version or not request.delivered or request.handle is not handle:
+            raise ValueError("Continuation handle is stale or already consumed")
+        return request
+
+    @torch.inference_mode()
+    def resume(self, handles, prompts, samplings, *, preserve_rng: bool = False) -> None:
+        if not len(handles) == len(prompts) == len(samplings):
+            raise ValueError("One prompt and sampling configuration is required per handle")
+        if len({h.slot for h in handles}) != len(handles):
+            raise ValueError("Cannot resume a handle twice")
+        work = []
+        for handle, prompt, sampling in zip(handles, prompts, samplings):
+            request = self._request_for(handle)
+            self._validate(prompt, sampling)
+            prefix = handle.prefix_token_ids
+            if tuple(prompt[:len(prefix)]) != prefix:
+                raise ValueError("Continuation requires the exact cached token prefix")
+            if preserve_rng and (tuple(prompt) != prefix or sampling.seed != request.sampling.seed
+                                 or sampling.stop_table is not request.sampling.stop_table
+                                 or sampling.stop_token_ids != request.sampling.stop_token_ids):
+                raise ValueError("Internal pauses must preserve the exact context, seed and stop rules")
+            work.append((handle, tuple(prompt), sampling, request))
+        if not work:
+            return
+        slots = [h.slot for h, _, _, _ in work]
+        if preserve_rng:
+            positions = self.state.rng_positions[slots].cpu().tolist()
+            states = self.state.stop_states[slots].cpu().tolist()
+        else:
+            positions, states = [0] * len(slots), [0] * len(slots)
+        # The final generated token never entered the cache: append it and the new suffix as one
+        # continuation chunk starting at the slot's cached length (= len(prefix) - 1).
+        appends = [list((h.prefix_token_ids[-1], *prompt[len(h.prefix_token_ids):])) for h, prompt, _, _ in work]
+        starts = [len(h.prefix_token_ids) - 1 for h, _, _, _ in work]
+        order = sorted(range(len(work)), key=lambda i: slots[i])
+        with self._timed("append"):
+            self.engine._prefill_packed(self.cache, [slots[i] for i in order], [appends[i] for i in order],
+                                        [starts[i] for i in order], self.entry.logits, self.decoder.max_prefill_tokens)
+        self._configure(slots, [p for _, p, _, _ in work], [s for _, _, s, _ in work],
+                        rng_positions=positions, stop_states=states)
+        for handle, prompt, _, _ in work:
+            self.stats["resumed_prefix_tokens"] += len(handle.prefix_token_ids) - 1
+            self.stats["appended_tokens"] += len(prompt) - len(handle.prefix_token_ids) + 1
+            self.stats["resumed_requests"] += 1
+
+    @torch.inference_mode()
+    def poll(self, *, steps: int | None = None) -> list[LFM25SessionResult]:
+        self._check_open()
+        steps = self.decoder.finish_check_interval if steps is None else steps
+        if type(steps) is not int or steps <= 0:
+            raise ValueError("steps must be a positive integer")
+        live = [i for i, r in enumerate(self.requests) if r is not None and not r.delivered]
+        if not live:
+            return []
+        graph, batch = self.decoder._select_graph(self.entry, live)
+        for _ in range(steps):
+            graph.replay()
+        self.stats["decode_steps"] += steps
+        self.stats["decode_row_steps"] += batch * steps
+        self.stats["reserved_row_steps"] += self.batch_size * steps
+        batches = self.stats["decode_batches"]
+        batches[str(batch)] = batches.get(str(batch), 0) + steps
+        reasons = self.state.reasons.cpu().tolist()  # the one device->host read per poll
+        self.cache.check_status()
+        done = [i for i in live if reasons[i]]
+        if not done:
+            return []
+        index = torch.tensor(done, device=self.engine.device)
+        lengths = self.state.lengths[index].cpu().tolist()
+        longest = max(lengths)
+        tokens = self.state.tokens[:, :longest].index_select(0, index).cpu().tolist()
+        logprobs = self.state.logprobs[:, :longest].index_select(0, index).cpu().tolist()
+        results = []
+        for slot, length, ids, probs in zip(done, lengths, tokens, logprobs):
+            request = self.requests[slot]
+            request.delivered = True
+            ids = tuple(ids[:length])
+            handle = LFM25ContinuationHandle(self, slot, request.version, request.prompt + ids)
+            request.handle = handle
+            results.append(LFM25SessionResult(handle, request.prompt, ids,
+                                              tuple(probs[:length]) if request.sampling.return_logprobs else None,
+                                              reasons[slot], None))
+        return results
+
+    @torch.inference_mode()
+    def release(self, handle: LFM25ContinuationHandle) -> None:
+        self._request_for(handle)
+        slot = handle.slot
+        self.requests[slot] = None
+        self.versions[slot] += 1
+        mask = torch.zeros(self.batch_size, dtype=torch.uint8)
+        mask[slot] = 1
+        mask = mask.to(self.engine.device)
+        self.state.alive.masked_fill_(mask.bool(), 0)
+        self.state.pending.masked_fill_(mask.bool(), 0)
+        self.cache.release(mask)
+
+    def close(self):
+        if not self.closed:
+            self.closed = True
+            self.requests = [None] * self.batch_size
+            self.state.alive.zero_()
+            self.state.pending.zero_()
+            if self.decoder._active_session is self:
+                self.decoder._active_session = None
+
+    def __enter__(self):
+        self._check_open()
+        return self
+
+    def __exit__(self, *_):
+        self.close()

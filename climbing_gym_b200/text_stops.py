@@ -1,0 +1,55 @@
+"""ASCII stop strings as a token-level automaton, so stop matching never decodes text on the hot path.
+
+Table format (shared with the sampler kernel's bookkeeping and with the reference,
+src/climbing_gym/inference/text_stops.py:6-45): ``table[state, token] = next_state + 65536 * matched``
+as int32 ``[states, vocab]``. A state is a proper prefix of some stop string that the generated text
+currently ends with (state 0 = empty prefix); ``matched`` is set when appending the token's text
+completes any stop string.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+
+def trim_after_stop(text: str, stops) -> str:
+    """Cut ``text`` right after the earliest-ending completed stop string (display only: the
+    sampled token that contained the stop, and its log-prob, stay in the rollout)."""
+    cut = None
+    for stop in stops:
+        if not stop:
+            continue
+        at = text.find(stop)
+        if at >= 0:
+            end = at + len(stop)
+            cut = end if cut is None else min(cut, end)
+    return text if cut is None else text[:cut]
+
+
+def build_stop_table(tokenizer, stops, *, vocab_size=None) -> torch.Tensor:
+    if any(not s or not s.isascii() for s in stops):
+        raise ValueError("Native text stops must be nonempty ASCII strings")
+    states = sorted({""} | {s[:i] for s in stops for i in range(1, len(s))}, key=len)
+    if len(states) >= 65536:
+        raise ValueError("Too many stop-prefix states")
+    n_tok = len(tokenizer)
+    vocab = n_tok if vocab_size is None else int(vocab_size)
+    if vocab < n_tok:
+        raise ValueError("Model vocabulary must cover the tokenizer vocabulary")
+    pieces = [tokenizer.decode([i], skip_special_tokens=False, clean_up_tokenization_spaces=False)
+              for i in range(n_tok)]
+    # ids past the tokenizer (padded output head) decode to nothing and keep the current state
+    pieces += [""] * (vocab - n_tok)
+    by_length = sorted(range(len(states)), key=lambda i: -len(states[i]))
+    table = np.zeros((len(states), vocab), dtype=np.int32)
+    for index, prefix in enumerate(states):
+        for token, piece in enumerate(pieces):
+            text = prefix + piece
+            longest = next(i for i in by_length if text.endswith(states[i]))
+            table[index, token] = longest + (65536 if any(s in text for s in stops) else 0)
+    return torch.from_numpy(table)
+
+
+def advance_text_stops(table, states, tokens, reasons):
+    value = table[states, tokens].long()
+    return value & 65535, torch.where((reasons == 0) & (value >= 65536), 2, reasons)

@@ -1,0 +1,234 @@
+/*
+ * cgym_b200 - C ABI of the B200-native LFM2.5 rollout-engine kernels (sm_100a).
+ *
+ * The reference (lms21a/climbing-gym) has no FFI: its hot path is Python calling Triton
+ * kernels, FlashAttention and cuBLAS. Each entry point below replaces one of those call
+ * sites; the comment on each cites the reference file:line it stands in for (paths are
+ * relative to src/climbing_gym/inference/ in the reference project).
+ *
+ * Conventions
+ *  - every pointer is a DEVICE pointer unless its name ends in _host;
+ *  - all device memory is owned by the caller (PyTorch tensors on the Python side);
+ *    the library allocates nothing unless an entry point says otherwise;
+ *  - every launch goes on the caller's stream and is CUDA-graph capturable;
+ *  - return value 0 = launched; non-zero = rejected before launch, message in
+ *    cgym_last_error(); device-detected conditions are reported through an int32 status
+ *    word the caller passes in (never a trap);
+ *  - dtype: CGYM_F32 (0) or CGYM_BF16 (1) for activations/weights; KV caches may also be
+ *    CGYM_E4M3 (2) with fp32 per-(token, head) scales.
+ *  - "rows" are batch rows of one step; a row maps to a physical cache slot through
+ *    `slots` (int32, may be NULL meaning row == slot; negative = padding row);
+ *    `active` (uint8, may be NULL meaning all active) masks state writes.
+ */
+#ifndef CGYM_B200_H
+#define CGYM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* cgym_stream_t; /* a cudaStream_t */
+
+enum { CGYM_F32 = 0, CGYM_BF16 = 1, CGYM_E4M3 = 2 };
+
+/* status-word bits written by device code */
+enum {
+  CGYM_STATUS_OK = 0,
+  CGYM_STATUS_PAGE_POOL_EXHAUSTED = 1,
+  CGYM_STATUS_BAD_PAGE = 2,
+  CGYM_STATUS_WAIT_TIMEOUT = 4,
+  CGYM_STATUS_CAPACITY = 8
+};
+
+/* Geometry of the paged hybrid cache (replaces the dense LFM25HybridCache,
+ * lfm25_engine.py:370-431,1165-1221). One page holds `page_size` tokens of every KV head of
+ * one attention layer: pool[layer][page][k|v][kv_head][token][dim]. */
+typedef struct {
+  void* kv_pool;          /* element type kv_dtype */
+  float* kv_scales;       /* [layer][page][k|v][kv_head][token], only for CGYM_E4M3, else NULL */
+  const int32_t* block_table; /* [n_slots][max_blocks] page ids, -1 = none */
+  int32_t n_pages;
+  int32_t page_size;      /* tokens per page, power of two */
+  int32_t max_blocks;     /* block_table row length */
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t kv_dtype;
+} cgym_kv_layout;
+
+const char* cgym_last_error(void);
+int cgym_version(void);
+/* kernels this library has enqueued so far in this process (launches recorded into a CUDA graph
+ * count once, at capture) */
+long long cgym_launch_count(void);
+/* 1 when the device of the current context is compute capability 10.x */
+int cgym_device_supported(void);
+
+/* F.embedding (lfm25_cuda.py:134). tokens int64 [rows]. */
+int cgym_embedding(void* out, const void* table, const int64_t* tokens, int rows, int hidden,
+                   int vocab, int dtype, cgym_stream_t stream);
+
+/* _rms_kernel / rms_norm (lfm25_cuda_kernels.py:32-55): optional residual add, rounded and
+ * emitted to sum_out; y = round(round(x*rsqrt(mean(x^2)+eps)) * w). */
+int cgym_rmsnorm(void* y, void* sum_out, const void* x, const void* residual, const void* w,
+                 int rows, int hidden, float eps, int dtype, cgym_stream_t stream);
+
+/* _rms_quantize / rms_norm_fp8 (lfm25_fp8.py:26-64): as above, then per-row e4m3. */
+int cgym_rmsnorm_quant(uint8_t* q, float* scales, void* sum_out, const void* x,
+                       const void* residual, const void* w, int rows, int hidden, float eps,
+                       cgym_stream_t stream);
+
+/* _swiglu_kernel (lfm25_cuda_kernels.py:58-72): [rows, 2F] -> [rows, F]. */
+int cgym_swiglu(void* y, const void* gate_up, int rows, int ffn, int dtype, cgym_stream_t stream);
+
+/* _swiglu_quantize / swiglu_fp8 (lfm25_fp8.py:44-73). */
+int cgym_swiglu_quant(uint8_t* q, float* scales, const void* gate_up, int rows, int ffn,
+                      cgym_stream_t stream);
+
+/* _quantize_rows (lfm25_fp8.py:16-23,108-116): per-row scale max(absmax/448, 1e-12). */
+int cgym_quantize_rows(uint8_t* q, float* scales, const void* x, int rows, int width, int dtype,
+                       cgym_stream_t stream);
+
+/* _conv_kernel / conv_update (lfm25_cuda_kernels.py:75-110): gated short-conv (k=3) decode
+ * step. state is [n_slots][3][hidden] (tap-major; newest tap last). */
+int cgym_conv_update(void* y, void* state, const void* bcx, const void* conv_w,
+                     const uint8_t* active, const int32_t* slots, int rows, int hidden, int dtype,
+                     cgym_stream_t stream);
+
+/* Prefill-side gated short-conv over packed sequences (lfm25_engine.py:1451-1511):
+ * sequence s covers packed rows [cu_seqlens[s], cu_seqlens[s+1]) and cache slot seq_slots[s];
+ * seq_starts[s] > 0 continues from the slot's stored taps (chunked prefill), 0 starts from
+ * zeros. Writes the slot's final taps. */
+int cgym_conv_prefill(void* y, void* state, const void* bcx, const void* conv_w,
+                      const int32_t* cu_seqlens, const int32_t* seq_slots,
+                      const int32_t* seq_starts, int n_seqs, int total_rows, int hidden,
+                      int dtype, cgym_stream_t stream);
+
+/* _qkv_kernel / prepare_qkv + KV append (lfm25_cuda_kernels.py:113-151, lfm25_batching.py:49-69,
+ * lfm25_fp8_kv.py:27-70): per-head RMSNorm of q and k, RoPE with model-dtype coefficients,
+ * q written to q_out [rows, Hq, D]; k and v of row r written into the paged cache of its slot at
+ * positions[r] (e4m3 caches quantise per (token, head)). k_new/v_new (optional) also receive the
+ * un-quantised rows [rows, Hkv, D]. */
+int cgym_qk_norm_rope_append(void* q_out, void* k_new, void* v_new, const void* qkv,
+                             const void* q_norm_w, const void* k_norm_w, const float* rope_cos,
+                             const float* rope_sin, const int32_t* positions,
+                             const int32_t* slots, const uint8_t* active,
+                             const cgym_kv_layout* kv, int layer, int rows, int n_q_heads,
+                             float eps, int dtype, int32_t* status, cgym_stream_t stream);
+
+/* flash_attn_with_kvcache / fp8 decode+combine (lfm25_cuda.py:146-165,
+ * lfm25_fp8_kv.py:72-172) and, for prefill rows, causal attention (lfm25_engine.py:1387-1394):
+ * row r attends to cache positions [0, kv_lens[r]) of its slot. out [rows, Hq, D].
+ * workspace: fp32, >= rows * Hq * n_splits * (D + 2) elements when n_splits > 1. */
+int cgym_paged_attention(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots,
+                         const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows,
+                         int n_q_heads, float scale, int n_splits, float* workspace, int dtype,
+                         cgym_stream_t stream);
+
+/* F.linear / cuBLAS GEMM and _gemv_kernel (lfm25_cuda_kernels.py:10-29; call sites
+ * lfm25_cuda.py:124-126,141,166,170-172,180,192): y[M,N] = x[M,K] . w[N,K]^T, fp32 accumulate.
+ * row_mask (uint8[M], optional): rows with 0 are not written (replaces the saved-logits
+ * where-merge, lfm25_cuda.py:237-245). impl: 0 = auto, 1 = SIMT tile kernel, 2 = tcgen05/TMEM.
+ * workspace/workspace_bytes: scratch for split-K partials (may be NULL => no split-K). */
+int cgym_gemm(void* y, const void* x, const void* w, const uint8_t* row_mask, int M, int N, int K,
+              int dtype, int impl, void* workspace, int64_t workspace_bytes, int32_t* status,
+              cgym_stream_t stream);
+
+/* _matmul (+_reduce_split) / PackedFP8Weight.linear_quantized (lfm25_fp8.py:76-168):
+ * y = bf16((xq . wq^T) * x_scales[m] * w_scales[n]). */
+int cgym_gemm_fp8(void* y, const uint8_t* xq, const float* x_scales, const uint8_t* wq,
+                  const float* w_scales, const uint8_t* row_mask, int M, int N, int K, int impl,
+                  void* workspace, int64_t workspace_bytes, int32_t* status, cgym_stream_t stream);
+
+/* Per-slot request state of the slot scheduler (LFM25GenerationSession's row tensors,
+ * lfm25_session.py:147-167). All arrays are indexed by slot. */
+typedef struct {
+  int64_t* tokens;        /* [n_slots][capacity] generated ids */
+  float* logprobs;        /* [n_slots][capacity] */
+  int32_t* lengths;       /* generated so far */
+  int32_t* limits;        /* per-request max_new_tokens */
+  int8_t* reasons;        /* 0 running, 1 EOS, 2 stop, 3 length */
+  uint8_t* alive;
+  uint8_t* pending;       /* last sampled token not yet in the cache */
+  int64_t* input_tokens;  /* next decode input */
+  int64_t* stop_states;
+  int64_t* stop_offsets;
+  const int32_t* stop_table; /* flat [states*vocab] tables, next_state + 65536*matched */
+  uint8_t* ignore_eos;
+  int64_t* rng_positions;
+  const int64_t* seeds;
+  const float* temperatures;
+  const int64_t* rng_offsets; /* Philox counter base per slot: row*vocab (batch keying) or 0 */
+  const int32_t* force_eos_at; /* optional: generated position whose token becomes EOS, -1 none */
+  int32_t* seq_lens;      /* cache length per slot; advanced here for rows in `advance` */
+  int32_t capacity;
+  int32_t eos_token_id;
+} cgym_slot_state;
+
+/* _partial_sample + _finish_sample + _record_sample fused (lfm25_sampling.py:10-58,
+ * lfm25_session.py:34-56): Gumbel-max / greedy over logits [n_slots, vocab], sampled-token
+ * log-prob from the untempered logits, then the per-slot bookkeeping. `advance` (uint8[n_slots],
+ * optional) marks rows whose decode input was consumed this step: their seq_lens += 1
+ * (lfm25_cuda.py:185-189). sampled_out/logp_out (optional) receive the raw draw per slot. */
+int cgym_sample_record(const void* logits, const cgym_slot_state* state, const uint8_t* advance,
+                       int64_t* sampled_out, float* logp_out, int n_slots, int vocab, int dtype,
+                       cgym_stream_t stream);
+
+/* Stand-alone sampler (sample_logits / RowSampler.sample, lfm25_sampling.py:61-123). */
+int cgym_sample(int64_t* tokens, float* logprobs, const void* logits, const int64_t* seeds,
+                const int64_t* steps, const float* temperatures, const int64_t* rng_offsets,
+                int rows, int vocab, int dtype, cgym_stream_t stream);
+
+/* Chunked-head completion scoring (lfm25_engine.py:1150-1154): logit[target] - logsumexp. */
+int cgym_target_logprobs(float* out, const void* logits, const int64_t* targets, int rows,
+                         int vocab, int dtype, cgym_stream_t stream);
+
+/* GPU-resident page allocator (no reference counterpart: the reference cache is dense per
+ * slot). free_bitmap bit=1 means free; pages are handed out lowest id first. */
+typedef struct {
+  uint32_t* free_bitmap;  /* [ceil(n_pages/32)] */
+  int32_t* refcount;      /* [n_pages] */
+  int32_t* block_table;   /* [n_slots][max_blocks] */
+  int32_t* n_blocks;      /* [n_slots] pages held */
+  int32_t n_pages;
+  int32_t page_size;
+  int32_t max_blocks;
+  int32_t n_slots;
+} cgym_page_pool;
+
+/* Start of a decode step, inside the graph: snapshots pending -> active_out (the rows whose input
+ * token is consumed this step, lfm25_session.py:467) when `pending` is given, else uses `active`;
+ * then every active row whose next position (seq_lens[slot]) needs a page it does not hold yet
+ * gets the lowest free page, rows served in row order. At most 1024 rows. */
+int cgym_step_begin(const cgym_page_pool* pool, const int32_t* seq_lens, const uint8_t* pending,
+                    uint8_t* active_out, const uint8_t* active, const int32_t* slots, int rows,
+                    int32_t* status, cgym_stream_t stream);
+
+/* Reserve pages so slot s can hold need_tokens[s] tokens (admission / prefill chunk).
+ * No reference counterpart (the reference allocates slots x capacity up front). */
+int cgym_pages_reserve(const cgym_page_pool* pool, const int32_t* slot_ids,
+                       const int32_t* need_tokens, int n, int32_t* status, cgym_stream_t stream);
+
+/* Drop every page of the slots with release_mask != 0 (refcount-aware) and zero their
+ * seq_lens (eviction of finished sequences; the reference only zeroes seq_lens on release,
+ * lfm25_session.py:511-518). */
+int cgym_pages_release(const cgym_page_pool* pool, const uint8_t* release_mask,
+                       int32_t* seq_lens, cgym_stream_t stream);
+
+/* Share a prefix: dst slots get src's full pages by reference (refcount++) and a private copy of
+ * the partially filled last page (replaces copy_prefix_from, lfm25_engine.py:400-423). */
+int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout* kv, int n_layers,
+                    const int32_t* src_slots, const int32_t* dst_slots, const int32_t* prefix_lens,
+                    int n, int32_t* status, cgym_stream_t stream);
+
+/* Test/debug helper: gather one slot's K or V history into a dense [len][Hkv][D] fp32 array
+ * (dequantised), standing in for the dense k_cache/v_cache views the reference tests read
+ * (tests/test_lfm25_adaptive.py:12-60). No reference counterpart as a kernel. */
+int cgym_gather_kv_dense(float* out, const cgym_kv_layout* kv, int layer, int which, int slot,
+                         int length, cgym_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CGYM_B200_H */
