@@ -310,6 +310,7 @@ class LFM25GenerationSession:
         self.state.pending.masked_fill_(mask.bool(), 0)
         self.cache.release(mask)
 
+    @torch.inference_mode()
     def close(self):
         if not self.closed:
             self.closed = True

@@ -54,6 +54,19 @@ def assert_bf16_close(got, want, *, exact_fraction=0.99, ulps=1, what=""):
     assert np.mean(diff == 0) >= exact_fraction, f"{what}: only {np.mean(diff == 0):.4f} bit-identical"
 
 
+def assert_gemm_close(got, want, *, exact_fraction=0.97, what=""):
+    """GEMM outputs: one bf16 rounding step of the value, plus an absolute term for results that are
+    the small remainder of a long cancelling sum (1e-3 of the output RMS, far above fp32
+    accumulation-order noise and far below one bf16 step of a typical output)."""
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2))) + 1e-30
+    err = np.abs(got - want)
+    bound = 2.0 ** -7 * np.abs(want) + 1e-3 * rms
+    assert np.all(err <= bound), f"{what}: worst excess {np.max(err - bound):.3e} (rms {rms:.3e})"
+    exact = np.mean(bf16_bits(got) == bf16_bits(want))
+    assert exact >= exact_fraction, f"{what}: only {exact:.4f} bit-identical"
+
+
 # ------------------------------------------------------------------------------------------ elementwise
 def test_rmsnorm_bf16_and_fp32(dev):
     inp = kernel_inputs()
@@ -154,7 +167,8 @@ def test_conv_prefill_packed_and_chunked(dev):
     y = torch.empty((total, h), device=dev, dtype=torch.bfloat16)
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     args = [torch.from_numpy(np.asarray(v, np.int32)).to(dev) for v in (cu, slots, starts)]
-    nv.call("cgym_conv_prefill", nv.ptr(y), nv.ptr(state), nv.ptr(bf(bcx_np, dev)), nv.ptr(bf(w_np, dev)),
+    bcx_dev, w_dev = bf(bcx_np, dev), bf(w_np, dev)  # keep alive past the launch
+    nv.call("cgym_conv_prefill", nv.ptr(y), nv.ptr(state), nv.ptr(bcx_dev), nv.ptr(w_dev),
             nv.ptr(args[0]), nv.ptr(args[1]), nv.ptr(args[2]), len(lens), total, h, nv.BF16, stream())
     got_y, got_state = f32(y), f32(state)
     for i, n in enumerate(lens):
@@ -185,8 +199,9 @@ def test_qk_norm_rope_append_and_gather(dev):
     slot_ids = torch.arange(rows, device=dev, dtype=torch.int32)
     cache.reserve(slot_ids, (positions + 1).int())
     q = torch.empty((rows, hq, d), device=dev, dtype=torch.bfloat16)
-    nv.call("cgym_qk_norm_rope_append", nv.ptr(q), None, None, nv.ptr(bf(inp["qkv"], dev)),
-            nv.ptr(bf(inp["q_norm_w"], dev)), nv.ptr(bf(inp["k_norm_w"], dev)), nv.ptr(cos), nv.ptr(sin),
+    qkv, q_w, k_w = bf(inp["qkv"], dev), bf(inp["q_norm_w"], dev), bf(inp["k_norm_w"], dev)  # keep alive past the launch
+    nv.call("cgym_qk_norm_rope_append", nv.ptr(q), None, None, nv.ptr(qkv),
+            nv.ptr(q_w), nv.ptr(k_w), nv.ptr(cos), nv.ptr(sin),
             nv.ptr(positions), None, None, cache.kv, 1, rows, hq, 1e-5, nv.BF16, nv.ptr(cache.status), stream())
     want_q, want_k, want_v = ok.qkv_rope(inp["qkv"], inp["q_norm_w"], inp["k_norm_w"], cos_np, sin_np,
                                          inp["positions"], hq, hkv, d, inp["eps"])
@@ -343,7 +358,7 @@ def test_gemm_simt_fp32_and_bf16(dev, shape):
     y = gemm_call(dev, torch.from_numpy(x_np).to(dev), torch.from_numpy(w_np).to(dev), impl=1)
     assert np.allclose(f32(y), want, rtol=1e-5, atol=1e-5)
     yb = gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=1)
-    assert_bf16_close(f32(yb), round_bf16(want), exact_fraction=0.97, what="simt bf16")
+    assert_gemm_close(f32(yb), round_bf16(want), exact_fraction=0.97, what="simt bf16")
 
 
 @pytest.mark.parametrize("shape", [(1, 128, 64), (8, 256, 256), (64, 512, 2048), (33, 384, 320), (128, 1536, 256),
@@ -354,12 +369,12 @@ def test_gemm_tcgen05_matches_fp32_accumulation(dev, shape):
     x_np, w_np = round_bf16(rng.standard_normal((m, k))), round_bf16(rng.standard_normal((n, k)) * 0.1)
     want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
     y = gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=2)
-    assert_bf16_close(f32(y), want, exact_fraction=0.97, what=f"tcgen05 {shape}")
+    assert_gemm_close(f32(y), want, exact_fraction=0.97, what=f"tcgen05 {shape}")
     mask_np = (rng.random(m) < 0.5).astype(np.uint8)
     ym = gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=2, mask=torch.from_numpy(mask_np).to(dev))
     got = f32(ym)
     assert np.all(got[mask_np == 0] == -3.0), "masked rows must not be written"
-    assert_bf16_close(got[mask_np == 1], want[mask_np == 1], exact_fraction=0.97, what="masked rows")
+    assert_gemm_close(got[mask_np == 1], want[mask_np == 1], exact_fraction=0.97, what="masked rows")
 
 
 def test_gemm_tcgen05_split_k_is_deterministic_and_correct(dev):
@@ -369,9 +384,9 @@ def test_gemm_tcgen05_split_k_is_deterministic_and_correct(dev):
     want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
     runs = [f32(gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=3, ws_bytes=8 * m * n * 4)) for _ in range(2)]
     assert np.array_equal(runs[0], runs[1])
-    assert_bf16_close(runs[0], want, exact_fraction=0.97, what="split-K")
+    assert_gemm_close(runs[0], want, exact_fraction=0.97, what="split-K")
     auto = f32(gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=0, ws_bytes=16 * m * n * 4))
-    assert_bf16_close(auto, want, exact_fraction=0.97, what="auto split-K")
+    assert_gemm_close(auto, want, exact_fraction=0.97, what="auto split-K")
 
 
 @pytest.mark.parametrize("impl", [1, 2])
@@ -389,7 +404,7 @@ def test_gemm_fp8_scaled_epilogue(dev, impl, shape):
             m, n, k, impl, None, 0, nv.ptr(status), stream())
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    assert_bf16_close(f32(y), want, exact_fraction=0.97, what=f"fp8 gemm impl {impl}")
+    assert_gemm_close(f32(y), want, exact_fraction=0.97, what=f"fp8 gemm impl {impl}")
 
 
 # ------------------------------------------------------------------------------------------ sampler
@@ -482,6 +497,6 @@ def test_target_logprobs(dev):
     logits_np = round_bf16(rng.standard_normal((7, 5000)) * 3)
     targets_np = rng.integers(0, 5000, size=7)
     out = torch.empty(7, device=dev, dtype=torch.float32)
-    nv.call("cgym_target_logprobs", nv.ptr(out), nv.ptr(bf(logits_np, dev)), nv.ptr(torch.from_numpy(targets_np).to(dev)),
-            7, 5000, nv.BF16, stream())
+    logits_dev, targets_dev = bf(logits_np, dev), torch.from_numpy(targets_np).to(dev)
+    nv.call("cgym_target_logprobs", nv.ptr(out), nv.ptr(logits_dev), nv.ptr(targets_dev), 7, 5000, nv.BF16, stream())
     assert np.allclose(out.cpu().numpy(), OracleEngine.logprob_of(logits_np, targets_np), atol=3e-6)
