@@ -64,7 +64,9 @@ SIGNATURES = {
     "cgym_conv_prefill": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "cgym_qk_norm_rope_append": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.POINTER(KVLayout), _I, _I, _I,
                                  _F, _I, _P, _P],
-    "cgym_paged_attention": [_P, _P, _P, _P, _P, C.POINTER(KVLayout), _I, _I, _I, _F, _I, _P, _I, _P],
+    "cgym_paged_attention": [_P, _P, _P, _P, _P, C.POINTER(KVLayout), _I, _I, _I, _F, _I, _P, _I, _I, _P, _P],
+    "cgym_prefill_attention": [_P, _P, _P, _P, _P, _P, C.POINTER(KVLayout), _I, _I, _I, _F, _I, _P, _P],
+    "cgym_scatter_kv_dense": [_P, _P, C.POINTER(KVLayout), _I, _I, _I, _I, _P],
     "cgym_gemm": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_fp8": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P],

@@ -66,11 +66,11 @@ paged_attention_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, const int
     float s[8];
     float v_scale = 1.0f;
     if (ok) {
-      const KV* krow = pool + kv_elem_offset(kv, layer, page, 0, kh, tok % P);
+      const KV* block = pool + kv_block_offset(kv, layer, page, kh);
 #pragma unroll
       for (int g = 0; g < 8; ++g) s[g] = 0.0f;
       for (int d = 0; d < D; ++d) {
-        const float kd = kv_load<KV>(krow + d);
+        const float kd = kv_load<KV>(block + kv_row_index(tok % P, d, D, static_cast<int>(sizeof(KV))));
 #pragma unroll
         for (int g = 0; g < 8; ++g)
           if (g < G) s[g] = fmaf(qs[g * D + d], kd, s[g]);
@@ -105,10 +105,11 @@ paged_attention_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, const int
     for (int tt = 0; tt < n_here; ++tt) {
       const int pg = __shfl_sync(0xffffffffu, page, tt);
       if (pg < 0 || pg >= kv.n_pages) continue;  // uniform across the warp
-      const KV* vrow = pool + kv_elem_offset(kv, layer, pg, 1, kh, (t0 + tt) % P);
+      const KV* vt = pool + kv_block_offset(kv, layer, pg, kh) + P * D;  // V^T part: row = dim
       float vv[PER_LANE];
 #pragma unroll
-      for (int j = 0; j < per_lane; ++j) vv[j] = kv_load<KV>(vrow + lane + 32 * j);
+      for (int j = 0; j < per_lane; ++j)
+        vv[j] = kv_load<KV>(vt + kv_row_index(lane + 32 * j, (t0 + tt) % P, P, static_cast<int>(sizeof(KV))));
 #pragma unroll
       for (int g = 0; g < 8; ++g) {
         if (g < G) {
@@ -178,21 +179,63 @@ __global__ void attention_combine_kernel(TQ* __restrict__ out, const float* __re
 
 using namespace cgym;
 
+namespace cgym {
+bool attention_mma_supported(const cgym_kv_layout* kv, int n_q_heads, int dtype);
+int launch_decode_attention_mma(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots,
+                                const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows, int n_q_heads,
+                                float scale, int n_splits, float* workspace, int32_t* status, cudaStream_t stream);
+int launch_prefill_attention_mma(void* out, const void* q, const int32_t* tile_row0, const int32_t* tile_ntok,
+                                 const int32_t* tile_slot, const int32_t* tile_pos0, const cgym_kv_layout* kv, int layer,
+                                 int n_tiles, int n_q_heads, float scale, int32_t* status, cudaStream_t stream);
+}  // namespace cgym
+
+extern "C" int cgym_prefill_attention(void* out, const void* q, const int32_t* tile_row0, const int32_t* tile_ntok,
+                                      const int32_t* tile_slot, const int32_t* tile_pos0, const cgym_kv_layout* kv,
+                                      int layer, int n_tiles, int n_q_heads, float scale, int dtype, int32_t* status,
+                                      cgym_stream_t stream) {
+  CGYM_REQUIRE(kv != nullptr && status != nullptr, "prefill_attention: kv layout and status are required");
+  CGYM_REQUIRE(tile_row0 && tile_ntok && tile_slot && tile_pos0, "prefill_attention: tile lists are required");
+  CGYM_REQUIRE(kv->n_kv_heads > 0 && n_q_heads % kv->n_kv_heads == 0, "prefill_attention: heads must group evenly");
+  CGYM_REQUIRE(attention_mma_supported(kv, n_q_heads, dtype),
+               "prefill_attention: needs bf16 activations, a bf16 or e4m3 cache, head_dim 64, 64-token pages, group <= 16");
+  CGYM_REQUIRE(kv->kv_dtype != CGYM_E4M3 || kv->kv_scales != nullptr, "e4m3 KV needs a scale pool");
+  if (n_tiles == 0) return 0;
+  if (int rc = launch_prefill_attention_mma(out, q, tile_row0, tile_ntok, tile_slot, tile_pos0, kv, layer, n_tiles,
+                                            n_q_heads, scale, status, as_stream(stream)))
+    return rc;
+  return check_launch("prefill_attention");
+}
+
 extern "C" int cgym_paged_attention(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots,
                                     const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows,
                                     int n_q_heads, float scale, int n_splits, float* workspace, int dtype,
-                                    cgym_stream_t stream) {
+                                    int impl, int32_t* status, cgym_stream_t stream) {
   CGYM_REQUIRE(kv != nullptr, "paged_attention: kv layout is required");
   const int D = kv->head_dim;
   CGYM_REQUIRE(D == 32 || D == 64 || D == 128 || D == 256, "paged_attention: head_dim must be 32, 64, 128 or 256");
   CGYM_REQUIRE(kv->n_kv_heads > 0 && n_q_heads % kv->n_kv_heads == 0, "paged_attention: heads must group evenly");
   const int G = n_q_heads / kv->n_kv_heads;
-  CGYM_REQUIRE(G <= 8 && G * D <= 32 * ATT_MAX_ACC, "paged_attention: group too large (G <= 8, G*D <= 1024)");
   CGYM_REQUIRE(n_splits >= 1 && n_splits <= 64, "paged_attention: n_splits must be in [1, 64]");
   CGYM_REQUIRE(n_splits == 1 || workspace != nullptr, "paged_attention: split-KV needs a workspace");
   CGYM_REQUIRE(kv->kv_dtype != CGYM_E4M3 || kv->kv_scales != nullptr, "e4m3 KV needs a scale pool");
+  CGYM_REQUIRE(impl >= 0 && impl <= 2, "paged_attention: impl must be 0 (auto), 1 (CUDA cores) or 2 (tensor cores)");
   if (rows == 0) return 0;
   CGYM_REQUIRE(kv->n_kv_heads <= 65535 && n_q_heads <= 65535, "too many heads");
+  const bool mma_ok = status != nullptr && attention_mma_supported(kv, n_q_heads, dtype);
+  CGYM_REQUIRE(impl != 2 || mma_ok, "paged_attention: the tensor-core kernel needs bf16 activations, a bf16 or e4m3 "
+                                    "cache, head_dim 64, 64-token pages, group <= 16 and a status word");
+  if (impl == 2 || (impl == 0 && mma_ok)) {
+    if (int rc = launch_decode_attention_mma(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits,
+                                             workspace, status, as_stream(stream)))
+      return rc;
+    if (n_splits > 1) {
+      if (dtype == CGYM_BF16)
+        attention_combine_kernel<__nv_bfloat16><<<dim3(rows, n_q_heads), D, 0, as_stream(stream)>>>(
+            static_cast<__nv_bfloat16*>(out), workspace, rows, n_q_heads, D, n_splits);
+    }
+    return check_launch("paged_attention", n_splits > 1 ? 2 : 1);
+  }
+  CGYM_REQUIRE(G <= 8 && G * D <= 32 * ATT_MAX_ACC, "paged_attention: group too large (G <= 8, G*D <= 1024)");
   dim3 grid(rows, kv->n_kv_heads, n_splits);
   const size_t smem = (static_cast<size_t>(G) * D * (1 + ATT_WARPS) + 2 * ATT_WARPS * G) * sizeof(float);
 #define LAUNCH_ATT_D(TQ, KV, PL)                                                                         \

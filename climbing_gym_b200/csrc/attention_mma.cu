@@ -1,0 +1,559 @@
+// Tensor-core paged attention for bf16 and e4m3 KV caches (head_dim 64, 64-token pages).
+//
+// Data movement: a (page, kv_head) block of the cache - K as [token][dim] followed by V^T as
+// [dim][token], 16-byte chunks already XOR-swizzled in global memory - is brought into shared memory
+// by ONE cp.async.bulk (TMA bulk copy, mbarrier completion), e4m3 caches add one 512-byte copy of the
+// per-token scales. Fragment loads are then plain 32-bit shared loads without bank conflicts.
+//
+// Math: S = Q.K^T and O += P.V on mma.sync m16n8k16 with fp32 accumulation; an m-tile is 16
+// (token, head) rows of one GQA group, so the G query heads that share a KV head reuse every staged
+// byte. Softmax is online in fp32 (exp2 domain, running max). P is rounded to the MMA input type
+// before P.V: bf16 for bf16 caches; for e4m3 caches K and V are widened to fp16 (exact) and the
+// per-token K scale multiplies the score, the V scale multiplies P before its rounding.
+//
+// decode kernel : one query token per row, grid (rows, kv_heads, splits); the four warps of a CTA
+//                 take pages round-robin, each with its own 2-stage bulk-copy ring and softmax
+//                 state, merged through shared memory (and splits through an fp32 workspace).
+// prefill kernel: a CTA owns up to 128 / G consecutive query tokens of one sequence for one KV head;
+//                 a producer warp streams the causal range of pages through a 4-stage ring that the
+//                 four consumer warps (two m-tiles each) share.
+// Every mbarrier wait is bounded; on expiry the CTA flags CGYM_STATUS_WAIT_TIMEOUT and drains.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace cgym {
+
+constexpr unsigned long long ATT_WAIT_LIMIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t att_smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ unsigned long long att_timer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void att_bar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void att_bar_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void att_bar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool att_bar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool att_bar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (att_bar_try(bar, parity)) return true;
+  const unsigned long long start = att_timer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (att_bar_try(bar, parity)) return true;
+    if ((spin & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (att_timer() - start > ATT_WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+// linear global -> shared bulk copy; both addresses 16-byte aligned, size a multiple of 16
+__device__ __forceinline__ void att_bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ uint32_t att_lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float att_lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
+template <bool F16>
+__device__ __forceinline__ void att_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (F16) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+template <bool F16>
+__device__ __forceinline__ uint32_t att_pack(float lo, float hi) {
+  if constexpr (F16) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+// two e4m3 codes (low 16 bits) -> packed fp16x2 (exact)
+__device__ __forceinline__ uint32_t att_e4m3x2_to_f16x2(uint32_t two_codes) {
+  uint32_t out;
+  asm volatile("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(out) : "r"(two_codes));
+  return out;
+}
+
+// Geometry of one staged (page, head) block for cache element size EB, head_dim D, page size P.
+template <int EB, int D, int P>
+struct BlockGeom {
+  static constexpr int K_ROW = D * EB;          // bytes per K row (one token)
+  static constexpr int V_ROW = P * EB;          // bytes per V^T row (one dim)
+  static constexpr int K_CPR = K_ROW / 16;
+  static constexpr int V_CPR = V_ROW / 16;
+  static constexpr int K_BYTES = P * K_ROW;
+  static constexpr int BLOCK_BYTES = 2 * P * D * EB;
+  static constexpr int SCALE_BYTES = (EB == 1) ? 2 * P * 4 : 0;
+  static constexpr int STAGE_BYTES = BLOCK_BYTES + SCALE_BYTES;
+  // token held in column c of S n-tile t (see the fragment notes in the file header of the C ABI docs)
+  static __device__ __forceinline__ int token_of(int t, int c) {
+    if constexpr (EB == 1) return 16 * (t >> 1) + 4 * (c >> 1) + 2 * (t & 1) + (c & 1);
+    else return 8 * t + c;
+  }
+};
+
+// Loads the A fragments of one m-tile of Q. Row R of the tile is (token R / G, head R % G).
+template <int EB, int D, typename TQ>
+__device__ __forceinline__ void load_q_frags(uint32_t (&qa)[D / 16][4], const TQ* __restrict__ q_base, int row_lo,
+                                             int row_hi, int n_rows, int G, int n_q_heads, int head0, int lane) {
+  constexpr bool F16 = EB == 1;
+  const int j = lane & 3;
+  const int rows[2] = {row_lo, row_hi};
+#pragma unroll
+  for (int s = 0; s < D / 16; ++s) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int R = rows[half];
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (R < n_rows) {
+        const TQ* src = q_base + (static_cast<int64_t>(R / G) * n_q_heads + head0 + (R % G)) * D;
+        // bf16 path: k = 16s + 2j + {0,1} and + 8; e4m3 path: dims 16s + 4j + {0,1} and {2,3}
+        const int d0 = F16 ? 16 * s + 4 * j : 16 * s + 2 * j;
+        const int d1 = F16 ? d0 + 2 : d0 + 8;
+        v[0] = Elem<TQ>::load(src + d0); v[1] = Elem<TQ>::load(src + d0 + 1);
+        v[2] = Elem<TQ>::load(src + d1); v[3] = Elem<TQ>::load(src + d1 + 1);
+      }
+      qa[s][half] = att_pack<F16>(v[0], v[1]);      // a0a1 (row_lo) / a2a3 (row_hi)
+      qa[s][2 + half] = att_pack<F16>(v[2], v[3]);  // a4a5 / a6a7
+    }
+  }
+}
+
+// One page for one m-tile: S = Q K^T (scaled, masked), online softmax update, O += P V.
+// limit_lo / limit_hi: number of cache positions rows row_lo / row_hi may see (0 masks the row).
+template <int EB, int D, int P>
+__device__ __forceinline__ void attend_page(const uint32_t (&qa)[D / 16][4], float (&o)[D / 8][4], float (&m)[2],
+                                            float (&l)[2], uint32_t stage, int page_token0, int limit_lo,
+                                            int limit_hi, float scale_log2, int lane) {
+  using Geo = BlockGeom<EB, D, P>;
+  constexpr bool F16 = EB == 1;
+  constexpr int NT = P / 8, KS = D / 16, OT = D / 8, PS = P / 16;
+  const int c8 = lane >> 2, j = lane & 3;
+  float s[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.f;
+    const int tok = Geo::token_of(t, c8);  // K row this thread feeds for column c8
+    const uint32_t row_addr = stage + tok * Geo::K_ROW;
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+      uint32_t b0, b1;
+      if constexpr (F16) {
+        const uint32_t w = att_lds32(row_addr + kv_swizzle(tok, k, Geo::K_CPR) * 16 + 4 * j);
+        b0 = att_e4m3x2_to_f16x2(w & 0xFFFFu);
+        b1 = att_e4m3x2_to_f16x2(w >> 16);
+      } else {
+        b0 = att_lds32(row_addr + kv_swizzle(tok, 2 * k, Geo::K_CPR) * 16 + 4 * j);
+        b1 = att_lds32(row_addr + kv_swizzle(tok, 2 * k + 1, Geo::K_CPR) * 16 + 4 * j);
+      }
+      att_mma<F16>(s[t], qa[k], b0, b1);
+    }
+  }
+  // scale (x per-token K scale for e4m3), causal / length mask, page maximum per row
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int tok = Geo::token_of(t, 2 * j + i);
+      float ks = scale_log2;
+      if constexpr (F16) ks *= att_lds_f32(stage + Geo::BLOCK_BYTES + 4 * tok);
+      const int pos = page_token0 + tok;
+      s[t][i] = pos < limit_lo ? s[t][i] * ks : -INFINITY;
+      s[t][2 + i] = pos < limit_hi ? s[t][2 + i] * ks : -INFINITY;
+      mx[0] = fmaxf(mx[0], s[t][i]);
+      mx[1] = fmaxf(mx[1], s[t][2 + i]);
+    }
+  }
+  float alpha[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    const float m_new = fmaxf(m[h], mx[h]);
+    alpha[h] = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - m_new);
+    m[h] = m_new;
+    l[h] *= alpha[h];
+  }
+#pragma unroll
+  for (int u = 0; u < OT; ++u) {
+    o[u][0] *= alpha[0]; o[u][1] *= alpha[0];
+    o[u][2] *= alpha[1]; o[u][3] *= alpha[1];
+  }
+  // P = exp2(S - m); fp32 row sums; P (x V scale) rounded to the MMA input type
+  const float m0 = (m[0] == -INFINITY) ? 0.f : m[0], m1 = (m[1] == -INFINITY) ? 0.f : m[1];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      float p0 = exp2f(s[t][i] - m0), p1 = exp2f(s[t][2 + i] - m1);  // exp2(-inf) = 0 for masked entries
+      l[0] += p0;
+      l[1] += p1;
+      if constexpr (F16) {
+        const float vs = att_lds_f32(stage + Geo::BLOCK_BYTES + 4 * P + 4 * Geo::token_of(t, 2 * j + i));
+        p0 *= vs;
+        p1 *= vs;
+      }
+      s[t][i] = p0;
+      s[t][2 + i] = p1;
+    }
+  }
+  const uint32_t vt = stage + Geo::K_BYTES;
+#pragma unroll
+  for (int k = 0; k < PS; ++k) {
+    uint32_t pa[4];
+    pa[0] = att_pack<F16>(s[2 * k][0], s[2 * k][1]);
+    pa[1] = att_pack<F16>(s[2 * k][2], s[2 * k][3]);
+    pa[2] = att_pack<F16>(s[2 * k + 1][0], s[2 * k + 1][1]);
+    pa[3] = att_pack<F16>(s[2 * k + 1][2], s[2 * k + 1][3]);
+#pragma unroll
+    for (int u = 0; u < OT; ++u) {
+      const int dim = 8 * u + c8;  // V^T row this thread feeds for output column c8
+      const uint32_t row_addr = vt + dim * Geo::V_ROW;
+      uint32_t b0, b1;
+      if constexpr (F16) {
+        const uint32_t w = att_lds32(row_addr + kv_swizzle(dim, k, Geo::V_CPR) * 16 + 4 * j);
+        b0 = att_e4m3x2_to_f16x2(w & 0xFFFFu);
+        b1 = att_e4m3x2_to_f16x2(w >> 16);
+      } else {
+        b0 = att_lds32(row_addr + kv_swizzle(dim, 2 * k, Geo::V_CPR) * 16 + 4 * j);
+        b1 = att_lds32(row_addr + kv_swizzle(dim, 2 * k + 1, Geo::V_CPR) * 16 + 4 * j);
+      }
+      att_mma<F16>(o[u], pa, b0, b1);
+    }
+  }
+}
+
+__device__ __forceinline__ void stage_block(uint32_t dst, uint32_t bar, const uint8_t* pool, const float* scales,
+                                            int64_t block_byte_offset, int64_t scale_offset, int block_bytes,
+                                            int scale_bytes) {
+  att_bar_expect(bar, block_bytes + scale_bytes);
+  att_bulk_copy(dst, pool + block_byte_offset, block_bytes, bar);
+  if (scale_bytes) att_bulk_copy(dst + block_bytes, scales + scale_offset, scale_bytes, bar);
+}
+
+// ------------------------------------------------------------------------------------------ decode
+template <typename TQ, int EB, int D, int P>
+__global__ void __launch_bounds__(128, 1)
+decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, const int32_t* __restrict__ kv_lens,
+                            const int32_t* __restrict__ slots, const uint8_t* __restrict__ active,
+                            cgym_kv_layout kv, int layer, int n_q_heads, float scale, int n_splits,
+                            float* __restrict__ workspace, int32_t* __restrict__ status) {
+  using Geo = BlockGeom<EB, D, P>;
+  constexpr int OT = D / 8;
+  extern __shared__ __align__(128) uint8_t att_smem[];
+  __shared__ __align__(8) uint64_t bars[4][2];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
+  const int G = n_q_heads / kv.n_kv_heads;
+  const int slot = slots != nullptr ? slots[row] : row;
+  int len = kv_lens[row];
+  if ((active != nullptr && !active[row]) || slot < 0 || len < 0) len = 0;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int w = 0; w < 4; ++w) { att_bar_init(att_smem_u32(&bars[w][0]), 1); att_bar_init(att_smem_u32(&bars[w][1]), 1); }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  const int total_pages = (len + P - 1) / P;
+  const int per_split = (total_pages + n_splits - 1) / n_splits;
+  const int page_begin = min(total_pages, split * per_split), page_end = min(total_pages, page_begin + per_split);
+  const int n_mine = (page_end - page_begin - warp + 3) / 4;  // pages page_begin + warp + 4 i
+  const int32_t* table = kv.block_table + static_cast<int64_t>(slot < 0 ? 0 : slot) * kv.max_blocks;
+  const uint8_t* pool = static_cast<const uint8_t*>(kv.kv_pool);
+  const uint32_t ring = att_smem_u32(att_smem) + warp * 2 * Geo::STAGE_BYTES;
+
+  uint32_t qa[D / 16][4];
+  load_q_frags<EB, D, TQ>(qa, q + static_cast<int64_t>(row) * n_q_heads * D, lane >> 2, (lane >> 2) + 8, G, G,
+                          n_q_heads, kh * G, lane);
+  float o[OT][4], m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < OT; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.f;
+  const float scale_log2 = scale * 1.4426950408889634f;
+
+  auto issue = [&](int i) {
+    if (lane == 0) {
+      int page = table[page_begin + warp + 4 * i];
+      if (page < 0 || page >= kv.n_pages) { atomicOr(status, CGYM_STATUS_BAD_PAGE); page = 0; }
+      stage_block(ring + (i & 1) * Geo::STAGE_BYTES, att_smem_u32(&bars[warp][i & 1]), pool, kv.kv_scales,
+                  kv_block_offset(kv, layer, page, kh) * EB, kv_scale_offset(kv, layer, page, 0, kh, 0),
+                  Geo::BLOCK_BYTES, Geo::SCALE_BYTES);
+    }
+  };
+  if (n_mine > 0) issue(0);
+  int issued = n_mine > 0 ? 1 : 0;
+  for (int i = 0; i < n_mine; ++i) {
+    if (i + 1 < n_mine) { issue(i + 1); issued = i + 2; }
+    if (!att_bar_wait(att_smem_u32(&bars[warp][i & 1]), (i >> 1) & 1, &abort_flag)) break;
+    const int token0 = (page_begin + warp + 4 * i) * P;
+    attend_page<EB, D, P>(qa, o, m, l, ring + (i & 1) * Geo::STAGE_BYTES, token0, len, len, scale_log2, lane);
+    __syncwarp();  // every lane is done reading this stage before lane 0 refills it
+  }
+  if (abort_flag && lane == 0) {  // let copies in flight land before shared memory is reused / released
+    for (int i = max(0, issued - 2); i < issued; ++i) att_bar_wait(att_smem_u32(&bars[warp][i & 1]), (i >> 1) & 1, &abort_flag);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) atomicOr(status, CGYM_STATUS_WAIT_TIMEOUT);
+
+  // merge the four warps through shared memory (the rings are free now)
+  float* w_o = reinterpret_cast<float*>(att_smem);          // [4][16][D]
+  float* w_m = w_o + 4 * 16 * D;                            // [4][16]
+  float* w_l = w_m + 4 * 16;                                // [4][16]
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+  }
+  {
+    const int r0 = lane >> 2, j = lane & 3;
+    if (j == 0) {
+      w_m[warp * 16 + r0] = m[0]; w_m[warp * 16 + r0 + 8] = m[1];
+      w_l[warp * 16 + r0] = l[0]; w_l[warp * 16 + r0 + 8] = l[1];
+    }
+#pragma unroll
+    for (int u = 0; u < OT; ++u) {
+      float* dst = w_o + (warp * 16 + r0) * D + 8 * u + 2 * j;
+      dst[0] = o[u][0]; dst[1] = o[u][1];
+      dst[8 * D] = o[u][2]; dst[8 * D + 1] = o[u][3];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i % D;
+    float mm = -INFINITY;
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, w_m[w * 16 + g]);
+    float total = 0.f, value = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float mw = w_m[w * 16 + g];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - mm);
+      total += f * w_l[w * 16 + g];
+      value += f * w_o[(w * 16 + g) * D + d];
+    }
+    const int head = kh * G + g;
+    if (n_splits == 1) {
+      Elem<TQ>::store(out + (static_cast<int64_t>(row) * n_q_heads + head) * D + d, value / fmaxf(total, 1.0e-20f));
+    } else {
+      const int64_t part = (static_cast<int64_t>(row) * n_q_heads + head) * n_splits + split;
+      const int64_t n_parts = static_cast<int64_t>(gridDim.x) * n_q_heads * n_splits;
+      workspace[part * D + d] = value;
+      if (d == 0) {
+        workspace[n_parts * D + part] = mm * 0.6931471805599453f;  // the combine kernel works in the natural-log domain
+        workspace[n_parts * (D + 1) + part] = total;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------ prefill
+struct PrefillTiles {
+  const int32_t* row0;   // packed row of the tile's first query token
+  const int32_t* ntok;   // query tokens in the tile (<= 128 / G)
+  const int32_t* slot;   // cache slot of the sequence
+  const int32_t* pos0;   // cache position of the tile's first query token
+};
+
+template <typename TQ, int EB, int D, int P>
+__global__ void __launch_bounds__(160, 1)
+prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, PrefillTiles tiles, cgym_kv_layout kv,
+                             int layer, int n_q_heads, float scale, int32_t* __restrict__ status) {
+  using Geo = BlockGeom<EB, D, P>;
+  constexpr int OT = D / 8, STAGES = 4, MT = 2;
+  extern __shared__ __align__(128) uint8_t att_smem[];
+  __shared__ __align__(8) uint64_t bar_full[STAGES];
+  __shared__ __align__(8) uint64_t bar_empty[STAGES];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, kh = blockIdx.y;
+  const int G = n_q_heads / kv.n_kv_heads;
+  const int row0 = tiles.row0[tile], ntok = tiles.ntok[tile], slot = tiles.slot[tile], pos0 = tiles.pos0[tile];
+  const int n_rows = ntok * G;                 // (token, head) rows of this tile, <= 128
+  const int n_pages = (pos0 + ntok + P - 1) / P;  // causal range of the tile's last token
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) { att_bar_init(att_smem_u32(&bar_full[s]), 1); att_bar_init(att_smem_u32(&bar_empty[s]), 4); }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const uint32_t ring = att_smem_u32(att_smem);
+  const int32_t* table = kv.block_table + static_cast<int64_t>(slot) * kv.max_blocks;
+
+  if (warp == 4) {
+    // ---- producer ----
+    if (lane == 0) {
+      const uint8_t* pool = static_cast<const uint8_t*>(kv.kv_pool);
+      int issued = 0;
+      for (int i = 0; i < n_pages; ++i) {
+        const int s = i % STAGES;
+        if (!att_bar_wait(att_smem_u32(&bar_empty[s]), ((i / STAGES) & 1) ^ 1, &abort_flag)) break;
+        int page = table[i];
+        if (page < 0 || page >= kv.n_pages) { atomicOr(status, CGYM_STATUS_BAD_PAGE); page = 0; }
+        stage_block(ring + s * Geo::STAGE_BYTES, att_smem_u32(&bar_full[s]), pool, kv.kv_scales,
+                    kv_block_offset(kv, layer, page, kh) * EB, kv_scale_offset(kv, layer, page, 0, kh, 0),
+                    Geo::BLOCK_BYTES, Geo::SCALE_BYTES);
+        issued = i + 1;
+      }
+      if (abort_flag)
+        for (int i = max(0, issued - STAGES); i < issued; ++i)
+          att_bar_wait(att_smem_u32(&bar_full[i % STAGES]), (i / STAGES) & 1, &abort_flag);
+    }
+  } else {
+    // ---- consumers: warp w owns rows [32 w, 32 w + 32) as two m-tiles ----
+    uint32_t qa[MT][D / 16][4];
+    float o[MT][OT][4], m[MT][2], l[MT][2];
+    int limit[MT][2];
+    const TQ* q_base = q + static_cast<int64_t>(row0) * n_q_heads * D;
+    int warp_limit = 0;
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const int r_lo = warp * 32 + t * 16 + (lane >> 2), r_hi = r_lo + 8;
+      load_q_frags<EB, D, TQ>(qa[t], q_base, r_lo, r_hi, n_rows, G, n_q_heads, kh * G, lane);
+      limit[t][0] = r_lo < n_rows ? pos0 + r_lo / G + 1 : 0;
+      limit[t][1] = r_hi < n_rows ? pos0 + r_hi / G + 1 : 0;
+      warp_limit = max(warp_limit, max(limit[t][0], limit[t][1]));
+      m[t][0] = m[t][1] = -INFINITY;
+      l[t][0] = l[t][1] = 0.f;
+#pragma unroll
+      for (int u = 0; u < OT; ++u) o[t][u][0] = o[t][u][1] = o[t][u][2] = o[t][u][3] = 0.f;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) warp_limit = max(warp_limit, __shfl_xor_sync(0xffffffffu, warp_limit, off));
+    const float scale_log2 = scale * 1.4426950408889634f;
+    for (int i = 0; i < n_pages; ++i) {
+      const int s = i % STAGES;
+      if (!att_bar_wait(att_smem_u32(&bar_full[s]), (i / STAGES) & 1, &abort_flag)) break;
+      if (i * P < warp_limit) {
+#pragma unroll
+        for (int t = 0; t < MT; ++t)
+          attend_page<EB, D, P>(qa[t], o[t], m[t], l[t], ring + s * Geo::STAGE_BYTES, i * P, limit[t][0], limit[t][1],
+                                scale_log2, lane);
+      }
+      __syncwarp();
+      if (lane == 0) att_bar_arrive(att_smem_u32(&bar_empty[s]));
+    }
+    // normalise and store: fragment (row, dims 8u + 2j + {0,1})
+    const int j = lane & 3;
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float sum = l[t][h];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        const int R = warp * 32 + t * 16 + (lane >> 2) + 8 * h;
+        if (R < n_rows) {
+          const float inv = 1.0f / fmaxf(sum, 1.0e-20f);
+          TQ* dst = out + (static_cast<int64_t>(row0 + R / G) * n_q_heads + kh * G + (R % G)) * D;
+#pragma unroll
+          for (int u = 0; u < OT; ++u) {
+            Elem<TQ>::store(dst + 8 * u + 2 * j, o[t][u][2 * h] * inv);
+            Elem<TQ>::store(dst + 8 * u + 2 * j + 1, o[t][u][2 * h + 1] * inv);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) atomicOr(status, CGYM_STATUS_WAIT_TIMEOUT);
+}
+
+// ------------------------------------------------------------------------------------------ launchers
+bool attention_mma_supported(const cgym_kv_layout* kv, int n_q_heads, int dtype) {
+  if (dtype != CGYM_BF16) return false;
+  if (kv->kv_dtype != CGYM_BF16 && kv->kv_dtype != CGYM_E4M3) return false;
+  if (kv->page_size != 64 || kv->head_dim != 64) return false;
+  const int G = n_q_heads / kv->n_kv_heads;
+  return G >= 1 && G <= 16 && n_q_heads % kv->n_kv_heads == 0;
+}
+
+template <typename K>
+static int set_smem(K kernel, int bytes) {
+  const cudaError_t rc = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  CGYM_REQUIRE(rc == cudaSuccess, "attention: cannot reserve %d bytes of shared memory: %s", bytes, cudaGetErrorString(rc));
+  return 0;
+}
+
+template <int EB, int D>
+static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots, const uint8_t* active,
+                         const cgym_kv_layout* kv, int layer, int rows, int n_q_heads, float scale, int n_splits,
+                         float* workspace, int32_t* status, cudaStream_t stream) {
+  using T = __nv_bfloat16;
+  using Geo = BlockGeom<EB, D, 64>;
+  constexpr int ring = 4 * 2 * Geo::STAGE_BYTES, merge = (4 * 16 * D + 2 * 4 * 16) * 4;
+  constexpr int smem = ring > merge ? ring : merge;
+  auto kernel = decode_attention_mma_kernel<T, EB, D, 64>;
+  static bool configured = false;
+  if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
+  kernel<<<dim3(rows, kv->n_kv_heads, n_splits), 128, smem, stream>>>(
+      static_cast<T*>(out), static_cast<const T*>(q), kv_lens, slots, active, *kv, layer, n_q_heads, scale, n_splits,
+      workspace, status);
+  return 0;
+}
+
+int launch_decode_attention_mma(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots,
+                                const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows, int n_q_heads,
+                                float scale, int n_splits, float* workspace, int32_t* status, cudaStream_t stream) {
+  const bool fp8 = kv->kv_dtype == CGYM_E4M3;
+  return fp8 ? launch_decode<1, 64>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, workspace, status, stream)
+             : launch_decode<2, 64>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, workspace, status, stream);
+}
+
+template <int EB, int D>
+static int launch_prefill(void* out, const void* q, const PrefillTiles& tiles, const cgym_kv_layout* kv, int layer,
+                          int n_tiles, int n_q_heads, float scale, int32_t* status, cudaStream_t stream) {
+  using T = __nv_bfloat16;
+  using Geo = BlockGeom<EB, D, 64>;
+  constexpr int smem = 4 * Geo::STAGE_BYTES;
+  auto kernel = prefill_attention_mma_kernel<T, EB, D, 64>;
+  static bool configured = false;
+  if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
+  kernel<<<dim3(n_tiles, kv->n_kv_heads), 160, smem, stream>>>(static_cast<T*>(out), static_cast<const T*>(q), tiles, *kv,
+                                                               layer, n_q_heads, scale, status);
+  return 0;
+}
+
+int launch_prefill_attention_mma(void* out, const void* q, const int32_t* tile_row0, const int32_t* tile_ntok,
+                                 const int32_t* tile_slot, const int32_t* tile_pos0, const cgym_kv_layout* kv, int layer,
+                                 int n_tiles, int n_q_heads, float scale, int32_t* status, cudaStream_t stream) {
+  const PrefillTiles tiles{tile_row0, tile_ntok, tile_slot, tile_pos0};
+  const bool fp8 = kv->kv_dtype == CGYM_E4M3;
+  return fp8 ? launch_prefill<1, 64>(out, q, tiles, kv, layer, n_tiles, n_q_heads, scale, status, stream)
+             : launch_prefill<2, 64>(out, q, tiles, kv, layer, n_tiles, n_q_heads, scale, status, stream);
+}
+
+}  // namespace cgym

@@ -86,15 +86,42 @@ __device__ __forceinline__ float block_max(float v, float* scratch) {
 }
 
 // ---- paged KV addressing ---------------------------------------------------------------
-// pool[layer][page][k|v][kv_head][token][dim]
-__host__ __device__ __forceinline__ int64_t kv_elem_offset(const cgym_kv_layout& kv, int layer, int page,
-                                                           int which, int head, int token) {
-  int64_t idx = (((static_cast<int64_t>(layer) * kv.n_pages + page) * 2 + which) * kv.n_kv_heads + head);
-  return (idx * kv.page_size + token) * kv.head_dim;
+// pool[layer][page][kv_head] is one contiguous block of 2 * page_size * head_dim elements:
+//   K part   [token][dim]   (row = token, head_dim elements)
+//   V^T part [dim][token]   (row = dim,   page_size elements)
+// so that both are "contraction-contiguous" B operands for the tensor-core attention kernels and a
+// (page, head) block moves with ONE bulk copy. Inside each row the 16-byte chunks are XOR-swizzled
+// by the row index, already in global memory: the block lands in shared memory through a linear
+// bulk copy and fragment loads of 8 consecutive rows at one column hit 8 different bank groups.
+__host__ __device__ __forceinline__ int kv_swizzle(int row, int chunk, int chunks_per_row) {
+  if (chunks_per_row >= 8) return chunk ^ (row & 7);
+  // fewer than 8 chunks per row: 8 / cpr consecutive rows share a 128-byte line
+  const int rows_per_line = 8 / chunks_per_row;  // 2 or 4 (or 8 when cpr == 1: nothing to swizzle)
+  return chunk ^ ((row / rows_per_line) & (chunks_per_row - 1));
 }
+__host__ __device__ __forceinline__ int64_t kv_block_offset(const cgym_kv_layout& kv, int layer, int page, int head) {
+  return ((static_cast<int64_t>(layer) * kv.n_pages + page) * kv.n_kv_heads + head) *
+         (2ll * kv.page_size * kv.head_dim);
+}
+// element index inside a row of `row_elems` elements of `elem_bytes` bytes each
+__host__ __device__ __forceinline__ int kv_row_index(int row, int col, int row_elems, int elem_bytes) {
+  const int per_chunk = 16 / elem_bytes;
+  const int chunk = kv_swizzle(row, col / per_chunk, row_elems / per_chunk);
+  return row * row_elems + chunk * per_chunk + (col % per_chunk);
+}
+__host__ __device__ __forceinline__ int64_t kv_k_offset(const cgym_kv_layout& kv, int layer, int page, int head,
+                                                        int token, int d, int elem_bytes) {
+  return kv_block_offset(kv, layer, page, head) + kv_row_index(token, d, kv.head_dim, elem_bytes);
+}
+__host__ __device__ __forceinline__ int64_t kv_v_offset(const cgym_kv_layout& kv, int layer, int page, int head,
+                                                        int token, int d, int elem_bytes) {
+  return kv_block_offset(kv, layer, page, head) + kv.page_size * kv.head_dim +
+         kv_row_index(d, token, kv.page_size, elem_bytes);
+}
+// scales[layer][page][kv_head][k|v][token]
 __host__ __device__ __forceinline__ int64_t kv_scale_offset(const cgym_kv_layout& kv, int layer, int page,
                                                             int which, int head, int token) {
-  int64_t idx = (((static_cast<int64_t>(layer) * kv.n_pages + page) * 2 + which) * kv.n_kv_heads + head);
+  int64_t idx = (((static_cast<int64_t>(layer) * kv.n_pages + page) * kv.n_kv_heads + head) * 2 + which);
   return idx * kv.page_size + token;
 }
 

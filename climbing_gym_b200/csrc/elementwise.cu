@@ -261,8 +261,8 @@ __global__ void qk_rope_append_kernel(T* __restrict__ q_out, T* __restrict__ k_n
     return;
   }
   KV* pool = static_cast<KV*>(kv.kv_pool);
-  const int64_t ko = kv_elem_offset(kv, layer, page, 0, kh, tok) + d;
-  const int64_t vo = kv_elem_offset(kv, layer, page, 1, kh, tok) + d;
+  const int64_t ko = kv_k_offset(kv, layer, page, kh, tok, d, static_cast<int>(sizeof(KV)));
+  const int64_t vo = kv_v_offset(kv, layer, page, kh, tok, d, static_cast<int>(sizeof(KV)));
   if constexpr (sizeof(KV) == 1) {
     const float ak = block_max(fabsf(rot), scratch);
     const float av = block_max(fabsf(v), scratch);

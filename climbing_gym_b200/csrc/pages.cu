@@ -167,14 +167,16 @@ __global__ void pages_copy_tail_kernel(cgym_page_pool pool, cgym_kv_layout kv, c
   const int sp = pool.block_table[static_cast<int64_t>(src_slots[i]) * pool.max_blocks + block];
   const int dp = pool.block_table[static_cast<int64_t>(dst_slots[i]) * pool.max_blocks + block];
   if (sp < 0 || dp < 0 || sp == dp) return;
-  const int plane = blockIdx.y;  // (layer * 2 + which) * n_kv_heads + head
-  const int head = plane % kv.n_kv_heads, which = (plane / kv.n_kv_heads) & 1, layer = plane / (2 * kv.n_kv_heads);
+  const int plane = blockIdx.y;  // layer * n_kv_heads + head
+  const int head = plane % kv.n_kv_heads, layer = plane / kv.n_kv_heads;
+  // the whole (page, head) block is copied: tokens past `rem` are don't-care in both copies
   KV* pool_data = static_cast<KV*>(kv.kv_pool);
-  const int64_t so = kv_elem_offset(kv, layer, sp, which, head, 0), doff = kv_elem_offset(kv, layer, dp, which, head, 0);
-  for (int j = threadIdx.x; j < rem * kv.head_dim; j += blockDim.x) pool_data[doff + j] = pool_data[so + j];
+  const int64_t so = kv_block_offset(kv, layer, sp, head), doff = kv_block_offset(kv, layer, dp, head);
+  const int block_elems = 2 * kv.page_size * kv.head_dim;
+  for (int j = threadIdx.x; j < block_elems; j += blockDim.x) pool_data[doff + j] = pool_data[so + j];
   if (kv.kv_scales != nullptr) {
-    const int64_t ss = kv_scale_offset(kv, layer, sp, which, head, 0), ds = kv_scale_offset(kv, layer, dp, which, head, 0);
-    for (int j = threadIdx.x; j < rem; j += blockDim.x) kv.kv_scales[ds + j] = kv.kv_scales[ss + j];
+    const int64_t ss = kv_scale_offset(kv, layer, sp, 0, head, 0), ds = kv_scale_offset(kv, layer, dp, 0, head, 0);
+    for (int j = threadIdx.x; j < 2 * kv.page_size; j += blockDim.x) kv.kv_scales[ds + j] = kv.kv_scales[ss + j];
   }
 }
 
@@ -187,7 +189,9 @@ __global__ void gather_kv_dense_kernel(float* __restrict__ out, cgym_kv_layout k
     const int head = j / kv.head_dim, d = j % kv.head_dim;
     float v = 0.0f;
     if (page >= 0) {
-      const int64_t off = kv_elem_offset(kv, layer, page, which, head, tok % kv.page_size) + d;
+      const int eb = static_cast<int>(sizeof(KV));
+      const int64_t off = which == 0 ? kv_k_offset(kv, layer, page, head, tok % kv.page_size, d, eb)
+                                     : kv_v_offset(kv, layer, page, head, tok % kv.page_size, d, eb);
       if constexpr (sizeof(KV) == 1) {
         v = from_e4m3(static_cast<const uint8_t*>(kv.kv_pool)[off]) *
             kv.kv_scales[kv_scale_offset(kv, layer, page, which, head, tok % kv.page_size)];
@@ -196,6 +200,35 @@ __global__ void gather_kv_dense_kernel(float* __restrict__ out, cgym_kv_layout k
       }
     }
     out[static_cast<int64_t>(tok) * width + j] = v;
+  }
+}
+
+// inverse of the gather: rows [start, start + gridDim.x) of one slot from dense fp32 [len][Hkv][D];
+// e4m3 caches quantise per (token, head) exactly like the append kernel. grid (len, Hkv), block D.
+template <typename KV>
+__global__ void scatter_kv_dense_kernel(const float* __restrict__ k, const float* __restrict__ v, cgym_kv_layout kv,
+                                        int layer, int slot, int start) {
+  __shared__ float scratch[32];
+  const int tok = start + blockIdx.x, head = blockIdx.y, d = threadIdx.x;
+  const int page = kv.block_table[static_cast<int64_t>(slot) * kv.max_blocks + tok / kv.page_size];
+  if (page < 0) return;
+  const int64_t src = (static_cast<int64_t>(blockIdx.x) * kv.n_kv_heads + head) * kv.head_dim + d;
+  const float kval = k[src], vval = v[src];
+  const int eb = static_cast<int>(sizeof(KV));
+  const int64_t ko = kv_k_offset(kv, layer, page, head, tok % kv.page_size, d, eb);
+  const int64_t vo = kv_v_offset(kv, layer, page, head, tok % kv.page_size, d, eb);
+  if constexpr (sizeof(KV) == 1) {
+    const float sk = fmaxf(block_max(fabsf(kval), scratch) / 448.0f, 1.0e-12f);
+    const float sv = fmaxf(block_max(fabsf(vval), scratch) / 448.0f, 1.0e-12f);
+    static_cast<uint8_t*>(kv.kv_pool)[ko] = to_e4m3(__fdiv_rn(kval, sk));
+    static_cast<uint8_t*>(kv.kv_pool)[vo] = to_e4m3(__fdiv_rn(vval, sv));
+    if (d == 0) {
+      kv.kv_scales[kv_scale_offset(kv, layer, page, 0, head, tok % kv.page_size)] = sk;
+      kv.kv_scales[kv_scale_offset(kv, layer, page, 1, head, tok % kv.page_size)] = sv;
+    }
+  } else {
+    Elem<KV>::store(static_cast<KV*>(kv.kv_pool) + ko, kval);
+    Elem<KV>::store(static_cast<KV*>(kv.kv_pool) + vo, vval);
   }
 }
 
@@ -255,7 +288,7 @@ extern "C" int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout*
   pages_share_kernel<<<n, 128, 0, as_stream(stream)>>>(*pool, src_slots, dst_slots, prefix_lens);
   pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, dst_slots, prefix_lens, nullptr, nullptr,
                                                                   nullptr, nullptr, n, status);
-  dim3 grid(n, n_layers * 2 * kv->n_kv_heads);
+  dim3 grid(n, n_layers * kv->n_kv_heads);
   if (kv->kv_dtype == CGYM_F32) pages_copy_tail_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);
   else if (kv->kv_dtype == CGYM_BF16) pages_copy_tail_kernel<__nv_bfloat16><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);
   else if (kv->kv_dtype == CGYM_E4M3) pages_copy_tail_kernel<uint8_t><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);
@@ -272,4 +305,17 @@ extern "C" int cgym_gather_kv_dense(float* out, const cgym_kv_layout* kv, int la
   else if (kv->kv_dtype == CGYM_E4M3) gather_kv_dense_kernel<uint8_t><<<length, 128, 0, as_stream(stream)>>>(out, *kv, layer, which, slot);
   else return fail("gather_kv_dense: unsupported kv dtype %d", kv->kv_dtype);
   return check_launch("gather_kv_dense");
+}
+
+extern "C" int cgym_scatter_kv_dense(const float* k, const float* v, const cgym_kv_layout* kv, int layer, int slot,
+                                     int start, int length, cgym_stream_t stream) {
+  CGYM_REQUIRE(kv != nullptr && k != nullptr && v != nullptr && length >= 0 && start >= 0,
+               "scatter_kv_dense: bad arguments");
+  if (length == 0) return 0;
+  dim3 grid(length, kv->n_kv_heads);
+  if (kv->kv_dtype == CGYM_F32) scatter_kv_dense_kernel<float><<<grid, kv->head_dim, 0, as_stream(stream)>>>(k, v, *kv, layer, slot, start);
+  else if (kv->kv_dtype == CGYM_BF16) scatter_kv_dense_kernel<__nv_bfloat16><<<grid, kv->head_dim, 0, as_stream(stream)>>>(k, v, *kv, layer, slot, start);
+  else if (kv->kv_dtype == CGYM_E4M3) scatter_kv_dense_kernel<uint8_t><<<grid, kv->head_dim, 0, as_stream(stream)>>>(k, v, *kv, layer, slot, start);
+  else return fail("scatter_kv_dense: unsupported kv dtype %d", kv->kv_dtype);
+  return check_launch("scatter_kv_dense");
 }

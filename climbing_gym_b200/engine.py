@@ -261,6 +261,10 @@ class LFM25Engine:
         if current:
             chunks.append(current)
         hidden_parts, consumed = [], 0
+        group = self.config.num_attention_heads // self.config.num_key_value_heads
+        use_tiles = (self.dtype == torch.bfloat16 and cache.page_size == 64 and self.config.head_dim == 64
+                     and group <= 16)
+        tile_tokens = max(1, 128 // group)
         for chunk in chunks:
             counts = [piece[1] for piece in chunk]
             rows, n = sum(counts), len(chunk)
@@ -272,31 +276,44 @@ class LFM25Engine:
             seq_slots = np.asarray([piece[0] for piece in chunk], dtype=np.int32)
             seq_starts = np.asarray([piece[2] for piece in chunk], dtype=np.int32)
             seq_ends = seq_starts + np.asarray(counts, dtype=np.int32)
-            meta = np.concatenate([positions, token_slots, positions + 1, cu, seq_slots, seq_starts, seq_ends])
+            # query tiles of the tensor-core prefill attention: <= 128 / group consecutive tokens of one piece
+            tile_fields, n_tiles = [np.zeros(0, np.int32)] * 4, 0
+            if use_tiles:
+                starts_t = [np.arange(0, c, tile_tokens, dtype=np.int32) for c in counts]
+                per_piece = [len(s) for s in starts_t]
+                offs = np.concatenate(starts_t)
+                base = np.repeat(cu[:-1], per_piece)
+                remaining = np.repeat(np.asarray(counts, dtype=np.int32), per_piece) - offs
+                tile_fields = [base + offs, np.minimum(remaining, tile_tokens).astype(np.int32),
+                               np.repeat(seq_slots, per_piece), np.repeat(seq_starts, per_piece) + offs]
+                n_tiles = len(offs)
+            meta = np.concatenate([positions, token_slots, positions + 1, cu, seq_slots, seq_starts, seq_ends,
+                                   *tile_fields]).astype(np.int32)
             meta_dev = torch.from_numpy(meta).to(dev, non_blocking=True)
             tokens_dev = flat_tokens[consumed:consumed + rows]
             consumed += rows
             views, o = [], 0
-            for size in (rows, rows, rows, n + 1, n, n, n):
+            for size in (rows, rows, rows, n + 1, n, n, n, n_tiles, n_tiles, n_tiles, n_tiles):
                 views.append(meta_dev[o:o + size])
                 o += size
-            positions_d, slots_d, kv_lens_d, cu_d, seq_slots_d, seq_starts_d, seq_ends_d = views
+            positions_d, slots_d, kv_lens_d, cu_d, seq_slots_d, seq_starts_d, seq_ends_d = views[:7]
+            tiles = (*views[7:], n_tiles) if use_tiles else None
             cache.reserve(seq_slots_d, seq_ends_d)
             finished = [i for i, piece in enumerate(chunk) if piece[3]]
             if return_hidden:
                 hidden = runner.prefill_chunk(bufs, cache, tokens_dev, positions_d, slots_d, kv_lens_d, cu_d,
-                                              seq_slots_d, seq_starts_d, n, rows, return_hidden=True)
+                                              seq_slots_d, seq_starts_d, n, rows, return_hidden=True, tiles=tiles)
                 hidden_parts.append((chunk, hidden.clone()))
             elif finished and logits is not None:
                 last_rows = torch.from_numpy(cu[1:][finished].astype(np.int64) - 1).to(dev, non_blocking=True)
                 out = torch.empty((len(finished), self.config.vocab_size), device=dev, dtype=self.dtype)
                 runner.prefill_chunk(bufs, cache, tokens_dev, positions_d, slots_d, kv_lens_d, cu_d, seq_slots_d,
-                                     seq_starts_d, n, rows, last_rows=last_rows, logits=out)
+                                     seq_starts_d, n, rows, last_rows=last_rows, logits=out, tiles=tiles)
                 dest = torch.from_numpy(seq_slots[finished].astype(np.int64)).to(dev, non_blocking=True)
                 logits.index_copy_(0, dest, out)
             else:
                 runner.prefill_chunk(bufs, cache, tokens_dev, positions_d, slots_d, kv_lens_d, cu_d, seq_slots_d,
-                                     seq_starts_d, n, rows)
+                                     seq_starts_d, n, rows, tiles=tiles)
             cache.seq_lens.index_copy_(0, seq_slots_d.long(), seq_ends_d)
         return hidden_parts
 

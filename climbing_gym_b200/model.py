@@ -57,6 +57,7 @@ class LFM25Runner:
         self.dt = nv.dtype_code(weights.dtype)
         self.fp8_mlp, self.fp8_lm_head = bool(fp8_mlp), bool(fp8_lm_head)
         self.gemm_impl = gemm_impl
+        self.attn_impl = 0  # 0 auto, 1 CUDA-core kernel, 2 tensor-core kernel (see cgym_paged_attention)
         self.fp8_weights: dict[int, PackedFP8Weight] = {}
         self.scale = float(self.cfg.head_dim ** -0.5)
         if (fp8_mlp or fp8_lm_head) and weights.dtype != torch.bfloat16:
@@ -98,7 +99,8 @@ class LFM25Runner:
 
     # ---- the layer stack ---------------------------------------------------------------------------
     def _layers(self, bufs: ForwardBuffers, cache: PagedHybridCache, rows: int, *, decode: bool,
-                positions, slots, active, kv_lens, cu_seqlens=None, seq_slots=None, seq_starts=None, n_seqs=0):
+                positions, slots, active, kv_lens, cu_seqlens=None, seq_slots=None, seq_starts=None, n_seqs=0,
+                tiles=None):
         """Runs every layer over bufs.embed[:rows]; returns (branch, residual) for the final norm."""
         cfg, dev = self.cfg, self.weights.device
         stream = nv.stream_ptr(dev)
@@ -121,9 +123,16 @@ class LFM25Runner:
                         nv.ptr(a.q_norm_weight), nv.ptr(a.k_norm_weight), nv.ptr(self.rope_cos), nv.ptr(self.rope_sin),
                         nv.ptr(positions), nv.ptr(slots), nv.ptr(active), cache.kv, a.cache_index, rows, hq,
                         float(cfg.norm_eps), self.dt, nv.ptr(status), stream)
-                nv.call("cgym_paged_attention", nv.ptr(bufs.attended), nv.ptr(bufs.q), nv.ptr(kv_lens), nv.ptr(slots),
-                        nv.ptr(active), cache.kv, a.cache_index, rows, hq, self.scale,
-                        bufs.attn_splits if decode else 1, nv.ptr(bufs.attn_ws), self.dt, stream)
+                if tiles is not None:
+                    row0, ntok, tslot, pos0, n_tiles = tiles
+                    nv.call("cgym_prefill_attention", nv.ptr(bufs.attended), nv.ptr(bufs.q), nv.ptr(row0), nv.ptr(ntok),
+                            nv.ptr(tslot), nv.ptr(pos0), cache.kv, a.cache_index, n_tiles, hq, self.scale, self.dt,
+                            nv.ptr(status), stream)
+                else:
+                    nv.call("cgym_paged_attention", nv.ptr(bufs.attended), nv.ptr(bufs.q), nv.ptr(kv_lens),
+                            nv.ptr(slots), nv.ptr(active), cache.kv, a.cache_index, rows, hq, self.scale,
+                            bufs.attn_splits if decode else 1, nv.ptr(bufs.attn_ws), self.dt, self.attn_impl,
+                            nv.ptr(status), stream)
                 self._gemm(bufs.branch, bufs.attended, a.out_weight, rows, bufs, status)
             else:
                 c = layer.conv
@@ -194,7 +203,7 @@ class LFM25Runner:
 
     def prefill_chunk(self, bufs: ForwardBuffers, cache: PagedHybridCache, tokens, positions, token_slots, kv_lens,
                       cu_seqlens, seq_slots, seq_starts, n_seqs: int, rows: int, *, last_rows=None, logits=None,
-                      return_hidden: bool = False):
+                      return_hidden: bool = False, tiles=None):
         """Packed rows of one or more sequences (or chunks of them). Pages must be reserved by the caller.
 
         last_rows (int64 row indices) selects the rows whose logits are wanted (written to ``logits``);
@@ -202,7 +211,8 @@ class LFM25Runner:
         self._embed(bufs, tokens, rows)
         x, residual = self._layers(bufs, cache, rows, decode=False, positions=positions, slots=token_slots,
                                    active=None, kv_lens=kv_lens, cu_seqlens=cu_seqlens, seq_slots=seq_slots,
-                                   seq_starts=seq_starts, n_seqs=n_seqs)
+                                   seq_starts=seq_starts, n_seqs=n_seqs,
+                                   tiles=tiles if self.attn_impl != 1 else None)
         if return_hidden:
             self._rmsnorm(bufs.final, x, self.weights.embedding_norm_weight, rows, residual, bufs.residual)
             return bufs.final[:rows]

@@ -8,8 +8,11 @@ group, and the allocator state (free bitmap, refcounts, block tables) lives on t
 decode graph grows and evicts sequences without a host round-trip.
 
 HBM layout
-  kv_pool     [attn_layers, n_pages, 2 (k|v), kv_heads, page_size, head_dim]  model dtype or e4m3
-  kv_scales   [attn_layers, n_pages, 2, kv_heads, page_size] fp32             (e4m3 only)
+  kv_pool     [attn_layers, n_pages, kv_heads, 2 * page_size * head_dim]  model dtype or e4m3; one
+              (page, head) block is K as [token][dim] followed by V^T as [dim][token], with the
+              16-byte chunks of every row XOR-swizzled by the row index (the layout the attention
+              kernels' shared-memory fragment loads want, so a block moves with one linear copy)
+  kv_scales   [attn_layers, n_pages, kv_heads, 2 (k|v), page_size] fp32   (e4m3 only)
   conv_state  [conv_layers, n_slots, 3, hidden]   tap-major, newest tap last
   block_table [n_slots, max_blocks] int32, n_blocks [n_slots], seq_lens [n_slots]
   free_bitmap [ceil(n_pages/32)] (bit = 1: free), refcount [n_pages], status [1]
@@ -47,10 +50,13 @@ class PagedHybridCache:
         self.n_kv_heads, self.head_dim, self.hidden_size = n_kv_heads, head_dim, hidden_size
         self.fp8_kv = bool(fp8_kv)
         dev = self.device
-        pool_shape = (max(n_attn_layers, 1), self.n_pages, 2, n_kv_heads, page_size, head_dim)
+        if page_size < 16:
+            raise ValueError("page_size must be at least 16 tokens")
+        # one (page, head) block = K [token][dim] then V^T [dim][token], 16-byte chunks swizzled by row
+        pool_shape = (max(n_attn_layers, 1), self.n_pages, n_kv_heads, 2 * page_size * head_dim)
         if fp8_kv:
             self.kv_pool = torch.zeros(pool_shape, device=dev, dtype=torch.uint8)
-            self.kv_scales = torch.zeros(pool_shape[:-1], device=dev, dtype=torch.float32)
+            self.kv_scales = torch.zeros((*pool_shape[:-1], 2, page_size), device=dev, dtype=torch.float32)
             self.kv_dtype = nv.E4M3
         else:
             self.kv_pool = torch.zeros(pool_shape, device=dev, dtype=dtype)
@@ -131,6 +137,13 @@ class PagedHybridCache:
                     nv.stream_ptr(self.device))
             out.append(dense)
         return out[0], out[1]
+
+    def write_dense_kv(self, layer: int, slot: int, start: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Test helper: store fp32 k, v [length, kv_heads, head_dim] at positions [start, start+length)."""
+        k, v = k.contiguous().float(), v.contiguous().float()
+        nv.call("cgym_scatter_kv_dense", nv.ptr(k), nv.ptr(v), self.kv, layer, slot, start, k.size(0),
+                nv.stream_ptr(self.device))
+        torch.cuda.current_stream(self.device).synchronize()  # k, v may be temporaries of the caller
 
     def dense_conv(self, layer: int, slot: int) -> torch.Tensor:
         """Conv taps of one slot in the reference's [hidden, 3] orientation."""

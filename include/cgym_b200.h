@@ -120,11 +120,27 @@ int cgym_qk_norm_rope_append(void* q_out, void* k_new, void* v_new, const void* 
 /* flash_attn_with_kvcache / fp8 decode+combine (lfm25_cuda.py:146-165,
  * lfm25_fp8_kv.py:72-172) and, for prefill rows, causal attention (lfm25_engine.py:1387-1394):
  * row r attends to cache positions [0, kv_lens[r]) of its slot. out [rows, Hq, D].
- * workspace: fp32, >= rows * Hq * n_splits * (D + 2) elements when n_splits > 1. */
+ * workspace: fp32, >= rows * Hq * n_splits * (D + 2) elements when n_splits > 1.
+ * impl: 0 = auto, 1 = CUDA-core kernel (any dtype / head_dim / page size), 2 = tensor-core kernel
+ * with bulk-copy page staging (bf16 activations, bf16 or e4m3 cache, head_dim 64, 64-token pages);
+ * status is required for impl 2 (bounded waits report there). */
 int cgym_paged_attention(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots,
                          const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows,
                          int n_q_heads, float scale, int n_splits, float* workspace, int dtype,
-                         cgym_stream_t stream);
+                         int impl, int32_t* status, cgym_stream_t stream);
+
+/* flash_attn_func on padded prompts (lfm25_engine.py:1387-1389,1415-1417), here on packed rows
+ * against the paged cache: tile i is tile_ntok[i] (<= 128 / group) consecutive query tokens of one
+ * sequence starting at packed row tile_row0[i] and cache position tile_pos0[i] in slot
+ * tile_slot[i]; each token attends causally to cache positions [0, its position]. The tile's K/V
+ * must already be in the cache (cgym_qk_norm_rope_append), which also makes a chunked prompt see
+ * its earlier chunks. Tensor-core kernel: bf16 activations, bf16 or e4m3 cache, head_dim 64,
+ * 64-token pages. q, out: [rows, Hq, D]. */
+int cgym_prefill_attention(void* out, const void* q, const int32_t* tile_row0,
+                           const int32_t* tile_ntok, const int32_t* tile_slot,
+                           const int32_t* tile_pos0, const cgym_kv_layout* kv, int layer,
+                           int n_tiles, int n_q_heads, float scale, int dtype, int32_t* status,
+                           cgym_stream_t stream);
 
 /* F.linear / cuBLAS GEMM and _gemv_kernel (lfm25_cuda_kernels.py:10-29; call sites
  * lfm25_cuda.py:124-126,141,166,170-172,180,192): y[M,N] = x[M,K] . w[N,K]^T, fp32 accumulate.
@@ -227,6 +243,13 @@ int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout* kv, int n_
  * (tests/test_lfm25_adaptive.py:12-60). No reference counterpart as a kernel. */
 int cgym_gather_kv_dense(float* out, const cgym_kv_layout* kv, int layer, int which, int slot,
                          int length, cgym_stream_t stream);
+
+/* Test/debug helper, inverse of the gather: writes dense fp32 k, v [length][Hkv][D] into cache
+ * positions [start, start + length) of one slot (pages must be reserved), quantising e4m3 caches
+ * per (token, head) like the append kernel. No reference counterpart as a kernel (the reference
+ * tests assign into k_cache / v_cache views, tests/test_lfm25_fp8_kv.py:24-90). */
+int cgym_scatter_kv_dense(const float* k, const float* v, const cgym_kv_layout* kv, int layer,
+                          int slot, int start, int length, cgym_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -50,7 +50,8 @@ def test_version_and_argument_validation_without_a_gpu(native):
     with pytest.raises(native.NativeKernelError, match="head_dim"):
         import ctypes as C
         kv = native.KVLayout(None, None, None, 4, 16, 4, 2, 48, native.BF16)
-        native.call("cgym_paged_attention", 1, 1, 1, None, None, C.byref(kv), 0, 1, 4, 1.0, 1, None, native.BF16, None)
+        native.call("cgym_paged_attention", 1, 1, 1, None, None, C.byref(kv), 0, 1, 4, 1.0, 1, None, native.BF16, 0,
+                    None, None)
 
 
 def test_engine_refuses_to_run_without_cuda():

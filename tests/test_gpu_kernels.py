@@ -230,59 +230,101 @@ def attention_reference(q, k, v, scale, ks=None, vs=None, rd=round_bf16):
     return (np.einsum("hgt,thd->hgd", rd(p), v) / total).reshape(hq, -1)
 
 
-@pytest.mark.parametrize("mode", ["f32", "bf16", "e4m3"])
+def fill_cache(cache, lens, hkv, d, rd, fp8, rng):
+    """Random K/V per slot, written through the scatter entry point; returns what the cache now
+    holds per slot as (k, v, k_scales, v_scales) with k/v dequantised codes for e4m3."""
+    stored = []
+    for slot, n in enumerate(lens):
+        k, v = rd(rng.standard_normal((n, hkv, d))), rd(rng.standard_normal((n, hkv, d)))
+        if n:
+            cache.write_dense_kv(0, slot, 0, torch.from_numpy(k).to(cache.device), torch.from_numpy(v).to(cache.device))
+        if fp8:
+            kc, ksc = ok.store_kv_e4m3(k)
+            vc, vsc = ok.store_kv_e4m3(v)
+            stored.append((decode_e4m3(kc), decode_e4m3(vc), ksc, vsc))
+        else:
+            stored.append((k, v, None, None))
+    return stored
+
+
+@pytest.mark.parametrize("mode,impl,page", [("f32", 1, 16), ("bf16", 1, 16), ("e4m3", 1, 16), ("bf16", 1, 64),
+                                            ("bf16", 2, 64), ("e4m3", 2, 64)])
 @pytest.mark.parametrize("splits", [1, 3])
-def test_paged_attention_matches_softmax_reference(dev, mode, splits):
+def test_paged_attention_matches_softmax_reference(dev, mode, impl, page, splits):
     rng = np.random.default_rng(5)
-    hq, hkv, d, page = 8, 2, 64, 16
-    lens = [1, 15, 16, 17, 130, 0]
+    hq, hkv, d = 8, 2, 64
+    lens = [1, 15, 16, 17, 130, 0, 64, 65, 300]
     rows = len(lens)
     dtype = torch.float32 if mode == "f32" else torch.bfloat16
-    cache = make_cache(dev, dtype=dtype, fp8=mode == "e4m3", slots=rows, max_len=256, page=page, hkv=hkv, d=d, layers=1)
+    cache = make_cache(dev, dtype=dtype, fp8=mode == "e4m3", slots=rows, max_len=320, page=page, hkv=hkv, d=d, layers=1)
     rd = (lambda x: np.asarray(x, np.float32)) if mode == "f32" else round_bf16
     slot_ids = torch.arange(rows, device=dev, dtype=torch.int32)
     cache.reserve(slot_ids, torch.tensor([max(n, 1) for n in lens], device=dev, dtype=torch.int32))
-    table = cache.block_table.cpu().numpy()
-    pool = np.zeros(tuple(cache.kv_pool.shape), np.float32)
-    scales = np.ones(tuple(cache.kv_pool.shape[:-1]), np.float32)
-    ks_all, vs_all, k_all, v_all = [], [], [], []
-    for row, n in enumerate(lens):
-        k, v = rd(rng.standard_normal((n, hkv, d))), rd(rng.standard_normal((n, hkv, d)))
-        if mode == "e4m3":
-            kc, ksc = ok.store_kv_e4m3(k)
-            vc, vsc = ok.store_kv_e4m3(v)
-            k, v = decode_e4m3(kc), decode_e4m3(vc)
-            ks_all.append(ksc); vs_all.append(vsc)
-        k_all.append(k); v_all.append(v)
-        for t in range(n):
-            pg = table[row, t // page]
-            pool[0, pg, 0, :, t % page] = k[t]
-            pool[0, pg, 1, :, t % page] = v[t]
-            if mode == "e4m3":
-                scales[0, pg, 0, :, t % page] = ksc[t]
-                scales[0, pg, 1, :, t % page] = vsc[t]
-    if mode == "e4m3":
-        from oracle.numerics import encode_e4m3
-        cache.kv_pool.copy_(torch.from_numpy(encode_e4m3(pool)).to(dev))
-        cache.kv_scales.copy_(torch.from_numpy(scales).to(dev))
-    else:
-        cache.kv_pool.copy_(torch.from_numpy(pool).to(dev).to(dtype))
+    stored = fill_cache(cache, lens, hkv, d, rd, mode == "e4m3", rng)
+    # the gather entry point reads back exactly what was stored (layout round trip)
+    k_back, v_back = cache.dense_kv(0, 4, 130)
+    ks, vs = stored[4][2], stored[4][3]
+    assert np.allclose(f32(k_back), stored[4][0] * (ks[..., None] if ks is not None else 1.0), rtol=1e-6)
+    assert np.allclose(f32(v_back), stored[4][1] * (vs[..., None] if vs is not None else 1.0), rtol=1e-6)
     q_np = rd(rng.standard_normal((rows, hq, d)))
     q = torch.from_numpy(q_np).to(dev).to(dtype)
     out = torch.full((rows, hq, d), 7.0, device=dev, dtype=dtype)
     ws = torch.empty(rows * hq * splits * (d + 2), device=dev, dtype=torch.float32)
     kv_lens = torch.tensor(lens, device=dev, dtype=torch.int32)
     nv.call("cgym_paged_attention", nv.ptr(out), nv.ptr(q), nv.ptr(kv_lens), None, None, cache.kv, 0, rows, hq,
-            d ** -0.5, splits, nv.ptr(ws), nv.F32 if mode == "f32" else nv.BF16, stream())
+            d ** -0.5, splits, nv.ptr(ws), nv.F32 if mode == "f32" else nv.BF16, impl, nv.ptr(cache.status), stream())
     got = f32(out)
+    assert int(cache.status.item()) == 0
     tol = 1e-5 if mode == "f32" else 0.012  # the reference's own fp8-KV decode tolerance
     for row, n in enumerate(lens):
         if n == 0:
             assert np.all(got[row] == 0), "empty history must give zeros"
             continue
-        want = attention_reference(q_np[row], k_all[row], v_all[row], d ** -0.5,
-                                   ks_all[row] if mode == "e4m3" else None, vs_all[row] if mode == "e4m3" else None, rd)
-        assert np.allclose(got[row].reshape(hq, d), want, atol=tol), f"row {row} len {n}: {np.abs(got[row].reshape(hq, d) - want).max()}"
+        k, v, ks, vs = stored[row]
+        want = attention_reference(q_np[row], k, v, d ** -0.5, ks, vs, rd)
+        err = np.abs(got[row].reshape(hq, d) - want).max()
+        assert err <= tol, f"row {row} len {n}: {err}"
+
+
+@pytest.mark.parametrize("mode", ["bf16", "e4m3"])
+@pytest.mark.parametrize("hq,hkv", [(8, 2), (4, 4), (6, 2)])
+def test_prefill_attention_tensor_core_causal_with_prefix(dev, mode, hq, hkv):
+    """Packed query tiles against the paged cache: a fresh prompt, a chunk continuing a cached prefix
+    and a one-token tail, each token attending causally to [0, its position]."""
+    rng = np.random.default_rng(8)
+    d, page, g = 64, 64, hq // hkv
+    tq = 128 // g
+    # (slot, cached prefix length, new tokens)
+    seqs = [(0, 0, 150), (2, 70, 45), (1, 200, 1)]
+    cache = make_cache(dev, fp8=mode == "e4m3", slots=3, max_len=320, page=page, hkv=hkv, d=d, layers=1)
+    totals = {slot: pre + new for slot, pre, new in seqs}
+    cache.reserve(torch.tensor(sorted(totals), device=dev, dtype=torch.int32),
+                  torch.tensor([totals[s] for s in sorted(totals)], device=dev, dtype=torch.int32))
+    stored = fill_cache(cache, [totals[s] for s in range(3)], hkv, d, round_bf16, mode == "e4m3", rng)
+    n_rows = sum(new for _, _, new in seqs)
+    q_np = round_bf16(rng.standard_normal((n_rows, hq, d)))
+    q = bf(q_np, dev)
+    out = torch.full((n_rows, hq, d), 7.0, device=dev, dtype=torch.bfloat16)
+    row0, ntok, tslot, pos0, base = [], [], [], [], 0
+    for slot, pre, new in seqs:
+        for off in range(0, new, tq):
+            row0.append(base + off); ntok.append(min(tq, new - off)); tslot.append(slot); pos0.append(pre + off)
+        base += new
+    meta = [torch.tensor(v, device=dev, dtype=torch.int32) for v in (row0, ntok, tslot, pos0)]
+    nv.call("cgym_prefill_attention", nv.ptr(out), nv.ptr(q), nv.ptr(meta[0]), nv.ptr(meta[1]), nv.ptr(meta[2]),
+            nv.ptr(meta[3]), cache.kv, 0, len(row0), hq, d ** -0.5, nv.BF16, nv.ptr(cache.status), stream())
+    got = f32(out)
+    assert int(cache.status.item()) == 0
+    base = 0
+    for slot, pre, new in seqs:
+        k, v, ks, vs = stored[slot]
+        for t in range(new):
+            n = pre + t + 1
+            want = attention_reference(q_np[base + t], k[:n], v[:n], d ** -0.5, None if ks is None else ks[:n],
+                                       None if vs is None else vs[:n], round_bf16)
+            err = np.abs(got[base + t].reshape(hq, d) - want).max()
+            assert err <= 0.012, f"slot {slot} token {t}: {err}"
+        base += new
 
 
 def test_page_allocator_trace_matches_oracle(dev):
