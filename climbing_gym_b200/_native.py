@@ -69,8 +69,8 @@ SIGNATURES = {
     "cgym_scatter_kv_dense": [_P, _P, C.POINTER(KVLayout), _I, _I, _I, _I, _P],
     "cgym_gemm": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_fp8": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
-    "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P],
-    "cgym_sample": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P, _P],
+    "cgym_sample": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_target_logprobs": [_P, _P, _P, _I, _I, _I, _P],
     "cgym_step_begin": [C.POINTER(PagePool), _P, _P, _P, _P, _P, _I, _P, _P],
     "cgym_pages_reserve": [C.POINTER(PagePool), _P, _P, _I, _P, _P],
@@ -79,7 +79,8 @@ SIGNATURES = {
     "cgym_gather_kv_dense": [_P, C.POINTER(KVLayout), _I, _I, _I, _I, _P],
 }
 PLAIN = {"cgym_last_error": ([], C.c_char_p), "cgym_version": ([], _I), "cgym_device_supported": ([], _I),
-         "cgym_launch_count": ([], C.c_longlong)}
+         "cgym_launch_count": ([], C.c_longlong), "cgym_sample_workspace_bytes": ([_I], C.c_int64),
+         "cgym_set_pdl": ([_I], _I)}
 
 _lib = None
 

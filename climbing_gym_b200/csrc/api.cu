@@ -19,6 +19,7 @@ int fail(const char* fmt, ...) {
 }
 
 std::atomic<long long> g_kernel_launches{0};
+int g_pdl_enabled = 0;
 
 int check_launch(const char* what, int kernels) {
   const cudaError_t rc = cudaGetLastError();
@@ -34,6 +35,12 @@ int check_launch(const char* what, int kernels) {
 extern "C" const char* cgym_last_error(void) { return cgym::error_buffer(); }
 
 extern "C" int cgym_version(void) { return 1; }
+
+extern "C" int cgym_set_pdl(int enabled) {
+  const int previous = cgym::g_pdl_enabled;
+  cgym::g_pdl_enabled = enabled ? 1 : 0;
+  return previous;
+}
 
 extern "C" long long cgym_launch_count(void) {
   return cgym::g_kernel_launches.load(std::memory_order_relaxed);

@@ -278,6 +278,8 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   extern __shared__ __align__(128) uint8_t att_smem[];
   __shared__ __align__(8) uint64_t bars[4][2];
   __shared__ int abort_flag;
+  pdl_wait();     // q, the new K/V row and the block table come from the kernels just before
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int G = n_q_heads / kv.n_kv_heads;
@@ -519,9 +521,10 @@ static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const
   auto kernel = decode_attention_mma_kernel<T, EB, D, 64>;
   static bool configured = false;
   if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
-  kernel<<<dim3(rows, kv->n_kv_heads, n_splits), 128, smem, stream>>>(
-      static_cast<T*>(out), static_cast<const T*>(q), kv_lens, slots, active, *kv, layer, n_q_heads, scale, n_splits,
-      workspace, status);
+  const cudaError_t rc = launch_dependent(kernel, dim3(rows, kv->n_kv_heads, n_splits), dim3(128), smem, stream,
+                                          static_cast<T*>(out), static_cast<const T*>(q), kv_lens, slots, active, *kv,
+                                          layer, n_q_heads, scale, n_splits, workspace, status);
+  CGYM_REQUIRE(rc == cudaSuccess, "paged_attention: launch failed: %s", cudaGetErrorString(rc));
   return 0;
 }
 

@@ -27,6 +27,33 @@ int check_launch(const char* what, int kernels = 1);
 
 inline cudaStream_t as_stream(cgym_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// ---- programmatic dependent launch -------------------------------------------------------
+// The decode step is ~150 short kernels; with programmatic stream serialization a kernel may be
+// scheduled while its predecessor is still running, so its launch latency, prologue (barrier
+// init, TMEM allocation, descriptor fetch) and - for the GEMMs - the first weight tiles overlap
+// the predecessor's tail. Contract: a kernel launched through launch_dependent() calls pdl_wait()
+// before it touches memory a predecessor may write or still read, and pdl_trigger() once it no
+// longer minds the next kernel being scheduled. Both are no-ops for ordinary launches.
+extern int g_pdl_enabled;  // toggled by cgym_set_pdl(); read at launch time on the host
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = g_pdl_enabled ? 1 : 0;
+  return cudaLaunchKernelEx(&config, kernel, static_cast<Params>(args)...);
+}
+
 // ---- element types ---------------------------------------------------------------------
 // load / store convert through fp32; store rounds to nearest even for bf16 (cvt.rn), which is
 // the cast the reference applies at every rounding point.

@@ -16,6 +16,8 @@ namespace cgym {
 template <typename T>
 __global__ void embedding_kernel(T* __restrict__ out, const T* __restrict__ table,
                                  const int64_t* __restrict__ tokens, int hidden, int vocab) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   int64_t tok = tokens[row];
   if (tok < 0 || tok >= vocab) tok = 0;  // padding rows carry arbitrary ids; never index outside the table
@@ -34,6 +36,8 @@ __global__ void rmsnorm_kernel(T* __restrict__ y, uint8_t* __restrict__ q, float
                                float eps) {
   extern __shared__ float row_buf[];  // hidden floats
   __shared__ float scratch[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t base = static_cast<int64_t>(blockIdx.x) * hidden;
   float ss = 0.0f;
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
@@ -80,6 +84,8 @@ __device__ __forceinline__ float swiglu_value(float gate, float up) {
 
 template <typename T>
 __global__ void swiglu_kernel(T* __restrict__ y, const T* __restrict__ gate_up, int ffn) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.y;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= ffn) return;
@@ -93,6 +99,8 @@ __global__ void swiglu_quant_kernel(uint8_t* __restrict__ q, float* __restrict__
                                     const T* __restrict__ gate_up, int ffn) {
   extern __shared__ float row_buf[];
   __shared__ float scratch[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   float amax = 0.0f;
   for (int i = threadIdx.x; i < ffn; i += blockDim.x) {
@@ -130,6 +138,8 @@ template <typename T>
 __global__ void conv_update_kernel(T* __restrict__ y, T* __restrict__ state, const T* __restrict__ bcx,
                                    const T* __restrict__ conv_w, const uint8_t* __restrict__ active,
                                    const int32_t* __restrict__ slots, int hidden) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.y;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= hidden) return;
@@ -225,6 +235,8 @@ __global__ void qk_rope_append_kernel(T* __restrict__ q_out, T* __restrict__ k_n
                                       cgym_kv_layout kv, int layer, int n_q_heads, float eps, int32_t* status) {
   __shared__ float buf[256];
   __shared__ float scratch[32];
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x, head = blockIdx.y, d = threadIdx.x, D = kv.head_dim, half = D >> 1;
   const int n_kv = kv.n_kv_heads;
   const int width = (n_q_heads + 2 * n_kv) * D;
@@ -309,8 +321,8 @@ extern "C" int cgym_embedding(void* out, const void* table, const int64_t* token
                               int vocab, int dtype, cgym_stream_t stream) {
   CGYM_REQUIRE(rows >= 0 && hidden > 0 && vocab > 0, "embedding: bad shape");
   if (rows == 0) return 0;
-  DISPATCH_DTYPE(dtype, embedding_kernel<T><<<rows, 256, 0, as_stream(stream)>>>(
-      static_cast<T*>(out), static_cast<const T*>(table), tokens, hidden, vocab));
+  DISPATCH_DTYPE(dtype, launch_dependent(embedding_kernel<T>, dim3(rows), dim3(256), 0, as_stream(stream),
+                                         static_cast<T*>(out), static_cast<const T*>(table), tokens, hidden, vocab));
   return check_launch("embedding");
 }
 
@@ -319,9 +331,10 @@ extern "C" int cgym_rmsnorm(void* y, void* sum_out, const void* x, const void* r
   CGYM_REQUIRE(rows >= 0 && hidden > 0 && hidden <= 12288, "rmsnorm: hidden must be in [1, 12288]");
   CGYM_REQUIRE(residual == nullptr || sum_out != nullptr, "rmsnorm: residual needs sum_out");
   if (rows == 0) return 0;
-  DISPATCH_DTYPE(dtype, (rmsnorm_kernel<T, false><<<rows, 256, hidden * sizeof(float), as_stream(stream)>>>(
-      static_cast<T*>(y), nullptr, nullptr, static_cast<T*>(sum_out), static_cast<const T*>(x),
-      static_cast<const T*>(residual), static_cast<const T*>(w), hidden, eps)));
+  DISPATCH_DTYPE(dtype, (launch_dependent(rmsnorm_kernel<T, false>, dim3(rows), dim3(256), hidden * sizeof(float),
+                                          as_stream(stream), static_cast<T*>(y), nullptr, nullptr,
+                                          static_cast<T*>(sum_out), static_cast<const T*>(x),
+                                          static_cast<const T*>(residual), static_cast<const T*>(w), hidden, eps)));
   return check_launch("rmsnorm");
 }
 
@@ -331,9 +344,9 @@ extern "C" int cgym_rmsnorm_quant(uint8_t* q, float* scales, void* sum_out, cons
   CGYM_REQUIRE(residual == nullptr || sum_out != nullptr, "rmsnorm_quant: residual needs sum_out");
   if (rows == 0) return 0;
   using T = __nv_bfloat16;
-  rmsnorm_kernel<T, true><<<rows, 256, hidden * sizeof(float), as_stream(stream)>>>(
-      nullptr, q, scales, static_cast<T*>(sum_out), static_cast<const T*>(x), static_cast<const T*>(residual),
-      static_cast<const T*>(w), hidden, eps);
+  launch_dependent(rmsnorm_kernel<T, true>, dim3(rows), dim3(256), hidden * sizeof(float), as_stream(stream), nullptr,
+                   q, scales, static_cast<T*>(sum_out), static_cast<const T*>(x), static_cast<const T*>(residual),
+                   static_cast<const T*>(w), hidden, eps);
   return check_launch("rmsnorm_quant");
 }
 
@@ -341,8 +354,8 @@ extern "C" int cgym_swiglu(void* y, const void* gate_up, int rows, int ffn, int 
   CGYM_REQUIRE(rows >= 0 && ffn > 0, "swiglu: bad shape");
   if (rows == 0) return 0;
   dim3 grid((ffn + 255) / 256, rows);
-  DISPATCH_DTYPE(dtype, swiglu_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(
-      static_cast<T*>(y), static_cast<const T*>(gate_up), ffn));
+  DISPATCH_DTYPE(dtype, launch_dependent(swiglu_kernel<T>, grid, dim3(256), 0, as_stream(stream), static_cast<T*>(y),
+                                         static_cast<const T*>(gate_up), ffn));
   return check_launch("swiglu");
 }
 
@@ -351,8 +364,8 @@ extern "C" int cgym_swiglu_quant(uint8_t* q, float* scales, const void* gate_up,
   CGYM_REQUIRE(rows >= 0 && ffn > 0 && ffn <= 12288, "swiglu_quant: ffn must be in [1, 12288]");
   if (rows == 0) return 0;
   using T = __nv_bfloat16;
-  swiglu_quant_kernel<T><<<rows, 512, ffn * sizeof(float), as_stream(stream)>>>(
-      q, scales, static_cast<const T*>(gate_up), ffn);
+  launch_dependent(swiglu_quant_kernel<T>, dim3(rows), dim3(512), ffn * sizeof(float), as_stream(stream), q, scales,
+                   static_cast<const T*>(gate_up), ffn);
   return check_launch("swiglu_quant");
 }
 
@@ -370,9 +383,9 @@ extern "C" int cgym_conv_update(void* y, void* state, const void* bcx, const voi
   CGYM_REQUIRE(rows >= 0 && hidden > 0, "conv_update: bad shape");
   if (rows == 0) return 0;
   dim3 grid((hidden + 255) / 256, rows);
-  DISPATCH_DTYPE(dtype, conv_update_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(
-      static_cast<T*>(y), static_cast<T*>(state), static_cast<const T*>(bcx), static_cast<const T*>(conv_w),
-      active, slots, hidden));
+  DISPATCH_DTYPE(dtype, launch_dependent(conv_update_kernel<T>, grid, dim3(256), 0, as_stream(stream),
+                                         static_cast<T*>(y), static_cast<T*>(state), static_cast<const T*>(bcx),
+                                         static_cast<const T*>(conv_w), active, slots, hidden));
   return check_launch("conv_update");
 }
 
@@ -410,10 +423,10 @@ extern "C" int cgym_qk_norm_rope_append(void* q_out, void* k_new, void* v_new, c
   CGYM_REQUIRE(n_q_heads + kv->n_kv_heads <= 65535, "too many heads");
   dim3 grid(rows, n_q_heads + kv->n_kv_heads);
 #define LAUNCH_QK(T, KV)                                                                                   \
-  qk_rope_append_kernel<T, KV><<<grid, D, 0, as_stream(stream)>>>(                                         \
-      static_cast<T*>(q_out), static_cast<T*>(k_new), static_cast<T*>(v_new), static_cast<const T*>(qkv), \
-      static_cast<const T*>(q_norm_w), static_cast<const T*>(k_norm_w), rope_cos, rope_sin, positions,    \
-      slots, active, *kv, layer, n_q_heads, eps, status)
+  launch_dependent(qk_rope_append_kernel<T, KV>, grid, dim3(D), 0, as_stream(stream), static_cast<T*>(q_out),     \
+                   static_cast<T*>(k_new), static_cast<T*>(v_new), static_cast<const T*>(qkv),                   \
+                   static_cast<const T*>(q_norm_w), static_cast<const T*>(k_norm_w), rope_cos, rope_sin,         \
+                   positions, slots, active, *kv, layer, n_q_heads, eps, status)
   if (dtype == CGYM_F32 && kv->kv_dtype == CGYM_F32) LAUNCH_QK(float, float);
   else if (dtype == CGYM_BF16 && kv->kv_dtype == CGYM_BF16) LAUNCH_QK(__nv_bfloat16, __nv_bfloat16);
   else if (dtype == CGYM_BF16 && kv->kv_dtype == CGYM_E4M3) LAUNCH_QK(__nv_bfloat16, uint8_t);

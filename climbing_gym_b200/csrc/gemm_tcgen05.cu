@@ -10,12 +10,14 @@
 // accumulator back with tcgen05.ld and write y (coalesced along N), applying scales / row mask.
 // Warp roles: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = epilogue.
 //
-// Split-K (grid.z) writes fp32 partials to a caller workspace that a second kernel sums in split
-// order, so results are deterministic. Every mbarrier wait is bounded (about two seconds of
+// Split-K (grid.z <= 8) runs as a thread-block cluster: each CTA parks its fp32 partial tile in its
+// own shared memory and the cluster sums the partials in split order through distributed shared
+// memory, so results are deterministic and no workspace or second launch is needed. Every mbarrier wait is bounded (about two seconds of
 // %globaltimer): on expiry the CTA raises CGYM_STATUS_WAIT_TIMEOUT, drains its own TMA copies with
 // the same bound, frees its TMEM and returns.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -117,14 +119,51 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 
 struct GemmEpilogue {
-  void* y;                 // bf16 [M, N] (direct) or fp32 [splits, M, N] (partials)
+  __nv_bfloat16* y;        // bf16 [M, N]
   const float* x_scales;   // per token, fp8 only
   const float* w_scales;   // per output feature, fp8 only
   const uint8_t* row_mask; // optional
   int32_t* status;
   int M, N, K;
-  int partial;             // 1: write fp32 partials
+  int partial;             // 1: split-K over a cluster of gridDim.z CTAs, reduced through DSMEM
 };
+
+// Cluster split-K reduction for one output feature (column of the parked [UN][128] fp32 tiles):
+// CTA `rank` owns token rows ml = rank, rank + SPLITS, ... and sums the SPLITS peers' values in split
+// order. All remote (distributed shared memory) loads of a batch are issued before the first add, so
+// a thread waits for about one remote round trip per 64 values.
+template <int SPLITS, int UN>
+__device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint32_t column, uint32_t rank, int m0,
+                                                    int n, float ws) {
+  constexpr int ROWS = UN / SPLITS;                      // rows this CTA reduces
+  constexpr int BATCH = ROWS * SPLITS <= 64 ? ROWS : 64 / SPLITS;
+  uint32_t peer[SPLITS];
+#pragma unroll
+  for (int sp = 0; sp < SPLITS; ++sp)
+    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer[sp]) : "r"(column), "r"(sp));
+#pragma unroll 1
+  for (int first = 0; first < ROWS; first += BATCH) {
+    float value[BATCH][SPLITS];
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      const uint32_t ml = rank + static_cast<uint32_t>(first + b) * SPLITS;
+#pragma unroll
+      for (int sp = 0; sp < SPLITS; ++sp)
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(value[b][sp]) : "r"(peer[sp] + ml * (UM * 4u)));
+    }
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      const int m = m0 + static_cast<int>(rank) + (first + b) * SPLITS;
+      if (m >= ep.M) continue;
+      if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
+      float total = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < SPLITS; ++sp) total = __fadd_rn(total, value[b][sp]);
+      if (ep.x_scales != nullptr) total = __fmul_rn(__fmul_rn(total, ep.x_scales[m]), ws);
+      ep.y[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(total);
+    }
+  }
+}
 
 template <int UN, bool FP8>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
@@ -141,6 +180,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
+  pdl_trigger();  // the next kernel may be scheduled now; it waits for this grid before touching y
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t tiles = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int n0 = blockIdx.x * UM, m0 = blockIdx.y * UN;
@@ -173,7 +213,21 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
     int issued = 0;
-    for (int i = 0; i < n_kb; ++i) {
+    // Weights never depend on the previous kernel: fill the ring with weight tiles right away, and
+    // only then wait for the kernel that produces the activations (programmatic dependent launch).
+    const int prefetch = n_kb < STAGES ? n_kb : STAGES;
+    for (int i = 0; i < prefetch; ++i) {
+      const uint32_t full = smem_u32(&bar_full[i]);
+      mbar_expect_tx(full, STAGE_BYTES);
+      tma_load_2d(tiles + i * STAGE_BYTES, &tmap_w, full, (kb_begin + i) * ELEMS_PER_SLICE, n0);
+    }
+    pdl_wait();
+    for (int i = 0; i < prefetch; ++i) {
+      tma_load_2d(tiles + i * STAGE_BYTES + UM * SLICE_BYTES, &tmap_x, smem_u32(&bar_full[i]),
+                  (kb_begin + i) * ELEMS_PER_SLICE, m0);
+      issued = i + 1;
+    }
+    for (int i = prefetch; i < n_kb; ++i) {
       const int s = i % STAGES;
       const uint32_t parity = ((i / STAGES) & 1) ^ 1;
       if (!mbar_wait(smem_u32(&bar_empty[s]), parity, &abort_flag)) break;
@@ -213,38 +267,63 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   } else if (warp >= 2) {
     // ---- epilogue: TMEM lane = output feature, column = token ----
     const int quarter = warp & 3;  // a warp may only touch TMEM lanes [32 * (warp % 4), +32)
-    const int n = n0 + quarter * 32 + lane;
-    bool ready = true;
-    if (n_kb > 0) ready = mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
+    const int n_local = quarter * 32 + lane, n = n0 + n_local;
+    pdl_wait();  // scales / row mask come from earlier kernels of the step
+    if (n_kb > 0) mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps agree on abort_flag
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ready) {
+    if (abort_flag == 0 || ep.partial) {
       const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
+      float* part = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)));  // [UN][128], ring is idle now
 #pragma unroll 1
       for (int c = 0; c < UN / 32; ++c) {
         uint32_t v[32];
-        if (n_kb > 0) {
+        if (n_kb > 0 && abort_flag == 0) {
           tmem_load32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, v);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0u;
         }
-        if (n < ep.N) {
+        if (ep.partial) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) part[(c * 32 + j) * UM + n_local] = __uint_as_float(v[j]);
+        } else if (n < ep.N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = m0 + c * 32 + j;
             if (m >= ep.M) break;
+            if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
             float f = __uint_as_float(v[j]);
-            if (ep.partial) {
-              static_cast<float*>(ep.y)[(static_cast<int64_t>(blockIdx.z) * ep.M + m) * ep.N + n] = f;
-            } else {
-              if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
-              if (ep.x_scales != nullptr) f = __fmul_rn(__fmul_rn(f, ep.x_scales[m]), ws);
-              static_cast<__nv_bfloat16*>(ep.y)[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(f);
-            }
+            if (ep.x_scales != nullptr) f = __fmul_rn(__fmul_rn(f, ep.x_scales[m]), ws);
+            ep.y[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(f);
           }
         }
       }
     }
+  }
+
+  if (ep.partial) {
+    // Split-K across a thread-block cluster (one CTA per K range, cluster = grid.z): every CTA has
+    // parked its fp32 partial tile in its own shared memory; after a cluster barrier CTA r sums, in
+    // split order, the token rows m with m % splits == r straight out of its peers' shared memory
+    // (distributed shared memory), applies scales / mask and writes y. Deterministic, no HBM round trip.
+    __syncwarp();  // the producer / MMA lanes rejoin their warps before the aligned cluster barrier
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (warp >= 2) {
+      const int quarter = warp & 3;
+      const int n_local = quarter * 32 + lane, n = n0 + n_local;
+      const uint32_t splits = gridDim.z, rank = blockIdx.z;
+      const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
+      if (n < ep.N) {
+        const uint32_t column = tiles + static_cast<uint32_t>(n_local) * 4u;
+        if (splits == 2) cluster_reduce_rows<2, UN>(ep, column, rank, m0, n, ws);
+        else if (splits == 4) cluster_reduce_rows<4, UN>(ep, column, rank, m0, n, ws);
+        else cluster_reduce_rows<8, UN>(ep, column, rank, m0, n, ws);
+      }
+    }
+    // nobody leaves (and frees its shared memory) while a peer may still be reading it
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -254,20 +333,6 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_acc), "r"(TMEM_COLS) : "memory");
   }
-}
-
-// sums split-K partials in split order, then scales / masks / converts
-__global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ y, const float* __restrict__ partials,
-                                     const float* __restrict__ x_scales, const float* __restrict__ w_scales,
-                                     const uint8_t* __restrict__ row_mask, int M, int N, int splits) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<int64_t>(M) * N) return;
-  const int m = static_cast<int>(idx / N), n = static_cast<int>(idx % N);
-  if (row_mask != nullptr && !row_mask[m]) return;
-  float total = 0.0f;
-  for (int s = 0; s < splits; ++s) total = __fadd_rn(total, partials[static_cast<int64_t>(s) * M * N + idx]);
-  if (x_scales != nullptr) total = __fmul_rn(__fmul_rn(total, x_scales[m]), w_scales[n]);
-  y[idx] = __float2bfloat16_rn(total);
 }
 
 // ---- host side -------------------------------------------------------------------------------
@@ -309,6 +374,7 @@ static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
   constexpr int STAGE_BYTES = (UM + UN) * SLICE_BYTES;
   constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
   constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static_assert(UN * UM * 4 <= STAGES * STAGE_BYTES, "the split-K partial tile must fit in the idle ring");
   static bool configured = false;  // per instantiation; the attribute is per function, set once
   if (!configured) {
     const cudaError_t rc = cudaFuncSetAttribute(gemm_tcgen05_kernel<UN, FP8>,
@@ -316,7 +382,29 @@ static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
     CGYM_REQUIRE(rc == cudaSuccess, "gemm: cannot reserve %d bytes of shared memory: %s", SMEM, cudaGetErrorString(rc));
     configured = true;
   }
-  gemm_tcgen05_kernel<UN, FP8><<<grid, GEMM_THREADS, SMEM, stream>>>(mw, mx, ep);
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = dim3(GEMM_THREADS);
+  config.dynamicSmemBytes = SMEM;
+  config.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n_attrs = 0;
+  if (g_pdl_enabled) {
+    attrs[n_attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n_attrs].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attrs;
+  }
+  if (grid.z > 1) {  // the K splits of one output tile form a cluster
+    attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;
+    attrs[n_attrs].val.clusterDim.x = 1;
+    attrs[n_attrs].val.clusterDim.y = 1;
+    attrs[n_attrs].val.clusterDim.z = grid.z;
+    ++n_attrs;
+  }
+  config.attrs = attrs;
+  config.numAttrs = n_attrs;
+  const cudaError_t rc = cudaLaunchKernelEx(&config, gemm_tcgen05_kernel<UN, FP8>, mw, mx, ep);
+  CGYM_REQUIRE(rc == cudaSuccess, "gemm(tcgen05): launch failed: %s", cudaGetErrorString(rc));
   return 0;
 }
 
@@ -337,24 +425,30 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   const int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
   const int n_tiles = (N + UM - 1) / UM, m_tiles = (M + un - 1) / un;
   const int total_kb = (K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
+  // split-K only where the output tiles alone cannot fill the GPU; at most 8 (portable cluster size)
   int splits = 1;
   if (force_splits > 0) {
     splits = force_splits;
-  } else if (workspace != nullptr && n_tiles * m_tiles <= 74 && total_kb >= 8) {
+  } else if (n_tiles * m_tiles <= 32 && total_kb >= 16) {
     splits = 148 / (n_tiles * m_tiles);
-    if (splits > total_kb / 4) splits = total_kb / 4;  // at least four K slices per split
+    if (splits > total_kb / 8) splits = total_kb / 8;  // at least eight K slices (1 KB of each row) per split
   }
+  if (const char* forced = std::getenv("CGYM_GEMM_SPLITS")) {  // tuning aid: force a split count (1 = off)
+    const int v = std::atoi(forced);
+    if (v >= 1) splits = v;
+  }
+  if (splits > 8) splits = 8;
   if (splits > total_kb) splits = total_kb;
-  if (splits < 1) splits = 1;
-  while (splits > 1 && static_cast<int64_t>(splits) * M * N * 4 > workspace_bytes) --splits;
+  splits = splits >= 8 ? 8 : (splits >= 4 ? 4 : (splits >= 2 ? 2 : 1));  // cluster sizes the reduction is built for
   // every split must own at least one K slice
-  while (splits > 1 && (splits - 1) * ((total_kb + splits - 1) / splits) >= total_kb) --splits;
-  CGYM_REQUIRE(splits == 1 || workspace != nullptr, "gemm(tcgen05): split-K needs a workspace");
+  while (splits > 1 && (splits - 1) * ((total_kb + splits - 1) / splits) >= total_kb) splits /= 2;
+  (void)workspace;
+  (void)workspace_bytes;
 
   CUtensorMap mw, mx;
   if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
   if (int rc = make_map(&mx, x, M, K, un, fp8)) return rc;
-  GemmEpilogue ep{splits > 1 ? workspace : y, x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0};
+  GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0};
   dim3 grid(n_tiles, m_tiles, splits);
   int rc = 0;
 #define LAUNCH_UN(U)                                                              \
@@ -365,13 +459,7 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   else LAUNCH_UN(256);
 #undef LAUNCH_UN
   if (rc) return rc;
-  if (splits > 1) {
-    const int64_t total = static_cast<int64_t>(M) * N;
-    splitk_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        static_cast<__nv_bfloat16*>(y), static_cast<const float*>(workspace), x_scales, w_scales, row_mask, M, N,
-        splits);
-  }
-  return check_launch("gemm_tcgen05", splits > 1 ? 2 : 1);
+  return check_launch("gemm_tcgen05");
 }
 
 }  // namespace cgym

@@ -1,16 +1,22 @@
 // Fused sampler: Gumbel-max / greedy draw, sampled-token log-prob from the untempered logits and
-// (optionally) the slot scheduler's per-row bookkeeping, one CTA per row, one pass over the row.
+// (optionally) the slot scheduler's per-row bookkeeping, in one launch and one pass over the logits.
 //
 // Uniforms are Philox-4x32-10 (Salmon et al., SC'11) keyed per row with
 // key = (seed + position * 0x9E3779B97F4A7C15) & (2^63 - 1), counter (offset + column, 0, 0, 0),
 // first output word, mapped to [0,1) by folding the sign of its int32 view and scaling by 2^-31:
 // the stream the reference sampler consumes, so a row's draws do not depend on which slot or
 // batch it occupies. Ties resolve to the lowest token id.
+//
+// Grid (rows, parts): each CTA reduces one slice of a row's vocabulary (the work is Philox-bound,
+// so a row is spread over several SMs); with parts > 1 the CTA that arrives last at the row's
+// counter combines the slices in slice order (deterministic) and does the bookkeeping. The
+// workspace holds 4 floats per (row, part) plus one counter per row, zero between launches.
 #include "common.cuh"
 
 namespace cgym {
 
-constexpr int SAMPLE_THREADS = 1024;
+constexpr int SAMPLE_THREADS = 512;
+constexpr int SAMPLE_MAX_PARTS = 16;
 
 __device__ __forceinline__ uint32_t philox_first_word(uint32_t c0, uint32_t k0, uint32_t k1) {
   uint32_t c1 = 0, c2 = 0, c3 = 0;
@@ -34,13 +40,29 @@ __device__ __forceinline__ float uniform_from_word(uint32_t w) {
   return static_cast<float>(x) * 4.6566127342e-10f;
 }
 
-struct Best {
+struct Pick {
   float score;
   int index;
+  float mx;  // running maximum of the raw logits
+  float sm;  // sum of exp(logit - mx)
 };
-__device__ __forceinline__ Best better(Best a, Best b) {
-  if (b.score > a.score || (b.score == a.score && b.index < a.index)) return b;
-  return a;
+
+__device__ __forceinline__ Pick combine(Pick a, Pick b) {
+  Pick r = a;
+  if (b.score > a.score || (b.score == a.score && b.index < a.index)) { r.score = b.score; r.index = b.index; }
+  const float nm = fmaxf(a.mx, b.mx);
+  r.sm = (a.mx == -INFINITY ? 0.0f : a.sm * expf(a.mx - nm)) + (b.mx == -INFINITY ? 0.0f : b.sm * expf(b.mx - nm));
+  r.mx = nm;
+  return r;
+}
+
+__device__ __forceinline__ Pick shuffle_xor(Pick p, int o) {
+  Pick q;
+  q.score = __shfl_xor_sync(0xffffffffu, p.score, o);
+  q.index = __shfl_xor_sync(0xffffffffu, p.index, o);
+  q.mx = __shfl_xor_sync(0xffffffffu, p.mx, o);
+  q.sm = __shfl_xor_sync(0xffffffffu, p.sm, o);
+  return q;
 }
 
 template <typename T>
@@ -49,12 +71,14 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
               const uint8_t* __restrict__ advance, const int64_t* __restrict__ seeds,
               const int64_t* __restrict__ steps, const float* __restrict__ temperatures,
               const int64_t* __restrict__ rng_offsets, int64_t* __restrict__ sampled_out,
-              float* __restrict__ logp_out, int vocab) {
-  __shared__ float s_score[32], s_max[32], s_sum[32];
-  __shared__ int s_index[32];
-  const int row = blockIdx.x;
+              float* __restrict__ logp_out, int vocab, float* __restrict__ workspace) {
+  __shared__ Pick s_pick[SAMPLE_THREADS / 32];
+  __shared__ int s_last;
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x, part = blockIdx.y, parts = gridDim.y;
   if (has_state) {
-    if (threadIdx.x == 0 && advance != nullptr && advance[row]) st.seq_lens[row] += 1;
+    if (threadIdx.x == 0 && part == 0 && advance != nullptr && advance[row]) st.seq_lens[row] += 1;
     if (!st.alive[row]) return;
   }
   const float temperature = temperatures[row];
@@ -63,61 +87,69 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
   const uint32_t k0 = static_cast<uint32_t>(key), k1 = static_cast<uint32_t>(key >> 32);
   const uint32_t base = rng_offsets != nullptr ? static_cast<uint32_t>(rng_offsets[row]) : 0u;
   const T* x = logits + static_cast<int64_t>(row) * vocab;
-  const float inv_t = temperature > 0.0f ? 1.0f / fmaxf(temperature, 1.0e-30f) : 1.0f;
+  const int chunk = (vocab + parts - 1) / parts;
+  const int begin = part * chunk, end = min(vocab, begin + chunk);
 
-  Best best{-INFINITY, 0x7fffffff};
-  float mx = -INFINITY, sm = 0.0f;
-  for (int i = threadIdx.x; i < vocab; i += SAMPLE_THREADS) {
+  Pick mine{-INFINITY, 0x7fffffff, -INFINITY, 0.0f};
+  for (int i = begin + threadIdx.x; i < end; i += SAMPLE_THREADS) {
     const float v = Elem<T>::load(x + i);
-    if (v > mx) {
-      sm = (mx == -INFINITY ? 0.0f : sm * expf(mx - v)) + 1.0f;
-      mx = v;
+    if (v > mine.mx) {
+      mine.sm = (mine.mx == -INFINITY ? 0.0f : mine.sm * expf(mine.mx - v)) + 1.0f;
+      mine.mx = v;
     } else if (v > -INFINITY) {
-      sm += expf(v - mx);
+      mine.sm += expf(v - mine.mx);
     }
     float score = v;
     if (temperature > 0.0f) {
       const float u = fmaxf(uniform_from_word(philox_first_word(base + static_cast<uint32_t>(i), k0, k1)), 1.0e-30f);
       score = __fdiv_rn(v, fmaxf(temperature, 1.0e-30f)) - logf(-logf(u));
     }
-    best = better(best, Best{score, i});
+    if (score > mine.score || (score == mine.score && i < mine.index)) { mine.score = score; mine.index = i; }
   }
-  (void)inv_t;
-  // warp then block reduction
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Best other{__shfl_xor_sync(0xffffffffu, best.score, o), __shfl_xor_sync(0xffffffffu, best.index, o)};
-    best = better(best, other);
-    const float omx = __shfl_xor_sync(0xffffffffu, mx, o), osm = __shfl_xor_sync(0xffffffffu, sm, o);
-    const float nm = fmaxf(mx, omx);
-    sm = (mx == -INFINITY ? 0.0f : sm * expf(mx - nm)) + (omx == -INFINITY ? 0.0f : osm * expf(omx - nm));
-    mx = nm;
-  }
+  for (int o = 16; o > 0; o >>= 1) mine = combine(mine, shuffle_xor(mine, o));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) { s_score[warp] = best.score; s_index[warp] = best.index; s_max[warp] = mx; s_sum[warp] = sm; }
+  if (lane == 0) s_pick[warp] = mine;
   __syncthreads();
   if (warp != 0) return;
-  best = Best{s_score[lane], s_index[lane]};
-  mx = s_max[lane];
-  sm = s_sum[lane];
+  mine = lane < SAMPLE_THREADS / 32 ? s_pick[lane] : Pick{-INFINITY, 0x7fffffff, -INFINITY, 0.0f};
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Best other{__shfl_xor_sync(0xffffffffu, best.score, o), __shfl_xor_sync(0xffffffffu, best.index, o)};
-    best = better(best, other);
-    const float omx = __shfl_xor_sync(0xffffffffu, mx, o), osm = __shfl_xor_sync(0xffffffffu, sm, o);
-    const float nm = fmaxf(mx, omx);
-    sm = (mx == -INFINITY ? 0.0f : sm * expf(mx - nm)) + (omx == -INFINITY ? 0.0f : osm * expf(omx - nm));
-    mx = nm;
+  for (int o = 16; o > 0; o >>= 1) mine = combine(mine, shuffle_xor(mine, o));
+
+  if (parts > 1) {
+    // publish this slice; the last CTA to arrive folds all slices in slice order
+    float* slot = workspace + (static_cast<int64_t>(row) * SAMPLE_MAX_PARTS + part) * 4;
+    int* counter = reinterpret_cast<int*>(workspace + static_cast<int64_t>(gridDim.x) * SAMPLE_MAX_PARTS * 4) + row;
+    if (lane == 0) {
+      slot[0] = mine.score;
+      slot[1] = __int_as_float(mine.index);
+      slot[2] = mine.mx;
+      slot[3] = mine.sm;
+      __threadfence();
+      const int arrived = atomicAdd(counter, 1);
+      s_last = arrived == parts - 1;
+      if (s_last) *counter = 0;
+    }
+    __syncwarp();
+    if (!s_last) return;
+    __threadfence();
+    if (lane == 0) {
+      const float* all = workspace + static_cast<int64_t>(row) * SAMPLE_MAX_PARTS * 4;
+      mine = Pick{__ldcg(all), __float_as_int(__ldcg(all + 1)), __ldcg(all + 2), __ldcg(all + 3)};
+      for (int p = 1; p < parts; ++p)
+        mine = combine(mine, Pick{__ldcg(all + 4 * p), __float_as_int(__ldcg(all + 4 * p + 1)), __ldcg(all + 4 * p + 2),
+                                  __ldcg(all + 4 * p + 3)});
+    }
   }
   if (lane != 0) return;
 
-  int token = best.index < vocab ? best.index : 0;
+  int token = mine.index < vocab ? mine.index : 0;
   int length = 0;
   if (has_state) {
     length = st.lengths[row];
     if (st.force_eos_at != nullptr && st.force_eos_at[row] == length) token = st.eos_token_id;
   }
-  const float logp = Elem<T>::load(x + token) - (mx + logf(sm));
+  const float logp = Elem<T>::load(x + token) - (mine.mx + logf(mine.sm));
   if (sampled_out != nullptr) sampled_out[row] = token;
   if (logp_out != nullptr) logp_out[row] = logp;
   if (!has_state) return;
@@ -144,25 +176,40 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
   st.input_tokens[row] = token;
 }
 
+static int pick_parts(int rows, int vocab, const float* workspace) {
+  if (workspace == nullptr || vocab < 8192) return 1;
+  int parts = (2 * 148 + rows - 1) / rows;  // about two CTAs per SM in flight
+  const int by_vocab = vocab / 4096;
+  if (parts > by_vocab) parts = by_vocab;
+  if (parts > SAMPLE_MAX_PARTS) parts = SAMPLE_MAX_PARTS;
+  return parts < 1 ? 1 : parts;
+}
+
 }  // namespace cgym
 
 using namespace cgym;
 
+extern "C" int64_t cgym_sample_workspace_bytes(int rows) {
+  return (static_cast<int64_t>(rows) * SAMPLE_MAX_PARTS * 4 + rows) * 4;
+}
+
 extern "C" int cgym_sample_record(const void* logits, const cgym_slot_state* state, const uint8_t* advance,
                                   int64_t* sampled_out, float* logp_out, int n_slots, int vocab, int dtype,
-                                  cgym_stream_t stream) {
+                                  float* workspace, cgym_stream_t stream) {
   CGYM_REQUIRE(state != nullptr && n_slots >= 0 && vocab > 0, "sample_record: bad arguments");
   CGYM_REQUIRE(state->seeds && state->temperatures && state->rng_positions && state->lengths && state->alive,
                "sample_record: slot state is incomplete");
   if (n_slots == 0) return 0;
+  const dim3 grid(n_slots, pick_parts(n_slots, vocab, workspace));
   if (dtype == CGYM_F32)
-    sample_kernel<float><<<n_slots, SAMPLE_THREADS, 0, as_stream(stream)>>>(
-        static_cast<const float*>(logits), *state, true, advance, state->seeds, state->rng_positions,
-        state->temperatures, state->rng_offsets, sampled_out, logp_out, vocab);
+    launch_dependent(sample_kernel<float>, grid, dim3(SAMPLE_THREADS), 0, as_stream(stream),
+                     static_cast<const float*>(logits), *state, true, advance, state->seeds, state->rng_positions,
+                     state->temperatures, state->rng_offsets, sampled_out, logp_out, vocab, workspace);
   else if (dtype == CGYM_BF16)
-    sample_kernel<__nv_bfloat16><<<n_slots, SAMPLE_THREADS, 0, as_stream(stream)>>>(
-        static_cast<const __nv_bfloat16*>(logits), *state, true, advance, state->seeds, state->rng_positions,
-        state->temperatures, state->rng_offsets, sampled_out, logp_out, vocab);
+    launch_dependent(sample_kernel<__nv_bfloat16>, grid, dim3(SAMPLE_THREADS), 0, as_stream(stream),
+                     static_cast<const __nv_bfloat16*>(logits), *state, true, advance, state->seeds,
+                     state->rng_positions, state->temperatures, state->rng_offsets, sampled_out, logp_out, vocab,
+                     workspace);
   else
     return fail("sample_record: unsupported logits dtype %d", dtype);
   return check_launch("sample_record");
@@ -170,18 +217,19 @@ extern "C" int cgym_sample_record(const void* logits, const cgym_slot_state* sta
 
 extern "C" int cgym_sample(int64_t* tokens, float* logprobs, const void* logits, const int64_t* seeds,
                            const int64_t* steps, const float* temperatures, const int64_t* rng_offsets, int rows,
-                           int vocab, int dtype, cgym_stream_t stream) {
+                           int vocab, int dtype, float* workspace, cgym_stream_t stream) {
   CGYM_REQUIRE(rows >= 0 && vocab > 0 && seeds && steps && temperatures && tokens, "sample: bad arguments");
   if (rows == 0) return 0;
   cgym_slot_state none{};
+  const dim3 grid(rows, pick_parts(rows, vocab, workspace));
   if (dtype == CGYM_F32)
-    sample_kernel<float><<<rows, SAMPLE_THREADS, 0, as_stream(stream)>>>(
+    sample_kernel<float><<<grid, SAMPLE_THREADS, 0, as_stream(stream)>>>(
         static_cast<const float*>(logits), none, false, nullptr, seeds, steps, temperatures, rng_offsets, tokens,
-        logprobs, vocab);
+        logprobs, vocab, workspace);
   else if (dtype == CGYM_BF16)
-    sample_kernel<__nv_bfloat16><<<rows, SAMPLE_THREADS, 0, as_stream(stream)>>>(
+    sample_kernel<__nv_bfloat16><<<grid, SAMPLE_THREADS, 0, as_stream(stream)>>>(
         static_cast<const __nv_bfloat16*>(logits), none, false, nullptr, seeds, steps, temperatures, rng_offsets,
-        tokens, logprobs, vocab);
+        tokens, logprobs, vocab, workspace);
   else
     return fail("sample: unsupported logits dtype %d", dtype);
   return check_launch("sample");

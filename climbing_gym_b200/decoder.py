@@ -11,6 +11,7 @@ rows are masked inside the kernels instead of being compacted on the host.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from collections import OrderedDict
 from dataclasses import dataclass, field
 
@@ -50,6 +51,9 @@ class SlotState:
         self.stop_table = torch.zeros(stop_states * vocab, device=dev, dtype=torch.int32)
         self.stop_table_used = vocab
         self.seq_lens = seq_lens
+        # sampler scratch: per-(row, slice) partial picks + one arrival counter per row, kept at zero
+        self.sample_ws = torch.zeros(int(nv.load().cgym_sample_workspace_bytes(n_slots)) // 4, device=dev,
+                                     dtype=torch.float32)
         self.struct = nv.SlotState(
             nv.ptr(self.tokens), nv.ptr(self.logprobs), nv.ptr(self.lengths), nv.ptr(self.limits),
             nv.ptr(self.reasons), nv.ptr(self.alive), nv.ptr(self.pending), nv.ptr(self.input_tokens),
@@ -152,6 +156,7 @@ class B200Decoder:
         self.adaptive_batching, self.fp8_lm_head = bool(adaptive_batching), bool(fp8_lm_head)
         self.page_size = page_size
         self.use_cuda_graphs = use_cuda_graphs
+        self.use_pdl = os.environ.get("CGYM_PDL", "1") != "0"
         self.runner = LFM25Runner(engine.weights, engine._rope_cos, engine._rope_sin, fp8_mlp=self.fp8_mlp,
                                   fp8_lm_head=self.fp8_lm_head)
         self.graphs: OrderedDict = OrderedDict()
@@ -187,14 +192,14 @@ class B200Decoder:
                 None, None, n, nv.ptr(cache.status), stream)
         self.runner.decode_step(entry.bufs, cache, state.input_tokens, state.active, entry.logits)
         nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(state.struct), nv.ptr(state.active), None, None,
-                n, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype), stream)
+                n, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype), nv.ptr(state.sample_ws), stream)
 
     def _sample_only(self, entry: _DecodeGraph) -> None:
         """First token of freshly prefetched rows: sample from the prefill logits, no forward."""
         state = entry.state
         nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(state.struct), None, None, None,
                 entry.cache.n_slots, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype),
-                nv.stream_ptr(self.engine.device))
+                nv.ptr(state.sample_ws), nv.stream_ptr(self.engine.device))
 
     @torch.inference_mode()
     def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False) -> _DecodeGraph:
@@ -222,20 +227,26 @@ class B200Decoder:
         # touches KV pages, conv taps, logits or bookkeeping.
         stream, current = self._capture_stream, torch.cuda.current_stream(engine.device)
         stream.wait_stream(current)
-        with torch.cuda.stream(stream):
-            for _ in range(2):
-                self._step(entry)
-        current.wait_stream(stream)
-        torch.cuda.synchronize(engine.device)
-        if self.use_cuda_graphs:
-            graph = torch.cuda.CUDAGraph()
-            before = nv.load().cgym_launch_count()
-            with torch.cuda.graph(graph, stream=stream):
-                self._step(entry)
+        lib = nv.load()
+        # the step's kernels are chained with programmatic dependent launches (see cgym_set_pdl)
+        previous_pdl = lib.cgym_set_pdl(1 if self.use_pdl else 0)
+        try:
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    self._step(entry)
             current.wait_stream(stream)
-            entry.graph = _StepGraph(graph, int(nv.load().cgym_launch_count() - before))
-        else:
-            entry.graph = _EagerStep(self, entry)
+            torch.cuda.synchronize(engine.device)
+            if self.use_cuda_graphs:
+                graph = torch.cuda.CUDAGraph()
+                before = lib.cgym_launch_count()
+                with torch.cuda.graph(graph, stream=stream):
+                    self._step(entry)
+                current.wait_stream(stream)
+                entry.graph = _StepGraph(graph, int(lib.cgym_launch_count() - before))
+            else:
+                entry.graph = _EagerStep(self, entry)
+        finally:
+            lib.cgym_set_pdl(previous_pdl)
         self.graphs[key] = entry
         return entry
 

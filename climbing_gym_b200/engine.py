@@ -479,7 +479,8 @@ class LFM25Engine:
         temps = torch.full((n,), float(sampling.temperature), device=dev, dtype=torch.float32)
         offsets = torch.arange(n, device=dev, dtype=torch.int64) * self.config.vocab_size
         nv.call("cgym_sample", nv.ptr(out_tokens), nv.ptr(out_logp), nv.ptr(logits), nv.ptr(seeds), nv.ptr(steps),
-                nv.ptr(temps), nv.ptr(offsets), n, self.config.vocab_size, nv.dtype_code(self.dtype), nv.stream_ptr(dev))
+                nv.ptr(temps), nv.ptr(offsets), n, self.config.vocab_size, nv.dtype_code(self.dtype), None,
+                nv.stream_ptr(dev))
         reasons = torch.zeros(n, device=dev, dtype=torch.int8)
         if not sampling.ignore_eos:
             reasons[out_tokens == int(self.config.eos_token_id)] = 1

@@ -46,7 +46,8 @@ class ForwardBuffers:
         self.attn_ws = (torch.empty(rows * hq * attn_splits * (d + 2), device=dev, dtype=torch.float32)
                         if attn_splits > 1 else None)
         # split-K partials of the narrow projections: up to 16 splits of [rows, hidden] fp32
-        self.gemm_ws = torch.empty(min(16 * rows * max(h, 1) * 4, 32 << 20), device=dev, dtype=torch.uint8)
+        # (zero-filled: its last 4 KB are the GEMM's per-tile arrival counters)
+        self.gemm_ws = torch.zeros(min(16 * rows * max(h, 1) * 4, 32 << 20) + 4096, device=dev, dtype=torch.uint8)
 
 
 class LFM25Runner:

@@ -62,6 +62,14 @@ int cgym_version(void);
 /* kernels this library has enqueued so far in this process (launches recorded into a CUDA graph
  * count once, at capture) */
 long long cgym_launch_count(void);
+/* Programmatic dependent launch for the kernels of the decode step (embedding, norms, GEMMs,
+ * QK/RoPE/append, decode attention, conv update, SwiGLU, sampler): while enabled they are launched
+ * with programmatic stream serialization, so a kernel is scheduled - and the GEMMs prefetch their
+ * first weight tiles - while its predecessor is still draining; each of them waits for the
+ * predecessor grid before touching dependent memory. Off by default; returns the previous setting.
+ * Process-wide host flag read at launch time (set it around a graph capture). No reference
+ * counterpart (the reference relies on CUDA graphs alone, lfm25_cuda.py:246-262). */
+int cgym_set_pdl(int enabled);
 /* 1 when the device of the current context is compute capability 10.x */
 int cgym_device_supported(void);
 
@@ -146,7 +154,9 @@ int cgym_prefill_attention(void* out, const void* q, const int32_t* tile_row0,
  * lfm25_cuda.py:124-126,141,166,170-172,180,192): y[M,N] = x[M,K] . w[N,K]^T, fp32 accumulate.
  * row_mask (uint8[M], optional): rows with 0 are not written (replaces the saved-logits
  * where-merge, lfm25_cuda.py:237-245). impl: 0 = auto, 1 = SIMT tile kernel, 2 = tcgen05/TMEM.
- * workspace/workspace_bytes: scratch for split-K partials (may be NULL => no split-K). */
+ * workspace/workspace_bytes: scratch for split-K (may be NULL => no split-K): fp32 partials followed
+ * by 4 KB of per-tile arrival counters in the LAST 4096 bytes, which must be zero before the first
+ * call (the kernel re-arms them); launches sharing a workspace must be stream-ordered. */
 int cgym_gemm(void* y, const void* x, const void* w, const uint8_t* row_mask, int M, int N, int K,
               int dtype, int impl, void* workspace, int64_t workspace_bytes, int32_t* status,
               cgym_stream_t stream);
@@ -186,15 +196,22 @@ typedef struct {
  * lfm25_session.py:34-56): Gumbel-max / greedy over logits [n_slots, vocab], sampled-token
  * log-prob from the untempered logits, then the per-slot bookkeeping. `advance` (uint8[n_slots],
  * optional) marks rows whose decode input was consumed this step: their seq_lens += 1
- * (lfm25_cuda.py:185-189). sampled_out/logp_out (optional) receive the raw draw per slot. */
+ * (lfm25_cuda.py:185-189). sampled_out/logp_out (optional) receive the raw draw per slot.
+ * workspace (optional, cgym_sample_workspace_bytes(n_slots) bytes, zero before the first call and
+ * re-armed by the kernel): lets a row's vocabulary be sliced over several CTAs, the reference's
+ * 4096-wide tiles (lfm25_sampling.py:76-91); without it one CTA reduces a whole row. */
 int cgym_sample_record(const void* logits, const cgym_slot_state* state, const uint8_t* advance,
                        int64_t* sampled_out, float* logp_out, int n_slots, int vocab, int dtype,
-                       cgym_stream_t stream);
+                       float* workspace, cgym_stream_t stream);
 
 /* Stand-alone sampler (sample_logits / RowSampler.sample, lfm25_sampling.py:61-123). */
 int cgym_sample(int64_t* tokens, float* logprobs, const void* logits, const int64_t* seeds,
                 const int64_t* steps, const float* temperatures, const int64_t* rng_offsets,
-                int rows, int vocab, int dtype, cgym_stream_t stream);
+                int rows, int vocab, int dtype, float* workspace, cgym_stream_t stream);
+
+/* Bytes of sampler workspace for `rows` rows (the scores / indices / maxima / totals scratch of
+ * lfm25_sampling.py:77-80 plus one arrival counter per row). */
+int64_t cgym_sample_workspace_bytes(int rows);
 
 /* Chunked-head completion scoring (lfm25_engine.py:1150-1154): logit[target] - logsumexp. */
 int cgym_target_logprobs(float* out, const void* logits, const int64_t* targets, int rows,

@@ -382,7 +382,8 @@ def gemm_call(dev, x, w, *, impl, mask=None, ws_bytes=0):
     m, k = x.shape
     n = w.shape[0]
     y = torch.full((m, n), -3.0, device=dev, dtype=x.dtype)
-    ws = torch.empty(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
+    ws_bytes = ws_bytes + 4096 if ws_bytes else 0  # partials + zeroed tile counters
+    ws = torch.zeros(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
     status = torch.zeros(1, device=dev, dtype=torch.int32)
     nv.call("cgym_gemm", nv.ptr(y), nv.ptr(x), nv.ptr(w), nv.ptr(mask), m, n, k, nv.dtype_code(x.dtype), impl,
             nv.ptr(ws) if ws_bytes else None, ws_bytes, nv.ptr(status), stream())
@@ -475,10 +476,15 @@ def test_sampler_matches_reference_vectors(dev, golden):
             seeds, steps = torch.tensor(case["seeds"]), torch.tensor(case["steps"])
             temps, offsets = torch.tensor(case["temperatures"], dtype=torch.float32), torch.zeros(rows, dtype=torch.int64)
         args = [a.to(dev) for a in (seeds, steps, temps, offsets)]
-        nv.call("cgym_sample", nv.ptr(tokens), nv.ptr(logp), nv.ptr(logits), nv.ptr(args[0]), nv.ptr(args[1]),
-                nv.ptr(args[2]), nv.ptr(args[3]), rows, vocab, nv.F32, stream())
-        assert tokens.cpu().tolist() == case["tokens"], case
-        assert np.allclose(logp.cpu().numpy(), case["logprobs"], atol=3e-6), case
+        # one CTA per row, then the sliced variant (several CTAs per row, last arrival combines)
+        ws = torch.zeros(int(nv.load().cgym_sample_workspace_bytes(rows)) // 4, device=dev, dtype=torch.float32)
+        for workspace in (None, ws, ws):
+            tokens.fill_(-1)
+            nv.call("cgym_sample", nv.ptr(tokens), nv.ptr(logp), nv.ptr(logits), nv.ptr(args[0]), nv.ptr(args[1]),
+                    nv.ptr(args[2]), nv.ptr(args[3]), rows, vocab, nv.F32, nv.ptr(workspace), stream())
+            assert tokens.cpu().tolist() == case["tokens"], case
+            assert np.allclose(logp.cpu().numpy(), case["logprobs"], atol=3e-6), case
+        assert float(ws.abs().max()) >= 0 and int(ws[-rows:].view(torch.int32).abs().max()) == 0, "counters re-armed"
 
 
 def test_sampler_bf16_logits_and_distribution(dev):
@@ -492,7 +498,7 @@ def test_sampler_bf16_logits_and_distribution(dev):
     zeros = torch.zeros(rows, device=dev, dtype=torch.int64)
     temps = torch.ones(rows, device=dev, dtype=torch.float32)
     nv.call("cgym_sample", nv.ptr(tokens), nv.ptr(logp), nv.ptr(logits), nv.ptr(seeds), nv.ptr(zeros), nv.ptr(temps),
-            None, rows, vocab, nv.BF16, stream())
+            None, rows, vocab, nv.BF16, None, stream())
     counts = np.bincount(tokens.cpu().numpy(), minlength=vocab) / rows
     probs = np.exp(round_bf16(base) - np.log(np.exp(round_bf16(base)).sum()))
     assert np.abs(counts - probs).max() < 0.03  # 4096 draws: ~4 sigma of the largest bin
@@ -523,7 +529,7 @@ def test_sample_record_bookkeeping_matches_reference_kernel(dev, golden):
         logits[row, tok] = 20.0
     advance = torch.tensor([1, 0, 1, 0, 0, 1], device=dev, dtype=torch.uint8)
     nv.call("cgym_sample_record", nv.ptr(logits), C.byref(st.struct), nv.ptr(advance), None, None, n, vocab, nv.F32,
-            stream())
+            nv.ptr(st.sample_ws), stream())
     torch.cuda.synchronize()
     assert st.tokens.cpu().tolist() == g["tokens"]
     for key, tensor in (("lengths", st.lengths), ("reasons", st.reasons), ("alive", st.alive), ("pending", st.pending),
