@@ -71,6 +71,7 @@ SIGNATURES = {
     "cgym_gemm_fp8": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_sample": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P],
+    "cgym_sample_static": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "cgym_target_logprobs": [_P, _P, _P, _I, _I, _I, _P],
     "cgym_step_begin": [C.POINTER(PagePool), _P, _P, _P, _P, _P, _I, _P, _P],
     "cgym_pages_reserve": [C.POINTER(PagePool), _P, _P, _I, _P, _P],

@@ -11,6 +11,8 @@
 // so a row is spread over several SMs); with parts > 1 the CTA that arrives last at the row's
 // counter combines the slices in slice order (deterministic) and does the bookkeeping. The
 // workspace holds 4 floats per (row, part) plus one counter per row, zero between launches.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace cgym {
@@ -233,4 +235,67 @@ extern "C" int cgym_sample(int64_t* tokens, float* logprobs, const void* logits,
   else
     return fail("sample: unsupported logits dtype %d", dtype);
   return check_launch("sample");
+}
+
+// ---- sampler whose slice scratch lives in the library image ---------------------------------
+// Same kernel and slicing as cgym_sample with a workspace, but the workspace is a fixed array of
+// this module, so the call needs no memory from the caller and requests none from the runtime.
+
+constexpr int SAMPLE_STATIC_MAX_ROWS = CGYM_SAMPLE_STATIC_MAX_ROWS;
+constexpr int SAMPLE_STATIC_FLOATS = SAMPLE_STATIC_MAX_ROWS * SAMPLE_MAX_PARTS * 4 + SAMPLE_STATIC_MAX_ROWS;  // 130 KiB
+constexpr int SAMPLE_STATIC_MAX_DEVICES = 64;
+
+static __device__ __align__(256) float g_sample_scratch[SAMPLE_STATIC_FLOATS];
+
+static std::mutex g_sample_static_mutex;
+static float* g_sample_scratch_ptr[SAMPLE_STATIC_MAX_DEVICES] = {};
+
+// Address of this device's copy of the scratch array, resolved once per device with that device
+// current (every device that loads the module has its own copy of the array).
+static int sample_scratch_for_current_device(float** out) {
+  int device = -1;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return fail("sample_static: cudaGetDevice failed: %s", cudaGetErrorString(err));
+  if (device < 0 || device >= SAMPLE_STATIC_MAX_DEVICES)
+    return fail("sample_static: device ordinal %d is beyond the %d this entry point keeps scratch for", device,
+                SAMPLE_STATIC_MAX_DEVICES);
+  std::lock_guard<std::mutex> lock(g_sample_static_mutex);
+  if (g_sample_scratch_ptr[device] == nullptr) {
+    float* ptr = nullptr;
+    err = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_sample_scratch);
+    if (err != cudaSuccess || ptr == nullptr)
+      return fail("sample_static: cudaGetSymbolAddress failed on device %d: %s", device, cudaGetErrorString(err));
+    g_sample_scratch_ptr[device] = ptr;
+  }
+  *out = g_sample_scratch_ptr[device];
+  return 0;
+}
+
+extern "C" int cgym_sample_static(int64_t* tokens, float* logprobs, const void* logits, const int64_t* seeds,
+                                  const int64_t* steps, const float* temperatures, const int64_t* rng_offsets,
+                                  int rows, int vocab, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(rows >= 0 && vocab > 0, "sample_static: bad arguments");
+  if (rows > SAMPLE_STATIC_MAX_ROWS)
+    return fail("sample_static: %d rows exceed the built-in scratch (at most %d rows per call); split the batch or "
+                "use cgym_sample with a caller-owned workspace", rows, SAMPLE_STATIC_MAX_ROWS);
+  CGYM_REQUIRE(dtype == CGYM_F32 || dtype == CGYM_BF16, "sample_static: unsupported logits dtype");
+  float* scratch = nullptr;
+  if (sample_scratch_for_current_device(&scratch) != 0) return 1;
+  if (rows == 0) return 0;  // set-up only
+  CGYM_REQUIRE(seeds && steps && temperatures && tokens && logits, "sample_static: bad arguments");
+  // the per-row arrival counters must read zero when the kernel starts; the slices need no clearing
+  float* counters = scratch + static_cast<int64_t>(rows) * SAMPLE_MAX_PARTS * 4;
+  cudaError_t err = cudaMemsetAsync(counters, 0, sizeof(int) * rows, as_stream(stream));
+  if (err != cudaSuccess) return fail("sample_static: clearing the counters failed: %s", cudaGetErrorString(err));
+  cgym_slot_state none{};
+  const dim3 grid(rows, pick_parts(rows, vocab, scratch));
+  if (dtype == CGYM_F32)
+    sample_kernel<float><<<grid, SAMPLE_THREADS, 0, as_stream(stream)>>>(
+        static_cast<const float*>(logits), none, false, nullptr, seeds, steps, temperatures, rng_offsets, tokens,
+        logprobs, vocab, scratch);
+  else
+    sample_kernel<__nv_bfloat16><<<grid, SAMPLE_THREADS, 0, as_stream(stream)>>>(
+        static_cast<const __nv_bfloat16*>(logits), none, false, nullptr, seeds, steps, temperatures, rng_offsets,
+        tokens, logprobs, vocab, scratch);
+  return check_launch("sample_static");
 }

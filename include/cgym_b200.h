@@ -213,6 +213,25 @@ int cgym_sample(int64_t* tokens, float* logprobs, const void* logits, const int6
  * lfm25_sampling.py:77-80 plus one arrival counter per row). */
 int64_t cgym_sample_workspace_bytes(int rows);
 
+/* cgym_sample for callers that cannot hand over a workspace and must not cause a device
+ * allocation: it has no counterpart in the reference, whose sampler allocates its slice scratch
+ * with torch on every call. Same draws, slicing and results as cgym_sample with a workspace; the
+ * slice scratch is a fixed 130 KiB array inside the library image, one copy per device.
+ *  - At most CGYM_SAMPLE_STATIC_MAX_ROWS rows per call; more is rejected with an error that says
+ *    so (split the batch, or use cgym_sample with your own workspace).
+ *  - The first call on each device, made with that device current, resolves the address of the
+ *    device's copy of the array (this may load the library's device code). Make that call before
+ *    any stream capture begins on the device; rows = 0 does only this set-up and launches nothing.
+ *  - Each call clears the row counters it needs with a memset on `stream` ahead of the kernel; it
+ *    calls no allocating or freeing routine of the CUDA runtime.
+ *  - Calls on one device share the one array: two calls whose execution can overlap (different
+ *    streams, or different host threads without ordering) race on it and give undefined draws.
+ *    Serialise them on one stream. The array keeps the last call's slices until the next call. */
+#define CGYM_SAMPLE_STATIC_MAX_ROWS 512
+int cgym_sample_static(int64_t* tokens, float* logprobs, const void* logits, const int64_t* seeds,
+                       const int64_t* steps, const float* temperatures, const int64_t* rng_offsets,
+                       int rows, int vocab, int dtype, cgym_stream_t stream);
+
 /* Chunked-head completion scoring (lfm25_engine.py:1150-1154): logit[target] - logsumexp. */
 int cgym_target_logprobs(float* out, const void* logits, const int64_t* targets, int rows,
                          int vocab, int dtype, cgym_stream_t stream);
