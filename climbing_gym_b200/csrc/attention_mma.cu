@@ -278,8 +278,8 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   extern __shared__ __align__(128) uint8_t att_smem[];
   __shared__ __align__(8) uint64_t bars[4][2];
   __shared__ int abort_flag;
-  pdl_wait();     // q, the new K/V row and the block table come from the kernels just before
   pdl_trigger();
+  pdl_wait();     // q, the new K/V row and the block table come from the kernels just before
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int G = n_q_heads / kv.n_kv_heads;

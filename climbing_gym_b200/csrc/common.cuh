@@ -33,7 +33,11 @@ inline cudaStream_t as_stream(cgym_stream_t s) { return reinterpret_cast<cudaStr
 // init, TMEM allocation, descriptor fetch) and - for the GEMMs - the first weight tiles overlap
 // the predecessor's tail. Contract: a kernel launched through launch_dependent() calls pdl_wait()
 // before it touches memory a predecessor may write or still read, and pdl_trigger() once it no
-// longer minds the next kernel being scheduled. Both are no-ops for ordinary launches.
+// longer minds the next kernel being scheduled. Every thread of every such kernel calls pdl_wait()
+// (so a grid never completes before its predecessor: the wait is transitive along the chain), and
+// kernels trigger BEFORE they wait, which lets the kernels several positions ahead become
+// resident - the GEMMs among them stream their first weight tiles - while the chain catches up.
+// Both are no-ops for ordinary launches.
 extern int g_pdl_enabled;  // toggled by cgym_set_pdl(); read at launch time on the host
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -16,8 +16,8 @@ namespace cgym {
 template <typename T>
 __global__ void embedding_kernel(T* __restrict__ out, const T* __restrict__ table,
                                  const int64_t* __restrict__ tokens, int hidden, int vocab) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   int64_t tok = tokens[row];
   if (tok < 0 || tok >= vocab) tok = 0;  // padding rows carry arbitrary ids; never index outside the table
@@ -36,8 +36,8 @@ __global__ void rmsnorm_kernel(T* __restrict__ y, uint8_t* __restrict__ q, float
                                float eps) {
   extern __shared__ float row_buf[];  // hidden floats
   __shared__ float scratch[32];
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int64_t base = static_cast<int64_t>(blockIdx.x) * hidden;
   float ss = 0.0f;
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
@@ -73,6 +73,129 @@ __global__ void rmsnorm_kernel(T* __restrict__ y, uint8_t* __restrict__ q, float
   }
 }
 
+// bf16 fast path: a row lives in registers. Thread t owns the 16-byte chunks t, t + 256, ... (CHUNKS of
+// them), all of whose loads are issued back to back, so a row costs one L2 round trip instead of one
+// per element; the norm weights do not depend on the previous kernel and are fetched before the
+// dependent-launch wait. Same rounding points as rmsnorm_kernel.
+constexpr int RMS_THREADS = 256;
+
+__device__ __forceinline__ void unpack8(const uint4& raw, float* out) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(p[j]);
+    out[2 * j] = f.x;
+    out[2 * j + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 raw;
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) p[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+  return raw;
+}
+
+template <int CHUNKS, bool QUANT>
+__global__ void __launch_bounds__(RMS_THREADS)
+rmsnorm_rows_bf16_kernel(__nv_bfloat16* __restrict__ y, uint8_t* __restrict__ q, float* __restrict__ scales,
+                         __nv_bfloat16* __restrict__ sum_out, const __nv_bfloat16* __restrict__ x,
+                         const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w,
+                         int hidden, float eps) {
+  __shared__ float scratch[32];
+  const int n_chunks = hidden >> 3;
+  uint4 w_raw[CHUNKS];
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int chunk = threadIdx.x + c * RMS_THREADS;
+    w_raw[c] = chunk < n_chunks ? __ldg(reinterpret_cast<const uint4*>(w) + chunk) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_trigger();
+  pdl_wait();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * n_chunks;  // in 16-byte chunks
+  uint4 x_raw[CHUNKS], r_raw[CHUNKS];
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int chunk = threadIdx.x + c * RMS_THREADS;
+    x_raw[c] = r_raw[c] = make_uint4(0, 0, 0, 0);
+    if (chunk < n_chunks) {
+      x_raw[c] = *(reinterpret_cast<const uint4*>(x) + base + chunk);
+      if (residual != nullptr) r_raw[c] = *(reinterpret_cast<const uint4*>(residual) + base + chunk);
+    }
+  }
+  float v[CHUNKS][8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int chunk = threadIdx.x + c * RMS_THREADS;
+    unpack8(x_raw[c], v[c]);
+    if (residual != nullptr) {
+      float r[8];
+      unpack8(r_raw[c], r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[c][j] = Elem<__nv_bfloat16>::round(__fadd_rn(v[c][j], r[j]));
+      if (chunk < n_chunks) *(reinterpret_cast<uint4*>(sum_out) + base + chunk) = pack8(v[c]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(v[c][j], v[c][j], ss);
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = rsqrtf(total / static_cast<float>(hidden) + eps);
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int chunk = threadIdx.x + c * RMS_THREADS;
+    float wv[8];
+    unpack8(w_raw[c], wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float n = Elem<__nv_bfloat16>::round(__fmul_rn(v[c][j], inv));
+      v[c][j] = Elem<__nv_bfloat16>::round(__fmul_rn(n, wv[j]));
+      amax = fmaxf(amax, fabsf(v[c][j]));
+    }
+    if (!QUANT && chunk < n_chunks) *(reinterpret_cast<uint4*>(y) + base + chunk) = pack8(v[c]);
+  }
+  if (QUANT) {
+    amax = block_max(amax, scratch);
+    const float scale = fmaxf(amax / 448.0f, 1.0e-12f);
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int chunk = threadIdx.x + c * RMS_THREADS;
+      if (chunk >= n_chunks) continue;
+      uint2 codes;
+      uint8_t* bytes = reinterpret_cast<uint8_t*>(&codes);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bytes[j] = to_e4m3(fminf(fmaxf(__fdiv_rn(v[c][j], scale), -448.0f), 448.0f));
+      *(reinterpret_cast<uint2*>(q) + base + chunk) = codes;
+    }
+    if (threadIdx.x == 0) scales[blockIdx.x] = scale;
+  }
+}
+
+// true when the register-resident kernel applies: bf16, rows of whole 16-byte chunks, 16-byte aligned
+static bool rms_fast_path(int hidden, const void* a, const void* b, const void* c, const void* d, const void* e) {
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c) |
+                         reinterpret_cast<uintptr_t>(d) | reinterpret_cast<uintptr_t>(e);
+  return hidden % 8 == 0 && hidden <= 8 * RMS_THREADS * 4 && (bits & 15u) == 0;
+}
+
+template <bool QUANT>
+static void launch_rms_fast(__nv_bfloat16* y, uint8_t* q, float* scales, __nv_bfloat16* sum_out, const __nv_bfloat16* x,
+                            const __nv_bfloat16* residual, const __nv_bfloat16* w, int rows, int hidden, float eps,
+                            cudaStream_t stream) {
+  const int chunks = (hidden / 8 + RMS_THREADS - 1) / RMS_THREADS;
+  if (chunks <= 1)
+    launch_dependent(rmsnorm_rows_bf16_kernel<1, QUANT>, dim3(rows), dim3(RMS_THREADS), 0, stream, y, q, scales, sum_out,
+                     x, residual, w, hidden, eps);
+  else if (chunks == 2)
+    launch_dependent(rmsnorm_rows_bf16_kernel<2, QUANT>, dim3(rows), dim3(RMS_THREADS), 0, stream, y, q, scales, sum_out,
+                     x, residual, w, hidden, eps);
+  else
+    launch_dependent(rmsnorm_rows_bf16_kernel<4, QUANT>, dim3(rows), dim3(RMS_THREADS), 0, stream, y, q, scales, sum_out,
+                     x, residual, w, hidden, eps);
+}
+
 // ------------------------------------------------------------------------------------------
 // SwiGLU (+ quantisation)
 // ------------------------------------------------------------------------------------------
@@ -84,8 +207,8 @@ __device__ __forceinline__ float swiglu_value(float gate, float up) {
 
 template <typename T>
 __global__ void swiglu_kernel(T* __restrict__ y, const T* __restrict__ gate_up, int ffn) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.y;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= ffn) return;
@@ -99,8 +222,8 @@ __global__ void swiglu_quant_kernel(uint8_t* __restrict__ q, float* __restrict__
                                     const T* __restrict__ gate_up, int ffn) {
   extern __shared__ float row_buf[];
   __shared__ float scratch[32];
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   float amax = 0.0f;
   for (int i = threadIdx.x; i < ffn; i += blockDim.x) {
@@ -138,8 +261,8 @@ template <typename T>
 __global__ void conv_update_kernel(T* __restrict__ y, T* __restrict__ state, const T* __restrict__ bcx,
                                    const T* __restrict__ conv_w, const uint8_t* __restrict__ active,
                                    const int32_t* __restrict__ slots, int hidden) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= hidden) return;
@@ -235,8 +358,8 @@ __global__ void qk_rope_append_kernel(T* __restrict__ q_out, T* __restrict__ k_n
                                       cgym_kv_layout kv, int layer, int n_q_heads, float eps, int32_t* status) {
   __shared__ float buf[256];
   __shared__ float scratch[32];
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x, head = blockIdx.y, d = threadIdx.x, D = kv.head_dim, half = D >> 1;
   const int n_kv = kv.n_kv_heads;
   const int width = (n_q_heads + 2 * n_kv) * D;
@@ -331,6 +454,13 @@ extern "C" int cgym_rmsnorm(void* y, void* sum_out, const void* x, const void* r
   CGYM_REQUIRE(rows >= 0 && hidden > 0 && hidden <= 12288, "rmsnorm: hidden must be in [1, 12288]");
   CGYM_REQUIRE(residual == nullptr || sum_out != nullptr, "rmsnorm: residual needs sum_out");
   if (rows == 0) return 0;
+  if (dtype == CGYM_BF16 && rms_fast_path(hidden, y, sum_out, x, residual, w)) {
+    using B = __nv_bfloat16;
+    launch_rms_fast<false>(static_cast<B*>(y), nullptr, nullptr, static_cast<B*>(sum_out), static_cast<const B*>(x),
+                           static_cast<const B*>(residual), static_cast<const B*>(w), rows, hidden, eps,
+                           as_stream(stream));
+    return check_launch("rmsnorm");
+  }
   DISPATCH_DTYPE(dtype, (launch_dependent(rmsnorm_kernel<T, false>, dim3(rows), dim3(256), hidden * sizeof(float),
                                           as_stream(stream), static_cast<T*>(y), nullptr, nullptr,
                                           static_cast<T*>(sum_out), static_cast<const T*>(x),
@@ -344,6 +474,12 @@ extern "C" int cgym_rmsnorm_quant(uint8_t* q, float* scales, void* sum_out, cons
   CGYM_REQUIRE(residual == nullptr || sum_out != nullptr, "rmsnorm_quant: residual needs sum_out");
   if (rows == 0) return 0;
   using T = __nv_bfloat16;
+  if (rms_fast_path(hidden, q, sum_out, x, residual, w) && (reinterpret_cast<uintptr_t>(q) & 7u) == 0) {
+    launch_rms_fast<true>(nullptr, q, scales, static_cast<T*>(sum_out), static_cast<const T*>(x),
+                          static_cast<const T*>(residual), static_cast<const T*>(w), rows, hidden, eps,
+                          as_stream(stream));
+    return check_launch("rmsnorm_quant");
+  }
   launch_dependent(rmsnorm_kernel<T, true>, dim3(rows), dim3(256), hidden * sizeof(float), as_stream(stream), nullptr,
                    q, scales, static_cast<T*>(sum_out), static_cast<const T*>(x), static_cast<const T*>(residual),
                    static_cast<const T*>(w), hidden, eps);

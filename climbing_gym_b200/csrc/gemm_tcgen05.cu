@@ -126,7 +126,24 @@ struct GemmEpilogue {
   int32_t* status;
   int M, N, K;
   int partial;             // 1: split-K over a cluster of gridDim.z CTAs, reduced through DSMEM
+#ifdef CGYM_TRACE
+  unsigned long long* trace;  // [ctas <= 512][4] globaltimer stamps of this launch (debug builds only)
+#endif
 };
+
+#ifdef CGYM_TRACE
+__device__ __forceinline__ void trace_stamp(const GemmEpilogue& ep, int which) {
+  if (ep.trace == nullptr) return;
+  const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (cta >= 512u) return;
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  ep.trace[cta * 4 + which] = t;
+}
+#define CGYM_STAMP(which) trace_stamp(ep, which)
+#else
+#define CGYM_STAMP(which)
+#endif
 
 // Cluster split-K reduction for one output feature (column of the parked [UN][128] fp32 tiles):
 // CTA `rank` owns token rows ml = rank, rank + SPLITS, ... and sums the SPLITS peers' values in split
@@ -165,12 +182,15 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
   }
 }
 
-template <int UN, bool FP8>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+// RING_KB bounds the TMA ring: 192 fills the SM for one CTA (large token tiles); 96 lets two CTAs
+// share an SM, so the CTAs of the NEXT kernel of a dependent-launch chain become resident - and
+// stream their first weight tiles - while this kernel's CTAs are still computing.
+template <int UN, bool FP8, int RING_KB>
+__global__ void __launch_bounds__(GEMM_THREADS, RING_KB <= 96 ? 2 : 1)
 gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     GemmEpilogue ep) {
   constexpr int STAGE_BYTES = (UM + UN) * SLICE_BYTES;
-  constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
+  constexpr int STAGES = (RING_KB * 1024 / STAGE_BYTES) > 8 ? 8 : (RING_KB * 1024 / STAGE_BYTES);
   constexpr int ELEMS_PER_SLICE = FP8 ? 128 : 64;
   constexpr int TMEM_COLS = UN < 32 ? 32 : UN;
   extern __shared__ uint8_t smem_raw[];
@@ -181,6 +201,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   __shared__ int abort_flag;
 
   pdl_trigger();  // the next kernel may be scheduled now; it waits for this grid before touching y
+  if (threadIdx.x == 0) CGYM_STAMP(0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t tiles = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int n0 = blockIdx.x * UM, m0 = blockIdx.y * UN;
@@ -222,6 +243,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
       tma_load_2d(tiles + i * STAGE_BYTES, &tmap_w, full, (kb_begin + i) * ELEMS_PER_SLICE, n0);
     }
     pdl_wait();
+    CGYM_STAMP(1);
     for (int i = 0; i < prefetch; ++i) {
       tma_load_2d(tiles + i * STAGE_BYTES + UM * SLICE_BYTES, &tmap_x, smem_u32(&bar_full[i]),
                   (kb_begin + i) * ELEMS_PER_SLICE, m0);
@@ -271,6 +293,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     pdl_wait();  // scales / row mask come from earlier kernels of the step
     if (n_kb > 0) mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps agree on abort_flag
+    if (warp == 2 && lane == 0) CGYM_STAMP(2);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (abort_flag == 0 || ep.partial) {
       const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
@@ -329,6 +352,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (threadIdx.x == 0 && abort_flag) atomicOr(ep.status, CGYM_STATUS_WAIT_TIMEOUT);
+  if (threadIdx.x == 0) CGYM_STAMP(3);
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_acc), "r"(TMEM_COLS) : "memory");
@@ -368,16 +392,16 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box
   return 0;
 }
 
-template <int UN, bool FP8>
+template <int UN, bool FP8, int RING_KB>
 static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmEpilogue& ep, dim3 grid,
                        cudaStream_t stream) {
   constexpr int STAGE_BYTES = (UM + UN) * SLICE_BYTES;
-  constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
+  constexpr int STAGES = (RING_KB * 1024 / STAGE_BYTES) > 8 ? 8 : (RING_KB * 1024 / STAGE_BYTES);
   constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
   static_assert(UN * UM * 4 <= STAGES * STAGE_BYTES, "the split-K partial tile must fit in the idle ring");
   static bool configured = false;  // per instantiation; the attribute is per function, set once
   if (!configured) {
-    const cudaError_t rc = cudaFuncSetAttribute(gemm_tcgen05_kernel<UN, FP8>,
+    const cudaError_t rc = cudaFuncSetAttribute(gemm_tcgen05_kernel<UN, FP8, RING_KB>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     CGYM_REQUIRE(rc == cudaSuccess, "gemm: cannot reserve %d bytes of shared memory: %s", SMEM, cudaGetErrorString(rc));
     configured = true;
@@ -403,10 +427,20 @@ static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
   }
   config.attrs = attrs;
   config.numAttrs = n_attrs;
-  const cudaError_t rc = cudaLaunchKernelEx(&config, gemm_tcgen05_kernel<UN, FP8>, mw, mx, ep);
+  const cudaError_t rc = cudaLaunchKernelEx(&config, gemm_tcgen05_kernel<UN, FP8, RING_KB>, mw, mx, ep);
   CGYM_REQUIRE(rc == cudaSuccess, "gemm(tcgen05): launch failed: %s", cudaGetErrorString(rc));
   return 0;
 }
+
+#ifdef CGYM_TRACE
+static unsigned long long* g_trace_buffer = nullptr;
+static int g_trace_launch = 0;
+extern "C" int cgym_debug_trace(void* buffer) {  // 512 launches x 512 CTAs x 4 stamps of u64
+  g_trace_buffer = static_cast<unsigned long long*>(buffer);
+  g_trace_launch = 0;
+  return 0;
+}
+#endif
 
 bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const void* w) {
   const int elem = fp8 ? 1 : 2;
@@ -425,13 +459,23 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   const int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
   const int n_tiles = (N + UM - 1) / UM, m_tiles = (M + un - 1) / un;
   const int total_kb = (K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
-  // split-K only where the output tiles alone cannot fill the GPU; at most 8 (portable cluster size)
+  // decode-sized token tiles take the half-SM ring (two CTAs per SM), larger ones the full ring
+  bool half_ring = un <= 64;
+  if (const char* forced = std::getenv("CGYM_GEMM_RING_KB")) half_ring = un <= 128 && std::atoi(forced) <= 96;  // tuning aid
+  // Split-K until the CTAs fill the GPU's resident slots (at most 8: the portable cluster size). A
+  // weight stream is bound by the bytes in flight, i.e. by how many rings are filling at once, so a
+  // decode GEMM wants about two CTAs on every SM, each owning as little as one ring of K slices.
+  static const int min_kb = [] {  // tuning aid: fewest K slices per split
+    const char* v = std::getenv("CGYM_GEMM_MIN_KB");
+    return v != nullptr && std::atoi(v) > 0 ? std::atoi(v) : 4;
+  }();
   int splits = 1;
   if (force_splits > 0) {
     splits = force_splits;
-  } else if (n_tiles * m_tiles <= 32 && total_kb >= 16) {
-    splits = 148 / (n_tiles * m_tiles);
-    if (splits > total_kb / 8) splits = total_kb / 8;  // at least eight K slices (1 KB of each row) per split
+  } else {
+    const int slots = half_ring ? 2 * 148 : 148;
+    splits = slots / (n_tiles * m_tiles);
+    if (splits > total_kb / min_kb) splits = total_kb / min_kb;
   }
   if (const char* forced = std::getenv("CGYM_GEMM_SPLITS")) {  // tuning aid: force a split count (1 = off)
     const int v = std::atoi(forced);
@@ -450,13 +494,16 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   if (int rc = make_map(&mx, x, M, K, un, fp8)) return rc;
   GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0};
   dim3 grid(n_tiles, m_tiles, splits);
+#ifdef CGYM_TRACE
+  ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 2048ull : nullptr;
+#endif
   int rc = 0;
-#define LAUNCH_UN(U)                                                              \
-  rc = fp8 ? launch_tile<U, true>(mw, mx, ep, grid, stream) : launch_tile<U, false>(mw, mx, ep, grid, stream)
-  if (un == 32) LAUNCH_UN(32);
-  else if (un == 64) LAUNCH_UN(64);
-  else if (un == 128) LAUNCH_UN(128);
-  else LAUNCH_UN(256);
+#define LAUNCH_UN(U, R)                                                                 \
+  rc = fp8 ? launch_tile<U, true, R>(mw, mx, ep, grid, stream) : launch_tile<U, false, R>(mw, mx, ep, grid, stream)
+  if (un == 32) { if (half_ring) LAUNCH_UN(32, 96); else LAUNCH_UN(32, 192); }
+  else if (un == 64) { if (half_ring) LAUNCH_UN(64, 96); else LAUNCH_UN(64, 192); }
+  else if (un == 128) { if (half_ring) LAUNCH_UN(128, 96); else LAUNCH_UN(128, 192); }
+  else LAUNCH_UN(256, 192);
 #undef LAUNCH_UN
   if (rc) return rc;
   return check_launch("gemm_tcgen05");

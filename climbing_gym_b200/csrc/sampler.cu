@@ -76,8 +76,8 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
               float* __restrict__ logp_out, int vocab, float* __restrict__ workspace) {
   __shared__ Pick s_pick[SAMPLE_THREADS / 32];
   __shared__ int s_last;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x, part = blockIdx.y, parts = gridDim.y;
   if (has_state) {
     if (threadIdx.x == 0 && part == 0 && advance != nullptr && advance[row]) st.seq_lens[row] += 1;
