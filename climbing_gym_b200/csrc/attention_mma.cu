@@ -267,6 +267,8 @@ __device__ __forceinline__ void stage_block(uint32_t dst, uint32_t bar, const ui
 }
 
 // ------------------------------------------------------------------------------------------ decode
+constexpr int DECODE_STAGES = 3;  // 4 warps x 3 pages x 16 KB (bf16) = 192 KB of KV in flight per SM
+
 template <typename TQ, int EB, int D, int P>
 __global__ void __launch_bounds__(128, 1)
 decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, const int32_t* __restrict__ kv_lens,
@@ -276,7 +278,8 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   using Geo = BlockGeom<EB, D, P>;
   constexpr int OT = D / 8;
   extern __shared__ __align__(128) uint8_t att_smem[];
-  __shared__ __align__(8) uint64_t bars[4][2];
+  constexpr int NST = DECODE_STAGES;  // pages in flight per warp
+  __shared__ __align__(8) uint64_t bars[4][NST];
   __shared__ int abort_flag;
   pdl_trigger();
   pdl_wait();     // q, the new K/V row and the block table come from the kernels just before
@@ -288,7 +291,8 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   if ((active != nullptr && !active[row]) || slot < 0 || len < 0) len = 0;
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int w = 0; w < 4; ++w) { att_bar_init(att_smem_u32(&bars[w][0]), 1); att_bar_init(att_smem_u32(&bars[w][1]), 1); }
+    for (int w = 0; w < 4; ++w)
+      for (int st = 0; st < NST; ++st) att_bar_init(att_smem_u32(&bars[w][st]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -299,7 +303,7 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   const int n_mine = (page_end - page_begin - warp + 3) / 4;  // pages page_begin + warp + 4 i
   const int32_t* table = kv.block_table + static_cast<int64_t>(slot < 0 ? 0 : slot) * kv.max_blocks;
   const uint8_t* pool = static_cast<const uint8_t*>(kv.kv_pool);
-  const uint32_t ring = att_smem_u32(att_smem) + warp * 2 * Geo::STAGE_BYTES;
+  const uint32_t ring = att_smem_u32(att_smem) + warp * NST * Geo::STAGE_BYTES;
 
   uint32_t qa[D / 16][4];
   load_q_frags<EB, D, TQ>(qa, q + static_cast<int64_t>(row) * n_q_heads * D, lane >> 2, (lane >> 2) + 8, G, G,
@@ -313,22 +317,23 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
     if (lane == 0) {
       int page = table[page_begin + warp + 4 * i];
       if (page < 0 || page >= kv.n_pages) { atomicOr(status, CGYM_STATUS_BAD_PAGE); page = 0; }
-      stage_block(ring + (i & 1) * Geo::STAGE_BYTES, att_smem_u32(&bars[warp][i & 1]), pool, kv.kv_scales,
+      stage_block(ring + (i % NST) * Geo::STAGE_BYTES, att_smem_u32(&bars[warp][i % NST]), pool, kv.kv_scales,
                   kv_block_offset(kv, layer, page, kh) * EB, kv_scale_offset(kv, layer, page, 0, kh, 0),
                   Geo::BLOCK_BYTES, Geo::SCALE_BYTES);
     }
   };
-  if (n_mine > 0) issue(0);
-  int issued = n_mine > 0 ? 1 : 0;
+  int issued = 0;
+  for (; issued < n_mine && issued < NST; ++issued) issue(issued);  // fill the warp's ring
   for (int i = 0; i < n_mine; ++i) {
-    if (i + 1 < n_mine) { issue(i + 1); issued = i + 2; }
-    if (!att_bar_wait(att_smem_u32(&bars[warp][i & 1]), (i >> 1) & 1, &abort_flag)) break;
+    if (!att_bar_wait(att_smem_u32(&bars[warp][i % NST]), (i / NST) & 1, &abort_flag)) break;
     const int token0 = (page_begin + warp + 4 * i) * P;
-    attend_page<EB, D, P>(qa, o, m, l, ring + (i & 1) * Geo::STAGE_BYTES, token0, len, len, scale_log2, lane);
+    attend_page<EB, D, P>(qa, o, m, l, ring + (i % NST) * Geo::STAGE_BYTES, token0, len, len, scale_log2, lane);
     __syncwarp();  // every lane is done reading this stage before lane 0 refills it
+    if (issued < n_mine) { issue(issued); ++issued; }
   }
   if (abort_flag && lane == 0) {  // let copies in flight land before shared memory is reused / released
-    for (int i = max(0, issued - 2); i < issued; ++i) att_bar_wait(att_smem_u32(&bars[warp][i & 1]), (i >> 1) & 1, &abort_flag);
+    for (int i = max(0, issued - NST); i < issued; ++i)
+      att_bar_wait(att_smem_u32(&bars[warp][i % NST]), (i / NST) & 1, &abort_flag);
   }
   __syncthreads();
   if (threadIdx.x == 0 && abort_flag) atomicOr(status, CGYM_STATUS_WAIT_TIMEOUT);
@@ -516,7 +521,7 @@ static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const
                          float* workspace, int32_t* status, cudaStream_t stream) {
   using T = __nv_bfloat16;
   using Geo = BlockGeom<EB, D, 64>;
-  constexpr int ring = 4 * 2 * Geo::STAGE_BYTES, merge = (4 * 16 * D + 2 * 4 * 16) * 4;
+  constexpr int ring = 4 * DECODE_STAGES * Geo::STAGE_BYTES, merge = (4 * 16 * D + 2 * 4 * 16) * 4;
   constexpr int smem = ring > merge ? ring : merge;
   auto kernel = decode_attention_mma_kernel<T, EB, D, 64>;
   static bool configured = false;

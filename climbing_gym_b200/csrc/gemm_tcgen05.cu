@@ -127,7 +127,7 @@ struct GemmEpilogue {
   int M, N, K;
   int partial;             // 1: split-K over a cluster of gridDim.z CTAs, reduced through DSMEM
 #ifdef CGYM_TRACE
-  unsigned long long* trace;  // [ctas <= 512][4] globaltimer stamps of this launch (debug builds only)
+  unsigned long long* trace;  // [ctas <= 512][8] globaltimer stamps of this launch (debug builds only)
 #endif
 };
 
@@ -138,47 +138,79 @@ __device__ __forceinline__ void trace_stamp(const GemmEpilogue& ep, int which) {
   if (cta >= 512u) return;
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  ep.trace[cta * 4 + which] = t;
+  ep.trace[cta * 8 + which] = t;
 }
 #define CGYM_STAMP(which) trace_stamp(ep, which)
 #else
 #define CGYM_STAMP(which)
 #endif
 
-// Cluster split-K reduction for one output feature (column of the parked [UN][128] fp32 tiles):
-// CTA `rank` owns token rows ml = rank, rank + SPLITS, ... and sums the SPLITS peers' values in split
-// order. All remote (distributed shared memory) loads of a batch are issued before the first add, so
-// a thread waits for about one remote round trip per 64 values.
+// Cluster split-K reduction of the parked [UN][128] fp32 tiles. CTA `rank` owns the token rows
+// ml = rank, rank + SPLITS, ...; epilogue warp `quarter` takes every fourth of them, and one 16-byte
+// load per lane fetches a whole 128-feature row of one peer's tile over distributed shared memory
+// (lane l holds features 4l .. 4l+3). All loads of a thread are issued before the first add; the
+// sum runs in split order, so the result does not depend on timing.
 template <int SPLITS, int UN>
-__device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint32_t column, uint32_t rank, int m0,
-                                                    int n, float ws) {
-  constexpr int ROWS = UN / SPLITS;                      // rows this CTA reduces
-  constexpr int BATCH = ROWS * SPLITS <= 64 ? ROWS : 64 / SPLITS;
+__device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint32_t tile, uint32_t rank, int quarter,
+                                                    int lane, int m0, int n0) {
+  constexpr int ROWS = UN / SPLITS;  // rows this CTA reduces (a multiple of 4: UN >= 32, SPLITS <= 8)
+  constexpr int MINE = ROWS / 4;     // rows per warp
+  static_assert(ROWS % 4 == 0, "each epilogue warp reduces ROWS / 4 rows");
+  const uint32_t column = tile + static_cast<uint32_t>(lane) * 16u;
   uint32_t peer[SPLITS];
 #pragma unroll
   for (int sp = 0; sp < SPLITS; ++sp)
     asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer[sp]) : "r"(column), "r"(sp));
+  const int n = n0 + 4 * lane;
+  float ws[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+  if (ep.w_scales != nullptr)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ws[j] = n + j < ep.N ? ep.w_scales[n + j] : 1.0f;
+  constexpr int BATCH = MINE * SPLITS <= 16 ? MINE : 16 / SPLITS;  // at most 16 loads of 16 bytes in flight
 #pragma unroll 1
-  for (int first = 0; first < ROWS; first += BATCH) {
-    float value[BATCH][SPLITS];
+  for (int first = 0; first < MINE; first += BATCH) {
+  float4 value[BATCH][SPLITS];
 #pragma unroll
-    for (int b = 0; b < BATCH; ++b) {
-      const uint32_t ml = rank + static_cast<uint32_t>(first + b) * SPLITS;
+  for (int b = 0; b < BATCH; ++b) {
+    const int i = first + b;
+    const uint32_t ml = rank + static_cast<uint32_t>(quarter + 4 * i) * SPLITS;
 #pragma unroll
-      for (int sp = 0; sp < SPLITS; ++sp)
-        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(value[b][sp]) : "r"(peer[sp] + ml * (UM * 4u)));
+    for (int sp = 0; sp < SPLITS; ++sp)
+      asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(value[b][sp].x), "=f"(value[b][sp].y), "=f"(value[b][sp].z), "=f"(value[b][sp].w)
+                   : "r"(peer[sp] + ml * (UM * 4u)));
+  }
+#pragma unroll
+  for (int b = 0; b < BATCH; ++b) {
+    const int i = first + b;
+    const int m = m0 + static_cast<int>(rank) + (quarter + 4 * i) * SPLITS;
+    if (m >= ep.M) continue;
+    if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
+    float total[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int sp = 0; sp < SPLITS; ++sp) {
+      total[0] = __fadd_rn(total[0], value[b][sp].x);
+      total[1] = __fadd_rn(total[1], value[b][sp].y);
+      total[2] = __fadd_rn(total[2], value[b][sp].z);
+      total[3] = __fadd_rn(total[3], value[b][sp].w);
     }
+    if (ep.x_scales != nullptr) {
+      const float xs = ep.x_scales[m];
 #pragma unroll
-    for (int b = 0; b < BATCH; ++b) {
-      const int m = m0 + static_cast<int>(rank) + (first + b) * SPLITS;
-      if (m >= ep.M) continue;
-      if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
-      float total = 0.0f;
-#pragma unroll
-      for (int sp = 0; sp < SPLITS; ++sp) total = __fadd_rn(total, value[b][sp]);
-      if (ep.x_scales != nullptr) total = __fmul_rn(__fmul_rn(total, ep.x_scales[m]), ws);
-      ep.y[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(total);
+      for (int j = 0; j < 4; ++j) total[j] = __fmul_rn(__fmul_rn(total[j], xs), ws[j]);
     }
+    __nv_bfloat16* dst = ep.y + static_cast<int64_t>(m) * ep.N + n;
+    if (n + 3 < ep.N && (ep.N & 3) == 0) {
+      uint2 packed;
+      *reinterpret_cast<__nv_bfloat162*>(&packed.x) = __floats2bfloat162_rn(total[0], total[1]);
+      *reinterpret_cast<__nv_bfloat162*>(&packed.y) = __floats2bfloat162_rn(total[2], total[3]);
+      *reinterpret_cast<uint2*>(dst) = packed;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (n + j < ep.N) dst[j] = __float2bfloat16_rn(total[j]);
+    }
+  }
   }
 }
 
@@ -331,22 +363,21 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     // split order, the token rows m with m % splits == r straight out of its peers' shared memory
     // (distributed shared memory), applies scales / mask and writes y. Deterministic, no HBM round trip.
     __syncwarp();  // the producer / MMA lanes rejoin their warps before the aligned cluster barrier
+    if (warp == 2 && lane == 0) CGYM_STAMP(4);
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (warp == 2 && lane == 0) CGYM_STAMP(5);
     if (warp >= 2) {
       const int quarter = warp & 3;
-      const int n_local = quarter * 32 + lane, n = n0 + n_local;
       const uint32_t splits = gridDim.z, rank = blockIdx.z;
-      const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
-      if (n < ep.N) {
-        const uint32_t column = tiles + static_cast<uint32_t>(n_local) * 4u;
-        if (splits == 2) cluster_reduce_rows<2, UN>(ep, column, rank, m0, n, ws);
-        else if (splits == 4) cluster_reduce_rows<4, UN>(ep, column, rank, m0, n, ws);
-        else cluster_reduce_rows<8, UN>(ep, column, rank, m0, n, ws);
-      }
+      if (splits == 2) cluster_reduce_rows<2, UN>(ep, tiles, rank, quarter, lane, m0, n0);
+      else if (splits == 4) cluster_reduce_rows<4, UN>(ep, tiles, rank, quarter, lane, m0, n0);
+      else cluster_reduce_rows<8, UN>(ep, tiles, rank, quarter, lane, m0, n0);
     }
     // nobody leaves (and frees its shared memory) while a peer may still be reading it
     __syncwarp();
+    if (warp == 2 && lane == 0) CGYM_STAMP(6);
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (warp == 2 && lane == 0) CGYM_STAMP(7);
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -475,6 +506,13 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   } else {
     const int slots = half_ring ? 2 * 148 : 148;
     splits = slots / (n_tiles * m_tiles);
+    // Output tiles that already cover most SMs stream near the HBM rate unsplit; splitting them would
+    // only add the cluster reduction and take the slots where the next GEMM's CTAs prefetch.
+    static const int unsplit_tiles = [] {  // tuning aid
+      const char* v = std::getenv("CGYM_GEMM_UNSPLIT_TILES");
+      return v != nullptr && std::atoi(v) > 0 ? std::atoi(v) : 100;
+    }();
+    if (n_tiles * m_tiles >= unsplit_tiles) splits = 1;
     if (splits > total_kb / min_kb) splits = total_kb / min_kb;
   }
   if (const char* forced = std::getenv("CGYM_GEMM_SPLITS")) {  // tuning aid: force a split count (1 = off)
@@ -495,7 +533,7 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0};
   dim3 grid(n_tiles, m_tiles, splits);
 #ifdef CGYM_TRACE
-  ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 2048ull : nullptr;
+  ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 4096ull : nullptr;
 #endif
   int rc = 0;
 #define LAUNCH_UN(U, R)                                                                 \
