@@ -23,6 +23,14 @@ __global__ void embedding_kernel(T* __restrict__ out, const T* __restrict__ tabl
   if (tok < 0 || tok >= vocab) tok = 0;  // padding rows carry arbitrary ids; never index outside the table
   const T* src = table + tok * hidden;
   T* dst = out + static_cast<int64_t>(row) * hidden;
+  const size_t row_bytes = static_cast<size_t>(hidden) * sizeof(T);
+  if (row_bytes % 16 == 0 && ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0) {
+    // 16-byte copies: a 4 KB row is one load per thread, i.e. one memory round trip
+    const uint4* src16 = reinterpret_cast<const uint4*>(src);
+    uint4* dst16 = reinterpret_cast<uint4*>(dst);
+    for (int i = threadIdx.x; i < static_cast<int>(row_bytes / 16); i += blockDim.x) dst16[i] = __ldg(src16 + i);
+    return;
+  }
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = src[i];
 }
 
@@ -215,6 +223,25 @@ __global__ void swiglu_kernel(T* __restrict__ y, const T* __restrict__ gate_up, 
   const float gate = Elem<T>::load(gate_up + row * 2 * ffn + col);
   const float up = Elem<T>::load(gate_up + row * 2 * ffn + ffn + col);
   Elem<T>::store(y + row * ffn + col, swiglu_value<T>(gate, up));
+}
+
+// bf16 fast path: eight columns per thread, 16-byte loads and stores (ffn a multiple of 8, 16-byte
+// aligned rows)
+__global__ void __launch_bounds__(256)
+swiglu_rows_bf16_kernel(__nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ gate_up, int ffn) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t row = blockIdx.y;
+  const int chunk = blockIdx.x * blockDim.x + threadIdx.x;  // 8 columns
+  if (chunk * 8 >= ffn) return;
+  const uint4 g_raw = *(reinterpret_cast<const uint4*>(gate_up + row * 2 * ffn) + chunk);
+  const uint4 u_raw = *(reinterpret_cast<const uint4*>(gate_up + row * 2 * ffn + ffn) + chunk);
+  float g[8], u[8];
+  unpack8(g_raw, g);
+  unpack8(u_raw, u);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) g[j] = swiglu_value<__nv_bfloat16>(g[j], u[j]);
+  *(reinterpret_cast<uint4*>(y + row * ffn) + chunk) = pack8(g);
 }
 
 template <typename T>
@@ -489,6 +516,13 @@ extern "C" int cgym_rmsnorm_quant(uint8_t* q, float* scales, void* sum_out, cons
 extern "C" int cgym_swiglu(void* y, const void* gate_up, int rows, int ffn, int dtype, cgym_stream_t stream) {
   CGYM_REQUIRE(rows >= 0 && ffn > 0, "swiglu: bad shape");
   if (rows == 0) return 0;
+  if (dtype == CGYM_BF16 && ffn % 8 == 0 && rows <= 65535 &&
+      ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(gate_up)) & 15u) == 0) {
+    using B = __nv_bfloat16;
+    launch_dependent(swiglu_rows_bf16_kernel, dim3((ffn / 8 + 255) / 256, rows), dim3(256), 0, as_stream(stream),
+                     static_cast<B*>(y), static_cast<const B*>(gate_up), ffn);
+    return check_launch("swiglu");
+  }
   dim3 grid((ffn + 255) / 256, rows);
   DISPATCH_DTYPE(dtype, launch_dependent(swiglu_kernel<T>, grid, dim3(256), 0, as_stream(stream), static_cast<T*>(y),
                                          static_cast<const T*>(gate_up), ffn));

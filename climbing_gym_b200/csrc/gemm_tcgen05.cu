@@ -506,13 +506,6 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   } else {
     const int slots = half_ring ? 2 * 148 : 148;
     splits = slots / (n_tiles * m_tiles);
-    // Output tiles that already cover most SMs stream near the HBM rate unsplit; splitting them would
-    // only add the cluster reduction and take the slots where the next GEMM's CTAs prefetch.
-    static const int unsplit_tiles = [] {  // tuning aid
-      const char* v = std::getenv("CGYM_GEMM_UNSPLIT_TILES");
-      return v != nullptr && std::atoi(v) > 0 ? std::atoi(v) : 100;
-    }();
-    if (n_tiles * m_tiles >= unsplit_tiles) splits = 1;
     if (splits > total_kb / min_kb) splits = total_kb / min_kb;
   }
   if (const char* forced = std::getenv("CGYM_GEMM_SPLITS")) {  // tuning aid: force a split count (1 = off)

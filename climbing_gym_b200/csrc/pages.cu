@@ -47,7 +47,8 @@ __global__ void __launch_bounds__(POOL_THREADS)
 pages_reserve_kernel(cgym_page_pool pool, const int32_t* __restrict__ slot_ids,
                      const int32_t* __restrict__ need_tokens, const int32_t* __restrict__ seq_lens,
                      const uint8_t* __restrict__ active, const uint8_t* __restrict__ pending_in,
-                     uint8_t* __restrict__ active_out, int n, int32_t* __restrict__ status) {
+                     uint8_t* __restrict__ active_out, int32_t* __restrict__ kv_lens_out, int n,
+                     int32_t* __restrict__ status) {
   __shared__ int s_excl[POOL_THREADS + 1];
   __shared__ int s_old[POOL_THREADS];
   __shared__ int s_slot[POOL_THREADS];
@@ -63,6 +64,8 @@ pages_reserve_kernel(cgym_page_pool pool, const int32_t* __restrict__ slot_ids,
       act = active[e] != 0;
     }
     slot = slot_ids != nullptr ? slot_ids[e] : e;
+    // attention length of the row this step: its cached tokens plus the one being appended
+    if (kv_lens_out != nullptr) kv_lens_out[e] = (slot >= 0 && slot < pool.n_slots) ? seq_lens[slot] + 1 : 0;
     if (act && slot >= 0 && slot < pool.n_slots) {
       const int need = need_tokens != nullptr ? need_tokens[e] : seq_lens[slot] + 1;
       int target = (need + pool.page_size - 1) / pool.page_size;
@@ -246,14 +249,14 @@ static int check_pool(const cgym_page_pool* pool) {
 using namespace cgym;
 
 extern "C" int cgym_step_begin(const cgym_page_pool* pool, const int32_t* seq_lens, const uint8_t* pending,
-                               uint8_t* active_out, const uint8_t* active, const int32_t* slots, int rows,
-                               int32_t* status, cgym_stream_t stream) {
+                               uint8_t* active_out, const uint8_t* active, const int32_t* slots,
+                               int32_t* kv_lens_out, int rows, int32_t* status, cgym_stream_t stream) {
   if (int rc = check_pool(pool)) return rc;
   CGYM_REQUIRE(seq_lens != nullptr && status != nullptr, "step_begin: seq_lens and status are required");
   CGYM_REQUIRE(rows >= 0 && rows <= POOL_THREADS, "step_begin: at most 1024 rows per step");
   if (rows == 0) return 0;
   pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, slots, nullptr, seq_lens, active, pending,
-                                                                  active_out, rows, status);
+                                                                  active_out, kv_lens_out, rows, status);
   return check_launch("step_begin");
 }
 
@@ -265,7 +268,8 @@ extern "C" int cgym_pages_reserve(const cgym_page_pool* pool, const int32_t* slo
   for (int done = 0; done < n; done += POOL_THREADS) {
     const int m = n - done < POOL_THREADS ? n - done : POOL_THREADS;
     pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, slot_ids + done, need_tokens + done,
-                                                                    nullptr, nullptr, nullptr, nullptr, m, status);
+                                                                    nullptr, nullptr, nullptr, nullptr, nullptr, m,
+                                                                    status);
   }
   return check_launch("pages_reserve", (n + POOL_THREADS - 1) / POOL_THREADS);
 }
@@ -287,7 +291,7 @@ extern "C" int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout*
   if (n == 0) return 0;
   pages_share_kernel<<<n, 128, 0, as_stream(stream)>>>(*pool, src_slots, dst_slots, prefix_lens);
   pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, dst_slots, prefix_lens, nullptr, nullptr,
-                                                                  nullptr, nullptr, n, status);
+                                                                  nullptr, nullptr, nullptr, n, status);
   dim3 grid(n, n_layers * kv->n_kv_heads);
   if (kv->kv_dtype == CGYM_F32) pages_copy_tail_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);
   else if (kv->kv_dtype == CGYM_BF16) pages_copy_tail_kernel<__nv_bfloat16><<<grid, 256, 0, as_stream(stream)>>>(*pool, *kv, src_slots, dst_slots, prefix_lens);

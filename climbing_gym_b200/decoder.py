@@ -188,9 +188,10 @@ class B200Decoder:
         cache, state = entry.cache, entry.state
         n = cache.n_slots
         stream = nv.stream_ptr(self.engine.device)
+        kv_lens = self.runner.kv_lens_buffer(cache)
         nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(state.pending), nv.ptr(state.active),
-                None, None, n, nv.ptr(cache.status), stream)
-        self.runner.decode_step(entry.bufs, cache, state.input_tokens, state.active, entry.logits)
+                None, None, nv.ptr(kv_lens), n, nv.ptr(cache.status), stream)
+        self.runner.decode_step(entry.bufs, cache, state.input_tokens, state.active, entry.logits, kv_lens=kv_lens)
         nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(state.struct), nv.ptr(state.active), None, None,
                 n, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype), nv.ptr(state.sample_ws), stream)
 

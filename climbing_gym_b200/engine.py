@@ -467,9 +467,10 @@ class LFM25Engine:
         bufs = ForwardBuffers(self.weights, cache.max_slots, fp8=runner.fp8_mlp or runner.fp8_lm_head)
         active = torch.ones(cache.max_slots, device=dev, dtype=torch.uint8)
         logits = torch.empty((cache.max_slots, self.config.vocab_size), device=dev, dtype=self.dtype)
+        kv_lens = runner.kv_lens_buffer(cache)
         nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), None, None, nv.ptr(active), None,
-                cache.max_slots, nv.ptr(cache.status), nv.stream_ptr(dev))
-        runner.decode_step(bufs, cache, tokens, active, logits)
+                nv.ptr(kv_lens), cache.max_slots, nv.ptr(cache.status), nv.stream_ptr(dev))
+        runner.decode_step(bufs, cache, tokens, active, logits, kv_lens=kv_lens)
         cache.seq_lens.add_(1)
         n = cache.max_slots
         out_tokens = torch.empty(n, device=dev, dtype=torch.int64)

@@ -178,15 +178,17 @@ class LFM25Runner:
 
     # ---- public sequences ------------------------------------------------------------------------------
     def decode_step(self, bufs: ForwardBuffers, cache: PagedHybridCache, tokens, active, logits, *, slots=None,
-                    rows: int | None = None) -> None:
+                    rows: int | None = None, kv_lens=None) -> None:
         """One token per row. Rows with active == 0 leave KV, conv taps and their logits row untouched.
-        positions are the slots' current seq_lens; the caller advances seq_lens afterwards."""
+        positions are the slots' current seq_lens; the caller advances seq_lens afterwards.
+        kv_lens: the per-row attention lengths cgym_step_begin wrote (seq_lens + 1); computed here with
+        a torch op when the caller did not ask step_begin for them."""
         rows = tokens.numel() if rows is None else rows
         self._embed(bufs, tokens, rows)
-        # a decode row at cache length L writes position L and then attends to L + 1 tokens; the
-        # attention kernel gets kv_lens = seq_lens + 1 through the precomputed view below
+        # a decode row at cache length L writes position L and then attends to L + 1 tokens
         positions = cache.seq_lens if slots is None else bufs_positions(cache, slots)
-        kv_lens = self._kv_lens_plus_one(cache, positions)
+        if kv_lens is None:
+            kv_lens = self._kv_lens_plus_one(cache, positions)
         x, residual = self._layers(bufs, cache, rows, decode=True, positions=positions, slots=slots, active=active,
                                    kv_lens=kv_lens)
         if self.fp8_lm_head:
@@ -195,12 +197,18 @@ class LFM25Runner:
             self._rmsnorm(bufs.final, x, self.weights.embedding_norm_weight, rows, residual, bufs.residual)
         self._head(bufs, logits, bufs.final, rows, cache.status, row_mask=active)
 
-    def _kv_lens_plus_one(self, cache, positions):
-        # torch op on a tiny int32 vector (capturable); keeps the attention ABI "attend to [0, kv_len)"
+    @staticmethod
+    def kv_lens_buffer(cache) -> torch.Tensor:
+        """int32 [slots] scratch for the per-row attention lengths of a decode step."""
         if not hasattr(cache, "_kv_lens"):
             cache._kv_lens = torch.empty_like(cache.seq_lens)
-        torch.add(positions, 1, out=cache._kv_lens[:positions.numel()])
         return cache._kv_lens
+
+    def _kv_lens_plus_one(self, cache, positions):
+        # torch op on a tiny int32 vector (capturable); keeps the attention ABI "attend to [0, kv_len)"
+        out = self.kv_lens_buffer(cache)
+        torch.add(positions, 1, out=out[:positions.numel()])
+        return out
 
     def prefill_chunk(self, bufs: ForwardBuffers, cache: PagedHybridCache, tokens, positions, token_slots, kv_lens,
                       cu_seqlens, seq_slots, seq_starts, n_seqs: int, rows: int, *, last_rows=None, logits=None,

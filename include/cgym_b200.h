@@ -252,10 +252,12 @@ typedef struct {
 /* Start of a decode step, inside the graph: snapshots pending -> active_out (the rows whose input
  * token is consumed this step, lfm25_session.py:467) when `pending` is given, else uses `active`;
  * then every active row whose next position (seq_lens[slot]) needs a page it does not hold yet
- * gets the lowest free page, rows served in row order. At most 1024 rows. */
+ * gets the lowest free page, rows served in row order. kv_lens_out (int32[rows], optional) receives
+ * each row's attention length for this step, seq_lens[slot] + 1 (the cache_seqlens + new token of
+ * flash_attn_with_kvcache, lfm25_cuda.py:156-165). At most 1024 rows. */
 int cgym_step_begin(const cgym_page_pool* pool, const int32_t* seq_lens, const uint8_t* pending,
-                    uint8_t* active_out, const uint8_t* active, const int32_t* slots, int rows,
-                    int32_t* status, cgym_stream_t stream);
+                    uint8_t* active_out, const uint8_t* active, const int32_t* slots,
+                    int32_t* kv_lens_out, int rows, int32_t* status, cgym_stream_t stream);
 
 /* Reserve pages so slot s can hold need_tokens[s] tokens (admission / prefill chunk).
  * No reference counterpart (the reference allocates slots x capacity up front). */

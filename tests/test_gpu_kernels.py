@@ -354,9 +354,11 @@ def test_page_allocator_trace_matches_oracle(dev):
     # decode steps: slot 2 crosses a page boundary at once, slot 3 after 15 more tokens
     pending = t([1, 0, 1, 1, 0, 0], torch.uint8)
     active = torch.zeros(slots, device=dev, dtype=torch.uint8)
+    kv_lens = torch.full((slots,), -7, device=dev, dtype=torch.int32)
     for _ in range(20):
         nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(pending), nv.ptr(active), None, None,
-                slots, nv.ptr(cache.status), stream())
+                nv.ptr(kv_lens), slots, nv.ptr(cache.status), stream())
+        assert kv_lens.cpu().tolist() == (cache.seq_lens + 1).cpu().tolist()
         oracle.step([1, 0, 1, 1, 0, 0])
         cache.seq_lens += pending.int()
         oracle.seq_lens += np.array([1, 0, 1, 1, 0, 0], np.int32)
