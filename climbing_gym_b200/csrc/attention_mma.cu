@@ -267,10 +267,11 @@ __device__ __forceinline__ void stage_block(uint32_t dst, uint32_t bar, const ui
 }
 
 // ------------------------------------------------------------------------------------------ decode
-constexpr int DECODE_STAGES = 3;  // 4 warps x 3 pages x 16 KB (bf16) = 192 KB of KV in flight per SM
-
-template <typename TQ, int EB, int D, int P>
-__global__ void __launch_bounds__(128, 1)
+// NST = pages in flight per warp. A CTA spends about 3 us outside its page loop (q and block-table
+// fetch, first page latency, merge, store), so the SM is better used by several short-ring CTAs whose
+// fixed phases overlap than by one CTA with a deep ring: NST = 1 -> 64 KB (bf16) and 3 CTAs per SM.
+template <typename TQ, int EB, int D, int P, int NST>
+__global__ void __launch_bounds__(128, NST == 1 ? 3 : 1)
 decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, const int32_t* __restrict__ kv_lens,
                             const int32_t* __restrict__ slots, const uint8_t* __restrict__ active,
                             cgym_kv_layout kv, int layer, int n_q_heads, float scale, int n_splits,
@@ -278,11 +279,13 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   using Geo = BlockGeom<EB, D, P>;
   constexpr int OT = D / 8;
   extern __shared__ __align__(128) uint8_t att_smem[];
-  constexpr int NST = DECODE_STAGES;  // pages in flight per warp
   __shared__ __align__(8) uint64_t bars[4][NST];
   __shared__ int abort_flag;
   pdl_trigger();
-  pdl_wait();     // q, the new K/V row and the block table come from the kernels just before
+  // Under programmatic dependent launch this CTA may run before the kernel just ahead of it (the
+  // QK-norm / RoPE / append) has finished. That kernel writes q and ONE cache position per row, in
+  // the row's last page; kv_lens, slots, active and the block table are fixed since the start of the
+  // step. So the pages before the last one are fetched right away and only q and the last page wait.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int G = n_q_heads / kv.n_kv_heads;
@@ -305,14 +308,6 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   const uint8_t* pool = static_cast<const uint8_t*>(kv.kv_pool);
   const uint32_t ring = att_smem_u32(att_smem) + warp * NST * Geo::STAGE_BYTES;
 
-  uint32_t qa[D / 16][4];
-  load_q_frags<EB, D, TQ>(qa, q + static_cast<int64_t>(row) * n_q_heads * D, lane >> 2, (lane >> 2) + 8, G, G,
-                          n_q_heads, kh * G, lane);
-  float o[OT][4], m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-#pragma unroll
-  for (int u = 0; u < OT; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.f;
-  const float scale_log2 = scale * 1.4426950408889634f;
-
   auto issue = [&](int i) {
     if (lane == 0) {
       int page = table[page_begin + warp + 4 * i];
@@ -323,7 +318,17 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
     }
   };
   int issued = 0;
-  for (; issued < n_mine && issued < NST; ++issued) issue(issued);  // fill the warp's ring
+  const int last_page = total_pages - 1;  // holds the position the append kernel writes this step
+  while (issued < n_mine && issued < NST && page_begin + warp + 4 * issued != last_page) issue(issued++);
+  pdl_wait();
+  uint32_t qa[D / 16][4];
+  load_q_frags<EB, D, TQ>(qa, q + static_cast<int64_t>(row) * n_q_heads * D, lane >> 2, (lane >> 2) + 8, G, G,
+                          n_q_heads, kh * G, lane);
+  float o[OT][4], m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < OT; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.f;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  for (; issued < n_mine && issued < NST; ++issued) issue(issued);  // fill the rest of the warp's ring
   for (int i = 0; i < n_mine; ++i) {
     if (!att_bar_wait(att_smem_u32(&bars[warp][i % NST]), (i / NST) & 1, &abort_flag)) break;
     const int token0 = (page_begin + warp + 4 * i) * P;
@@ -515,15 +520,15 @@ static int set_smem(K kernel, int bytes) {
   return 0;
 }
 
-template <int EB, int D>
+template <int EB, int D, int NST>
 static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots, const uint8_t* active,
                          const cgym_kv_layout* kv, int layer, int rows, int n_q_heads, float scale, int n_splits,
                          float* workspace, int32_t* status, cudaStream_t stream) {
   using T = __nv_bfloat16;
   using Geo = BlockGeom<EB, D, 64>;
-  constexpr int ring = 4 * DECODE_STAGES * Geo::STAGE_BYTES, merge = (4 * 16 * D + 2 * 4 * 16) * 4;
+  constexpr int ring = 4 * NST * Geo::STAGE_BYTES, merge = (4 * 16 * D + 2 * 4 * 16) * 4;
   constexpr int smem = ring > merge ? ring : merge;
-  auto kernel = decode_attention_mma_kernel<T, EB, D, 64>;
+  auto kernel = decode_attention_mma_kernel<T, EB, D, 64, NST>;
   static bool configured = false;
   if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
   const cudaError_t rc = launch_dependent(kernel, dim3(rows, kv->n_kv_heads, n_splits), dim3(128), smem, stream,
@@ -537,8 +542,17 @@ int launch_decode_attention_mma(void* out, const void* q, const int32_t* kv_lens
                                 const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows, int n_q_heads,
                                 float scale, int n_splits, float* workspace, int32_t* status, cudaStream_t stream) {
   const bool fp8 = kv->kv_dtype == CGYM_E4M3;
-  return fp8 ? launch_decode<1, 64>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, workspace, status, stream)
-             : launch_decode<2, 64>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, workspace, status, stream);
+  // More CTAs than one per SM: short rings, several CTAs per SM. Fewer: one deep ring per SM.
+  static const int forced = [] {  // tuning aid: CGYM_ATTN_STAGES=1|3
+    const char* v = std::getenv("CGYM_ATTN_STAGES");
+    return v != nullptr ? std::atoi(v) : 0;
+  }();
+  const bool shallow = forced ? forced == 1 : static_cast<int64_t>(rows) * kv->n_kv_heads * n_splits > 148;
+#define CGYM_DECODE(EB, NST) \
+  launch_decode<EB, 64, NST>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, workspace, status, stream)
+  if (fp8) return shallow ? CGYM_DECODE(1, 1) : CGYM_DECODE(1, 3);
+  return shallow ? CGYM_DECODE(2, 1) : CGYM_DECODE(2, 3);
+#undef CGYM_DECODE
 }
 
 template <int EB, int D>

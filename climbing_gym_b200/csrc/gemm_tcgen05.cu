@@ -125,7 +125,8 @@ struct GemmEpilogue {
   const uint8_t* row_mask; // optional
   int32_t* status;
   int M, N, K;
-  int partial;             // 1: split-K over a cluster of gridDim.z CTAs, reduced through DSMEM
+  int partial;             // 1: split-K over a cluster of gridDim.z CTAs
+  float* split_ws;         // split-K partial tiles [tile][split][UN][128] fp32; NULL = exchange through DSMEM
 #ifdef CGYM_TRACE
   unsigned long long* trace;  // [ctas <= 512][8] globaltimer stamps of this launch (debug builds only)
 #endif
@@ -138,7 +139,7 @@ __device__ __forceinline__ void trace_stamp(const GemmEpilogue& ep, int which) {
   if (cta >= 512u) return;
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  ep.trace[cta * 8 + which] = t;
+  ep.trace[cta * 16 + which] = t;
 }
 #define CGYM_STAMP(which) trace_stamp(ep, which)
 #else
@@ -150,17 +151,24 @@ __device__ __forceinline__ void trace_stamp(const GemmEpilogue& ep, int which) {
 // load per lane fetches a whole 128-feature row of one peer's tile over distributed shared memory
 // (lane l holds features 4l .. 4l+3). All loads of a thread are issued before the first add; the
 // sum runs in split order, so the result does not depend on timing.
-template <int SPLITS, int UN>
-__device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint32_t tile, uint32_t rank, int quarter,
-                                                    int lane, int m0, int n0) {
+//
+// GLOBAL = true is the same reduction with the partial tiles parked in a global fp32 workspace
+// ([split][UN][128] per output tile, L2-resident) instead of shared memory: the SM-to-SM network
+// moves about 15 GB/s per SM, an order of magnitude below what an SM draws from L2, so the exchange
+// is faster through L2 and needs no barrier after it (nobody reads a peer's shared memory).
+template <int SPLITS, int UN, bool GLOBAL>
+__device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint32_t tile, const float* ws_tile,
+                                                    uint32_t rank, int quarter, int lane, int m0, int n0) {
   constexpr int ROWS = UN / SPLITS;  // rows this CTA reduces (a multiple of 4: UN >= 32, SPLITS <= 8)
   constexpr int MINE = ROWS / 4;     // rows per warp
   static_assert(ROWS % 4 == 0, "each epilogue warp reduces ROWS / 4 rows");
   const uint32_t column = tile + static_cast<uint32_t>(lane) * 16u;
   uint32_t peer[SPLITS];
+  if (!GLOBAL) {
 #pragma unroll
-  for (int sp = 0; sp < SPLITS; ++sp)
-    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer[sp]) : "r"(column), "r"(sp));
+    for (int sp = 0; sp < SPLITS; ++sp)
+      asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer[sp]) : "r"(column), "r"(sp));
+  }
   const int n = n0 + 4 * lane;
   float ws[4] = {1.0f, 1.0f, 1.0f, 1.0f};
   if (ep.w_scales != nullptr)
@@ -175,11 +183,28 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
     const int i = first + b;
     const uint32_t ml = rank + static_cast<uint32_t>(quarter + 4 * i) * SPLITS;
 #pragma unroll
-    for (int sp = 0; sp < SPLITS; ++sp)
-      asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                   : "=f"(value[b][sp].x), "=f"(value[b][sp].y), "=f"(value[b][sp].z), "=f"(value[b][sp].w)
-                   : "r"(peer[sp] + ml * (UM * 4u)));
+    for (int sp = 0; sp < SPLITS; ++sp) {
+      if (GLOBAL)
+        value[b][sp] = __ldcg(reinterpret_cast<const float4*>(ws_tile + (static_cast<size_t>(sp) * UN + ml) * UM) + lane);
+      else
+        asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(value[b][sp].x), "=f"(value[b][sp].y), "=f"(value[b][sp].z), "=f"(value[b][sp].w)
+                     : "r"(peer[sp] + ml * (UM * 4u)));
+    }
   }
+#ifdef CGYM_TRACE
+  if (ep.trace != nullptr && quarter == 2 && lane == 0 && first == 0) {  // stamp 8: all remote loads have landed
+    float sink = 0.0f;
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b)
+#pragma unroll
+      for (int sp = 0; sp < SPLITS; ++sp) sink += value[b][sp].w;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(sink));
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (cta < 512u) ep.trace[cta * 16 + 8] = t;
+  }
+#endif
 #pragma unroll
   for (int b = 0; b < BATCH; ++b) {
     const int i = first + b;
@@ -329,7 +354,10 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (abort_flag == 0 || ep.partial) {
       const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
-      float* part = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)));  // [UN][128], ring is idle now
+      // partial tile [UN][128]: in this CTA's shared memory (the ring is idle now) or in the workspace
+      float* part = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)));
+      if (ep.partial && ep.split_ws != nullptr)
+        part = ep.split_ws + ((static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * gridDim.z + blockIdx.z) * (UN * UM);
 #pragma unroll 1
       for (int c = 0; c < UN / 32; ++c) {
         uint32_t v[32];
@@ -369,14 +397,24 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     if (warp >= 2) {
       const int quarter = warp & 3;
       const uint32_t splits = gridDim.z, rank = blockIdx.z;
-      if (splits == 2) cluster_reduce_rows<2, UN>(ep, tiles, rank, quarter, lane, m0, n0);
-      else if (splits == 4) cluster_reduce_rows<4, UN>(ep, tiles, rank, quarter, lane, m0, n0);
-      else cluster_reduce_rows<8, UN>(ep, tiles, rank, quarter, lane, m0, n0);
+      if (ep.split_ws != nullptr) {
+        const float* ws_tile =
+            ep.split_ws + (static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * gridDim.z * (UN * UM);
+        if (splits == 2) cluster_reduce_rows<2, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, m0, n0);
+        else if (splits == 4) cluster_reduce_rows<4, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, m0, n0);
+        else cluster_reduce_rows<8, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, m0, n0);
+      } else {
+        if (splits == 2) cluster_reduce_rows<2, UN, false>(ep, tiles, nullptr, rank, quarter, lane, m0, n0);
+        else if (splits == 4) cluster_reduce_rows<4, UN, false>(ep, tiles, nullptr, rank, quarter, lane, m0, n0);
+        else cluster_reduce_rows<8, UN, false>(ep, tiles, nullptr, rank, quarter, lane, m0, n0);
+      }
     }
-    // nobody leaves (and frees its shared memory) while a peer may still be reading it
-    __syncwarp();
     if (warp == 2 && lane == 0) CGYM_STAMP(6);
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (ep.split_ws == nullptr) {
+      // nobody leaves (and frees its shared memory) while a peer may still be reading it
+      __syncwarp();
+      asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    }
     if (warp == 2 && lane == 0) CGYM_STAMP(7);
   }
 
@@ -517,16 +555,25 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   splits = splits >= 8 ? 8 : (splits >= 4 ? 4 : (splits >= 2 ? 2 : 1));  // cluster sizes the reduction is built for
   // every split must own at least one K slice
   while (splits > 1 && (splits - 1) * ((total_kb + splits - 1) / splits) >= total_kb) splits /= 2;
-  (void)workspace;
-  (void)workspace_bytes;
+  // partial tiles go through the caller's workspace (L2) when it is large enough, else through DSMEM
+  static const bool use_workspace = [] {  // tuning aid: CGYM_GEMM_SPLIT_WS=0 forces the DSMEM exchange
+    const char* v = std::getenv("CGYM_GEMM_SPLIT_WS");
+    return v == nullptr || std::atoi(v) != 0;
+  }();
+  const int64_t split_bytes = static_cast<int64_t>(n_tiles) * m_tiles * splits * un * UM * 4;
+  float* split_ws = nullptr;
+  if (splits > 1 && use_workspace && workspace != nullptr && workspace_bytes >= split_bytes &&
+      (reinterpret_cast<uintptr_t>(workspace) & 15u) == 0)
+    split_ws = static_cast<float*>(workspace);
 
   CUtensorMap mw, mx;
   if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
   if (int rc = make_map(&mx, x, M, K, un, fp8)) return rc;
-  GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0};
+  GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0,
+                  split_ws};
   dim3 grid(n_tiles, m_tiles, splits);
 #ifdef CGYM_TRACE
-  ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 4096ull : nullptr;
+  ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 8192ull : nullptr;
 #endif
   int rc = 0;
 #define LAUNCH_UN(U, R)                                                                 \

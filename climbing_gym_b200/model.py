@@ -45,9 +45,10 @@ class ForwardBuffers:
         self.attn_splits = attn_splits
         self.attn_ws = (torch.empty(rows * hq * attn_splits * (d + 2), device=dev, dtype=torch.float32)
                         if attn_splits > 1 else None)
-        # split-K partials of the narrow projections: up to 16 splits of [rows, hidden] fp32
-        # (zero-filled: its last 4 KB are the GEMM's per-tile arrival counters)
-        self.gemm_ws = torch.zeros(min(16 * rows * max(h, 1) * 4, 32 << 20) + 4096, device=dev, dtype=torch.uint8)
+        # split-K partial tiles of the decode GEMMs: at most 2 x 148 resident CTAs, each parking one
+        # [token tile][128] fp32 tile (token tile = 32 / 64 / 128 rows); larger row counts do not split
+        token_tile = 32 if rows <= 32 else 64 if rows <= 64 else 128
+        self.gemm_ws = torch.empty(2 * 148 * token_tile * 128 * 4, device=dev, dtype=torch.uint8)
 
 
 class LFM25Runner:

@@ -131,7 +131,11 @@ int cgym_qk_norm_rope_append(void* q_out, void* k_new, void* v_new, const void* 
  * workspace: fp32, >= rows * Hq * n_splits * (D + 2) elements when n_splits > 1.
  * impl: 0 = auto, 1 = CUDA-core kernel (any dtype / head_dim / page size), 2 = tensor-core kernel
  * with bulk-copy page staging (bf16 activations, bf16 or e4m3 cache, head_dim 64, 64-token pages);
- * status is required for impl 2 (bounded waits report there). */
+ * status is required for impl 2 (bounded waits report there).
+ * While cgym_set_pdl(1) is in force, impl 2 starts fetching every page but a row's last one before
+ * the kernel launched just ahead of it has finished: kv_lens, slots, active, the block table and
+ * all cache positions below kv_lens[r] - 1 must then be final before that kernel starts (in the
+ * decode step they come from cgym_step_begin and from earlier steps). */
 int cgym_paged_attention(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots,
                          const uint8_t* active, const cgym_kv_layout* kv, int layer, int rows,
                          int n_q_heads, float scale, int n_splits, float* workspace, int dtype,

@@ -384,7 +384,7 @@ def gemm_call(dev, x, w, *, impl, mask=None, ws_bytes=0):
     m, k = x.shape
     n = w.shape[0]
     y = torch.full((m, n), -3.0, device=dev, dtype=x.dtype)
-    ws_bytes = ws_bytes + 4096 if ws_bytes else 0  # partials + zeroed tile counters
+    ws_bytes = ws_bytes + 4096 if ws_bytes else 0  # room for the split-K partial tiles
     ws = torch.zeros(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
     status = torch.zeros(1, device=dev, dtype=torch.int32)
     nv.call("cgym_gemm", nv.ptr(y), nv.ptr(x), nv.ptr(w), nv.ptr(mask), m, n, k, nv.dtype_code(x.dtype), impl,
@@ -427,9 +427,17 @@ def test_gemm_tcgen05_split_k_is_deterministic_and_correct(dev):
     rng = np.random.default_rng(9)
     x_np, w_np = round_bf16(rng.standard_normal((m, k))), round_bf16(rng.standard_normal((n, k)) * 0.05)
     want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
+    # partial tiles exchanged through the workspace (2 tiles x 4 splits x [64][128] fp32 = 256 KiB) ...
     runs = [f32(gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=3, ws_bytes=8 * m * n * 4)) for _ in range(2)]
     assert np.array_equal(runs[0], runs[1])
     assert_gemm_close(runs[0], want, exact_fraction=0.97, what="split-K")
+    # ... and, without one, through distributed shared memory: same split order, same bits
+    dsmem = f32(gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=3, ws_bytes=0))
+    assert np.array_equal(dsmem, runs[0])
+    mask_np = (rng.random(m) < 0.5).astype(np.uint8)
+    masked = f32(gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=3, ws_bytes=8 * m * n * 4,
+                           mask=torch.from_numpy(mask_np).to(dev)))
+    assert np.all(masked[mask_np == 0] == -3.0) and np.array_equal(masked[mask_np == 1], runs[0][mask_np == 1])
     auto = f32(gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=0, ws_bytes=16 * m * n * 4))
     assert_gemm_close(auto, want, exact_fraction=0.97, what="auto split-K")
 
