@@ -321,6 +321,7 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   const int last_page = total_pages - 1;  // holds the position the append kernel writes this step
   while (issued < n_mine && issued < NST && page_begin + warp + 4 * issued != last_page) issue(issued++);
   pdl_wait();
+  q = pdl_fresh(q);
   uint32_t qa[D / 16][4];
   load_q_frags<EB, D, TQ>(qa, q + static_cast<int64_t>(row) * n_q_heads * D, lane >> 2, (lane >> 2) + 8, G, G,
                           n_q_heads, kh * G, lane);

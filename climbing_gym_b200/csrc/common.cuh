@@ -41,6 +41,16 @@ inline cudaStream_t as_stream(cgym_stream_t s) { return reinterpret_cast<cudaStr
 extern int g_pdl_enabled;  // toggled by cgym_set_pdl(); read at launch time on the host
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// A kernel that does work BEFORE pdl_wait() must reach its predecessor's output only through pointers
+// passed through pdl_fresh() after the wait. Inputs are declared `const T* __restrict__`, which tells
+// the compiler that nothing changes that memory during the kernel - so it may hoist such loads above
+// the wait to batch them with the early ones, and read what the predecessor has not written yet. The
+// empty volatile asm makes the pointer's value a product of a statement that follows the wait.
+template <typename P>
+__device__ __forceinline__ P* pdl_fresh(P* p) {
+  asm volatile("" : "+l"(p)::"memory");
+  return p;
+}
 
 template <typename... Params, typename... Args>
 inline cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,

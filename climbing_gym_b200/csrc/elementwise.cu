@@ -121,6 +121,8 @@ rmsnorm_rows_bf16_kernel(__nv_bfloat16* __restrict__ y, uint8_t* __restrict__ q,
   }
   pdl_trigger();
   pdl_wait();
+  x = pdl_fresh(x);
+  residual = pdl_fresh(residual);
   const int64_t base = static_cast<int64_t>(blockIdx.x) * n_chunks;  // in 16-byte chunks
   uint4 x_raw[CHUNKS], r_raw[CHUNKS];
 #pragma unroll
@@ -289,18 +291,22 @@ __global__ void conv_update_kernel(T* __restrict__ y, T* __restrict__ state, con
                                    const T* __restrict__ conv_w, const uint8_t* __restrict__ active,
                                    const int32_t* __restrict__ slots, int hidden) {
   pdl_trigger();
-  pdl_wait();
   const int row = blockIdx.y;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= hidden) return;
+  // the taps, the filter and the row's slot do not depend on the kernel ahead: fetch them before the wait
   int slot = slots != nullptr ? slots[row] : row;
   if (slot < 0) slot = 0;
-  const T* in = bcx + static_cast<int64_t>(row) * 3 * hidden;
+  T* st = state + static_cast<int64_t>(slot) * 3 * hidden;
+  float s0 = 0.f, s1 = 0.f, w0 = 0.f, w1 = 0.f, w2 = 0.f;
+  if (col < hidden) {
+    s0 = Elem<T>::load(st + hidden + col), s1 = Elem<T>::load(st + 2 * hidden + col);
+    w0 = Elem<T>::load(conv_w + col * 3), w1 = Elem<T>::load(conv_w + col * 3 + 1), w2 = Elem<T>::load(conv_w + col * 3 + 2);
+  }
+  pdl_wait();
+  if (col >= hidden) return;
+  const T* in = pdl_fresh(bcx) + static_cast<int64_t>(row) * 3 * hidden;
   const float b = Elem<T>::load(in + col), c = Elem<T>::load(in + hidden + col), x = Elem<T>::load(in + 2 * hidden + col);
   const float bx = Elem<T>::round(__fmul_rn(b, x));
-  T* st = state + static_cast<int64_t>(slot) * 3 * hidden;
-  const float s0 = Elem<T>::load(st + hidden + col), s1 = Elem<T>::load(st + 2 * hidden + col);
-  const float w0 = Elem<T>::load(conv_w + col * 3), w1 = Elem<T>::load(conv_w + col * 3 + 1), w2 = Elem<T>::load(conv_w + col * 3 + 2);
   const float p0 = Elem<T>::round(__fmul_rn(s0, w0)), p1 = Elem<T>::round(__fmul_rn(s1, w1)), p2 = Elem<T>::round(__fmul_rn(bx, w2));
   const float conv = Elem<T>::round(__fadd_rn(__fadd_rn(p0, p1), p2));
   if (active == nullptr || active[row]) {
@@ -386,21 +392,33 @@ __global__ void qk_rope_append_kernel(T* __restrict__ q_out, T* __restrict__ k_n
   __shared__ float buf[256];
   __shared__ float scratch[32];
   pdl_trigger();
-  pdl_wait();
   const int row = blockIdx.x, head = blockIdx.y, d = threadIdx.x, D = kv.head_dim, half = D >> 1;
   const int n_kv = kv.n_kv_heads;
   const int width = (n_q_heads + 2 * n_kv) * D;
   const bool is_q = head < n_q_heads;
-  const float x = Elem<T>::load(qkv + static_cast<int64_t>(row) * width + head * D + d);
-  const float ms = block_sum(x * x, scratch) / static_cast<float>(D);
-  float n = Elem<T>::round(__fmul_rn(x, rsqrtf(ms + eps)));
-  n = Elem<T>::round(__fmul_rn(n, Elem<T>::load((is_q ? q_w : k_w) + d)));
-  buf[d] = n;
-  __syncthreads();
-  const float other = buf[d < half ? d + half : d - half];
+  // Everything but qkv is settled before the kernel ahead of this one starts (positions, slots, active
+  // and the block table date from the start of the step, the tables and weights are constants), so
+  // the dependent position -> RoPE row -> page chain is walked before the dependent-launch wait.
   const int pos = positions[row];
   const float c = Elem<T>::round(rope_cos[static_cast<int64_t>(pos) * half + (d % half)]);
   const float s = Elem<T>::round(rope_sin[static_cast<int64_t>(pos) * half + (d % half)]);
+  const float norm_w = Elem<T>::load((is_q ? q_w : k_w) + d);
+  const bool writes_cache = !is_q && (active == nullptr || active[row]);
+  const int slot = slots != nullptr ? slots[row] : row;
+  int page = -1;
+  if (writes_cache && slot >= 0) {
+    const int block = pos / kv.page_size;
+    page = block < kv.max_blocks ? kv.block_table[static_cast<int64_t>(slot) * kv.max_blocks + block] : -1;
+  }
+  pdl_wait();
+  qkv = pdl_fresh(qkv);
+  const float x = Elem<T>::load(qkv + static_cast<int64_t>(row) * width + head * D + d);
+  const float ms = block_sum(x * x, scratch) / static_cast<float>(D);
+  float n = Elem<T>::round(__fmul_rn(x, rsqrtf(ms + eps)));
+  n = Elem<T>::round(__fmul_rn(n, norm_w));
+  buf[d] = n;
+  __syncthreads();
+  const float other = buf[d < half ? d + half : d - half];
   const float left = Elem<T>::round(__fmul_rn(n, c)), right = Elem<T>::round(__fmul_rn(other, s));
   const float rot = Elem<T>::round(d < half ? __fsub_rn(left, right) : __fadd_rn(left, right));
   if (is_q) {
@@ -413,11 +431,8 @@ __global__ void qk_rope_append_kernel(T* __restrict__ q_out, T* __restrict__ k_n
     Elem<T>::store(k_new + (static_cast<int64_t>(row) * n_kv + kh) * D + d, rot);
     Elem<T>::store(v_new + (static_cast<int64_t>(row) * n_kv + kh) * D + d, v);
   }
-  if (active != nullptr && !active[row]) return;
-  const int slot = slots != nullptr ? slots[row] : row;
-  if (slot < 0) return;
-  const int block = pos / kv.page_size, tok = pos % kv.page_size;
-  const int page = block < kv.max_blocks ? kv.block_table[static_cast<int64_t>(slot) * kv.max_blocks + block] : -1;
+  if (!writes_cache || slot < 0) return;
+  const int tok = pos % kv.page_size;
   if (page < 0 || page >= kv.n_pages) {  // uniform across the block
     if (d == 0) atomicOr(status, CGYM_STATUS_BAD_PAGE);
     return;

@@ -66,7 +66,12 @@ long long cgym_launch_count(void);
  * QK/RoPE/append, decode attention, conv update, SwiGLU, sampler): while enabled they are launched
  * with programmatic stream serialization, so a kernel is scheduled - and the GEMMs prefetch their
  * first weight tiles - while its predecessor is still draining; each of them waits for the
- * predecessor grid before touching dependent memory. Off by default; returns the previous setting.
+ * predecessor grid before touching dependent memory. What a kernel reads BEFORE that wait is, by
+ * contract, settled before the chain of dependent launches begins: weights and tables, positions /
+ * kv_lens / slots / active, block tables, conv taps and every cache position the step does not
+ * write (in the decode step these come from cgym_step_begin - launched without the attribute, so it
+ * completes before the chain starts - or from earlier steps). A caller that chains entry points
+ * itself while this is enabled must keep to the same rule. Off by default; returns the previous setting.
  * Process-wide host flag read at launch time (set it around a graph capture). No reference
  * counterpart (the reference relies on CUDA graphs alone, lfm25_cuda.py:246-262). */
 int cgym_set_pdl(int enabled);
