@@ -305,3 +305,16 @@ def write_checkpoint_description(model_dir, output_path) -> Path:
     path.parent.mkdir(parents=True, exist_ok=True)
     path.write_text(json.dumps(describe_lfm25_checkpoint(model_dir), indent=2) + "\n", encoding="utf-8")
     return path
+
+
+def load_tokenizer(model_dir, **kwargs):
+    """The checkpoint's tokenizer (models/lfm2_compat.py:36-48 of the reference): AutoTokenizer, or the
+    generic fast tokenizer when the export names a tokenizer class this transformers does not know."""
+    from transformers import AutoTokenizer, PreTrainedTokenizerFast
+
+    try:
+        return AutoTokenizer.from_pretrained(str(model_dir), **kwargs)
+    except ValueError as exc:
+        if "does not exist" not in str(exc):
+            raise
+        return PreTrainedTokenizerFast.from_pretrained(str(model_dir), **kwargs)
