@@ -67,6 +67,23 @@ __device__ __forceinline__ Pick shuffle_xor(Pick p, int o) {
   return q;
 }
 
+// eight consecutive logits, 16-byte aligned
+__device__ __forceinline__ void load8(const float* p, float* out) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* out) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* pairs = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(pairs[j]);
+    out[2 * j] = f.x;
+    out[2 * j + 1] = f.y;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(SAMPLE_THREADS)
 sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
@@ -89,24 +106,54 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
   const uint32_t k0 = static_cast<uint32_t>(key), k1 = static_cast<uint32_t>(key >> 32);
   const uint32_t base = rng_offsets != nullptr ? static_cast<uint32_t>(rng_offsets[row]) : 0u;
   const T* x = logits + static_cast<int64_t>(row) * vocab;
-  const int chunk = (vocab + parts - 1) / parts;
-  const int begin = part * chunk, end = min(vocab, begin + chunk);
 
   Pick mine{-INFINITY, 0x7fffffff, -INFINITY, 0.0f};
-  for (int i = begin + threadIdx.x; i < end; i += SAMPLE_THREADS) {
-    const float v = Elem<T>::load(x + i);
-    if (v > mine.mx) {
-      mine.sm = (mine.mx == -INFINITY ? 0.0f : mine.sm * expf(mine.mx - v)) + 1.0f;
-      mine.mx = v;
-    } else if (v > -INFINITY) {
-      mine.sm += expf(v - mine.mx);
-    }
+  const float t_div = fmaxf(temperature, 1.0e-30f);
+  // Gumbel-max score of element i (x / 1 is exact, so the division is skipped at temperature 1)
+  auto consider = [&](int i, float v) {
     float score = v;
     if (temperature > 0.0f) {
       const float u = fmaxf(uniform_from_word(philox_first_word(base + static_cast<uint32_t>(i), k0, k1)), 1.0e-30f);
-      score = __fdiv_rn(v, fmaxf(temperature, 1.0e-30f)) - logf(-logf(u));
+      score = (temperature == 1.0f ? v : __fdiv_rn(v, t_div)) - logf(-logf(u));
     }
     if (score > mine.score || (score == mine.score && i < mine.index)) { mine.score = score; mine.index = i; }
+  };
+  const bool wide = vocab % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
+  if (wide) {
+    // eight consecutive logits per thread and step (one or two 16-byte loads): a thread walks its
+    // slice in a few memory round trips, and the eight Philox chains of a group run side by side
+    const int groups = vocab / 8, per_part = (groups + parts - 1) / parts;
+    const int g_end = min(groups, (part + 1) * per_part);
+    for (int g = part * per_part + threadIdx.x; g < g_end; g += SAMPLE_THREADS) {
+      float v[8];
+      load8(x + static_cast<int64_t>(g) * 8, v);
+      float top = v[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) top = fmaxf(top, v[j]);
+      if (top > mine.mx) {
+        mine.sm = mine.mx == -INFINITY ? 0.0f : mine.sm * expf(mine.mx - top);
+        mine.mx = top;
+      }
+      if (mine.mx > -INFINITY) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mine.sm += expf(v[j] - mine.mx);  // exp(-inf) = 0 for masked logits
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) consider(g * 8 + j, v[j]);
+    }
+  } else {
+    const int chunk = (vocab + parts - 1) / parts;
+    const int begin = part * chunk, end = min(vocab, begin + chunk);
+    for (int i = begin + threadIdx.x; i < end; i += SAMPLE_THREADS) {
+      const float v = Elem<T>::load(x + i);
+      if (v > mine.mx) {
+        mine.sm = (mine.mx == -INFINITY ? 0.0f : mine.sm * expf(mine.mx - v)) + 1.0f;
+        mine.mx = v;
+      } else if (v > -INFINITY) {
+        mine.sm += expf(v - mine.mx);
+      }
+      consider(i, v);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mine = combine(mine, shuffle_xor(mine, o));
