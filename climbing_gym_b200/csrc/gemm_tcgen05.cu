@@ -10,11 +10,12 @@
 // accumulator back with tcgen05.ld and write y (coalesced along N), applying scales / row mask.
 // Warp roles: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = epilogue.
 //
-// Split-K (grid.z <= 8) runs as a thread-block cluster: each CTA parks its fp32 partial tile in its
-// own shared memory and the cluster sums the partials in split order through distributed shared
-// memory, so results are deterministic and no workspace or second launch is needed. Every mbarrier wait is bounded (about two seconds of
-// %globaltimer): on expiry the CTA raises CGYM_STATUS_WAIT_TIMEOUT, drains its own TMA copies with
-// the same bound, frees its TMEM and returns.
+// Split-K (grid.z <= 8) runs as a thread-block cluster: each CTA parks its fp32 partial tile - in the
+// caller's workspace (L2) when one is given, else in its own shared memory - and after a cluster
+// barrier every CTA sums its share of the tile's rows over all partials in split order, so results
+// are deterministic and no second launch is needed. Every mbarrier wait is bounded (about two
+// seconds of %globaltimer): on expiry the CTA raises CGYM_STATUS_WAIT_TIMEOUT, drains its own TMA
+// copies with the same bound, frees its TMEM and returns.
 #include <cuda.h>
 
 #include <cstdlib>

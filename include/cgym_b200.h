@@ -163,9 +163,13 @@ int cgym_prefill_attention(void* out, const void* q, const int32_t* tile_row0,
  * lfm25_cuda.py:124-126,141,166,170-172,180,192): y[M,N] = x[M,K] . w[N,K]^T, fp32 accumulate.
  * row_mask (uint8[M], optional): rows with 0 are not written (replaces the saved-logits
  * where-merge, lfm25_cuda.py:237-245). impl: 0 = auto, 1 = SIMT tile kernel, 2 = tcgen05/TMEM.
- * impl 3 = tcgen05 with split-K forced (test hook). Split-K is done inside a thread-block cluster
- * over distributed shared memory and needs no scratch: workspace/workspace_bytes are reserved
- * (pass NULL, 0). status receives CGYM_STATUS_WAIT_TIMEOUT if a bounded barrier wait gave up. */
+ * impl 3 = tcgen05 with split-K forced (test hook). Split-K runs inside a thread-block cluster and
+ * is deterministic. workspace/workspace_bytes (optional, 16-byte aligned, contents irrelevant): when
+ * it holds tiles * splits * token_tile * 128 fp32 (2 * 148 * token_tile * 512 bytes always suffice;
+ * token_tile = 32 / 64 / 128 / 256 >= M) the partial tiles are exchanged through it (L2), which is
+ * faster; without it they go through distributed shared memory, same bits. Launches that share a
+ * workspace must be stream-ordered. status receives CGYM_STATUS_WAIT_TIMEOUT if a bounded barrier
+ * wait gave up. */
 int cgym_gemm(void* y, const void* x, const void* w, const uint8_t* row_mask, int M, int N, int K,
               int dtype, int impl, void* workspace, int64_t workspace_bytes, int32_t* status,
               cgym_stream_t stream);
