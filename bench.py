@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -49,6 +50,16 @@ WORKLOADS = {
 # same two terms (weights once, KV history once), so `roofline.traffic` scales the full-size
 # algorithmic bytes by this ratio.
 DRAM_TRAFFIC_RATIO = {"bf16-b64x512": 1.0513}
+
+# Continuous batching through a generation session: a queue of requests served by a fixed number of
+# live slots; a finished request's slot is refilled from the queue at the next poll.
+#   name: (model, graph options, requests, slots, max_model_len, max output, mean output, prompt
+#          median, prompt sigma, prompt clip, poll interval)
+QUEUE_WORKLOADS = {
+    "fp8-queue2048x256": ("1p2b", {"fp8_mlp": True, "fp8_kv": True}, 2048, 256, 8192, 4096, 1500.0, 400.0, 0.8,
+                          (32, 4096), 32),
+    "tiny-queue": ("tiny", {}, 24, 8, 256, 32, 12.0, 24.0, 0.5, (4, 96), 8),
+}
 
 
 def peaks():
@@ -270,6 +281,148 @@ def run_ours(args) -> dict:
     return result if rank == 0 else {}
 
 
+def queue_requests(name: str, vocab: int, seed: int):
+    """Seeded synthetic requests of a queue workload: prompt lengths lognormal around the median and
+    clipped, output lengths geometric with the given mean and capped (a per-request length limit
+    stands in for the EOS hazard), prompt + output within max_model_len."""
+    import numpy as np
+
+    _, _, n, _, max_len, cap, mean_out, median, sigma, (low, high), _ = QUEUE_WORKLOADS[name]
+    rng = np.random.default_rng(seed)
+    prompt_lens = np.clip(np.rint(rng.lognormal(np.log(median), sigma, n)), low, high).astype(np.int64)
+    limits = np.minimum(rng.geometric(1.0 / mean_out, n), cap).astype(np.int64)
+    limits = np.maximum(1, np.minimum(limits, max_len - prompt_lens - 1))
+    prompts = [rng.integers(3, vocab, size=int(length)).tolist() for length in prompt_lens]
+    return prompts, [int(v) for v in limits]
+
+
+def run_queue(args) -> dict:
+    """One step = the whole request queue through one generation session."""
+    import torch
+    import torch.distributed as dist
+    from climbing_gym_b200 import _native as nv
+    from climbing_gym_b200.config import LFM25SamplingConfig
+    from climbing_gym_b200.replica import broadcast_policy_weights
+
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if not torch.cuda.is_available():
+        raise RuntimeError("bench.py needs a CUDA device: the engine has no CPU path")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    model, options, n_requests, slots, max_len, cap, mean_out, median, sigma, clip, poll_steps = QUEUE_WORKLOADS[args.workload]
+    engine, cfg = build_engine(model, device, options, max_model_len=max_len)
+    if world > 1:
+        broadcast_policy_weights(engine, src=0)
+    prompts, limits = queue_requests(args.workload, cfg.vocab_size, seed=2000 + rank)
+    staged = [torch.tensor(p, device=device, dtype=torch.int64) for p in prompts]
+    samplings = [LFM25SamplingConfig(temperature=1.0, top_k=0, top_p=1.0, max_new_tokens=limit, seed=index,
+                                     ignore_eos=True, return_logprobs=True) for index, limit in enumerate(limits)]
+
+    def one_pass(on_device: bool) -> dict:
+        generated, next_request, live = 0, 0, 0
+        with engine.generation_session(max_batch_size=slots, max_new_tokens=cap, profile_timings=True) as session:
+            def admit(count, into=None):
+                nonlocal next_request, live
+                pick = slice(next_request, next_request + count)
+                session.admit(prompts[pick], samplings[pick], slots=into,
+                              device_prompts=staged[pick] if on_device else None)
+                next_request += count
+                live += count
+
+            admit(min(slots, n_requests))
+            while live:
+                freed = []
+                for result in session.poll(steps=poll_steps):
+                    generated += len(result.token_ids)
+                    if result.logprobs is None or not all(math.isfinite(v) for v in result.logprobs):
+                        raise RuntimeError("session returned no or non-finite log-probs")
+                    freed.append(result.handle.slot)
+                    session.release(result.handle)
+                    live -= 1
+                refill = min(len(freed), n_requests - next_request)
+                if refill:
+                    admit(refill, freed[:refill])
+            timing = session.timing_stats()
+            stats = dict(session.stats)
+        return {"generated": generated, "decode_s": timing.get("decode_gpu_seconds", 0.0),
+                "prefill_s": timing.get("prefill_gpu_seconds", 0.0), "replays": stats["decode_steps"]}
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def timed(on_device: bool, steps: int):
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        passes = [one_pass(on_device) for _ in range(steps)]
+        end.record()
+        barrier()
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, passes
+
+    for _ in range(args.warmup):
+        one_pass(True)
+    launches_before = nv.launch_count()
+    with ClockSampler(local_rank) as clocks:
+        total_ms, passes = timed(True, args.steps)
+    launches = nv.launch_count() - launches_before
+    e2e_ms, _ = timed(False, args.steps)
+    expected = sum(limits)
+    if any(p["generated"] != expected for p in passes):
+        raise RuntimeError("a pass did not deliver every request's output budget")
+    value = world * expected * args.steps / (total_ms / 1e3)
+    e2e_value = world * expected * args.steps / (e2e_ms / 1e3)
+
+    # decode roofline: every replay streams the weights once and each live row's KV history once
+    w_bytes = weight_bytes(engine, options)
+    n_attn = engine.weights.num_attention_layers
+    fp8_kv = bool(options.get("fp8_kv"))
+    kv_tok = n_attn * 2 * cfg.num_key_value_heads * (cfg.head_dim * (1 if fp8_kv else 2) + (4 if fp8_kv else 0))
+    kv_tokens = sum((n - 1) * len(p) + (n - 1) * n // 2 for p, n in zip(prompts, limits))  # sum over decode steps of context
+    replays = sum(p["replays"] for p in passes) / len(passes)
+    decode_s = sum(p["decode_s"] for p in passes) / len(passes)
+    bytes_per_replay = w_bytes + kv_tok * kv_tokens / replays
+    peak, peak_source = peaks()
+    achieved = bytes_per_replay * replays / decode_s / 1e9
+    roofline = {"bound": "hbm", "kernel": f"decode step graph at {slots} slots (all kernels of one token step)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_source": peak_source, "traffic": None, "ms_per_launch": round(decode_s * 1e3 / replays, 4),
+                "algorithmic_bytes_per_launch": int(bytes_per_replay), "launches_timed": int(replays * len(passes)),
+                "decode_share_of_step": round(decode_s * 1e3 * len(passes) / total_ms, 4),
+                "prefill_share_of_step": round(sum(p["prefill_s"] for p in passes) * 1e3 / total_ms, 4)}
+    prompt_tokens = sum(len(p) for p in prompts)
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16+e4m3" if options else "bf16", "data": "synthetic",
+        "config": {"workload": args.workload,
+                   "model": "LFM2.5-1.2B architecture, random init" if model == "1p2b" else "tiny hybrid",
+                   "requests_per_gpu": n_requests, "live_slots": slots, "max_model_len": max_len,
+                   "prompt_lengths": f"lognormal(median {median:g}, sigma {sigma:g}) clipped to {list(clip)}",
+                   "output_lengths": f"geometric(mean {mean_out:g}) capped at {cap}, enforced as per-request limits",
+                   "prompt_tokens": prompt_tokens, "output_tokens": expected, "poll_interval": poll_steps,
+                   "options": options, "sampling": "temperature 1, full support", "replicas": world,
+                   "l2": "working set per decode step (weights + KV) is far larger than the 126 MB L2"},
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": int(prompt_tokens * 8),
+                "d2h_bytes_per_step": int(expected * 12 + replays / poll_steps * slots), "ms_per_step": round(e2e_ms / args.steps, 3)},
+        "gpu_launches": int(launches), "clocks": clocks.summary(), "roofline": roofline,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(model, seconds_budget=args.cpu_seconds)
+    if world > 1:
+        dist.destroy_process_group()
+    return result if rank == 0 else {}
+
+
 def cpu_baseline(model: str, *, seconds_budget: float = 25.0, steps: int = 1, warmup: int = 0) -> dict:
     """The CPU oracle (numpy restatement of the reference's eager engine) on a bounded sample of the
     workload: 8 prompts of 64 tokens, 48 sampled tokens each, fp32 on the host cores. `warmup` untimed
@@ -311,12 +464,12 @@ def run_reference(args) -> dict:
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return {}
-    model = WORKLOADS[args.workload][0]
+    model = (QUEUE_WORKLOADS.get(args.workload) or WORKLOADS[args.workload])[0]
     t0 = time.perf_counter()
     # every step is one pass over the bounded sample; a pass takes 10-15 s, so the step count actually
     # timed is capped to keep the whole run within a few minutes (the cap is reported in `sample`)
     base = cpu_baseline(model, seconds_budget=150.0, steps=min(args.steps, 10), warmup=min(args.warmup, 1))
-    model_name, batch, low, high, new_tokens, _ = WORKLOADS[args.workload]
+    model_name = model
     return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(base["seconds"] * 1e3 / base["passes"], 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -334,13 +487,16 @@ def main():
     parser.add_argument("--steps", type=int, default=3)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    parser.add_argument("--workload", default="bf16-b64x512", choices=sorted(WORKLOADS))
+    parser.add_argument("--workload", default="bf16-b64x512", choices=sorted([*WORKLOADS, *QUEUE_WORKLOADS]))
     parser.add_argument("--batch", type=int, default=0, help="override prompts per GPU")
     parser.add_argument("--new-tokens", type=int, default=0, help="override sampled tokens per prompt")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=25.0)
     args = parser.parse_args()
-    result = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.impl == "reference":
+        result = run_reference(args)
+    else:
+        result = run_queue(args) if args.workload in QUEUE_WORKLOADS else run_ours(args)
     if result:
         print(json.dumps(result), flush=True)
 

@@ -526,11 +526,18 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
                "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
   CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
-  const int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
+  // Token tile: the smallest that covers M up to 128; up to 256 rows (a full decode batch) two tiles of
+  // 128 keep the weight-streaming layout (half-SM rings, split-K) - the second tile's weight loads hit
+  // L2 - and only larger M (prefill) takes the 256-token tile that halves L2 -> SM traffic per FLOP.
+  static const int wide_from = [] {  // tuning aid: smallest M that uses the 256-token tile
+    const char* v = std::getenv("CGYM_GEMM_WIDE_FROM");
+    return v != nullptr && std::atoi(v) > 0 ? std::atoi(v) : 257;
+  }();
+  const int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M < wide_from ? 128 : 256));
   const int n_tiles = (N + UM - 1) / UM, m_tiles = (M + un - 1) / un;
   const int total_kb = (K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
   // decode-sized token tiles take the half-SM ring (two CTAs per SM), larger ones the full ring
-  bool half_ring = un <= 64;
+  bool half_ring = un <= 128;
   if (const char* forced = std::getenv("CGYM_GEMM_RING_KB")) half_ring = un <= 128 && std::atoi(forced) <= 96;  // tuning aid
   // Split-K until the CTAs fill the GPU's resident slots (at most 8: the portable cluster size). A
   // weight stream is bound by the bytes in flight, i.e. by how many rings are filling at once, so a

@@ -183,23 +183,37 @@ class LFM25GenerationSession:
 
     @torch.inference_mode()
     def admit(self, prompts: Sequence[Sequence[int]], samplings: Sequence[LFM25SamplingConfig], *,
-              slots: Sequence[int] | None = None) -> list[int]:
+              slots: Sequence[int] | None = None, device_prompts: Sequence[torch.Tensor] | None = None) -> list[int]:
+        """Prefill ``prompts`` into free slots (lowest first unless ``slots`` names them) and start their
+        generation. ``device_prompts`` (optional, one int64 tensor per prompt, already on the engine's
+        device and holding the same ids) skips the host-to-device copy of the token ids."""
         self._check_open()
         if len(prompts) != len(samplings):
             raise ValueError("One sampling configuration is required per prompt")
+        if device_prompts is not None and len(device_prompts) != len(prompts):
+            raise ValueError("device_prompts must align with prompts")
         free = [i for i, request in enumerate(self.requests) if request is None]
         slots = list(free[:len(prompts)] if slots is None else slots)
         if len(slots) != len(prompts) or len(set(slots)) != len(slots) or any(i not in free for i in slots):
             raise ValueError("Admission requires distinct free session slots")
-        work = sorted(zip(slots, prompts, samplings), key=lambda item: item[0])
+        order = sorted(range(len(slots)), key=lambda i: slots[i])
+        work = [(slots[i], prompts[i], samplings[i]) for i in order]
         for _, prompt, sampling in work:
             self._validate(prompt, sampling)
         if not work:
             return slots
         ordered_slots = [slot for slot, _, _ in work]
         with self._timed("prefill"):
-            self.engine._prefill_packed(self.cache, ordered_slots, [list(p) for _, p, _ in work], [0] * len(work),
-                                        self.entry.logits, self.decoder.max_prefill_tokens)
+            if device_prompts is None:
+                self.engine._prefill_packed(self.cache, ordered_slots, [list(p) for _, p, _ in work], [0] * len(work),
+                                            self.entry.logits, self.decoder.max_prefill_tokens)
+            else:
+                staged = [device_prompts[i] for i in order]
+                if any(t.numel() != len(p) for t, (_, p, _) in zip(staged, work)):
+                    raise ValueError("device_prompts must hold the same ids as prompts")
+                self.engine._prefill_packed(self.cache, ordered_slots, [len(p) for _, p, _ in work], [0] * len(work),
+                                            self.entry.logits, self.decoder.max_prefill_tokens,
+                                            flat_tokens=torch.cat(staged).to(torch.int64))
         for slot, prompt, _ in work:
             self.stats["slot_refills"] += int(self.versions[slot] > 0)
             self.stats["prefilled_tokens"] += len(prompt)
@@ -268,8 +282,9 @@ class LFM25GenerationSession:
         if not live:
             return []
         graph, batch = self.decoder._select_graph(self.entry, live)
-        for _ in range(steps):
-            graph.replay()
+        with self._timed("decode"):
+            for _ in range(steps):
+                graph.replay()
         self.stats["decode_steps"] += steps
         self.stats["decode_row_steps"] += batch * steps
         self.stats["reserved_row_steps"] += self.batch_size * steps
