@@ -42,6 +42,9 @@ WORKLOADS = {
     "bf16-b64x512": ("1p2b", 64, 64, 1024, 512, {}),
     "fp8-b64x512": ("1p2b", 64, 64, 1024, 512, {"fp8_mlp": True, "fp8_kv": True}),
     "tiny": ("tiny", 8, 8, 64, 32, {}),
+    # long-context stress: 32 sequences, prompts of 16-30 K tokens prefilled in 4096-token chunks
+    "bf16-long32x1024": ("1p2b", 32, 16384, 30720, 1024, {}),
+    "fp8kv-long32x1024": ("1p2b", 32, 16384, 30720, 1024, {"fp8_kv": True}),
 }
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum over the 140 kernels of ONE decode-step

@@ -47,7 +47,7 @@ class SlotState(C.Structure):
                 ("stop_offsets", C.c_void_p), ("stop_table", C.c_void_p), ("ignore_eos", C.c_void_p),
                 ("rng_positions", C.c_void_p), ("seeds", C.c_void_p), ("temperatures", C.c_void_p),
                 ("rng_offsets", C.c_void_p), ("force_eos_at", C.c_void_p), ("seq_lens", C.c_void_p),
-                ("capacity", C.c_int32), ("eos_token_id", C.c_int32)]
+                ("min_logits", C.c_void_p), ("capacity", C.c_int32), ("eos_token_id", C.c_int32)]
 
 
 _P, _I, _F, _L = C.c_void_p, C.c_int, C.c_float, C.c_int64
@@ -72,6 +72,7 @@ SIGNATURES = {
     "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_sample": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_sample_static": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "cgym_filter_thresholds": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "cgym_target_logprobs": [_P, _P, _P, _I, _I, _I, _P],
     "cgym_step_begin": [C.POINTER(PagePool), _P, _P, _P, _P, _P, _P, _I, _P, _P],
     "cgym_pages_reserve": [C.POINTER(PagePool), _P, _P, _I, _P, _P],

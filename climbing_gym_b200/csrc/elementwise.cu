@@ -246,6 +246,59 @@ swiglu_rows_bf16_kernel(__nv_bfloat16* __restrict__ y, const __nv_bfloat16* __re
   *(reinterpret_cast<uint4*>(y + row * ffn) + chunk) = pack8(g);
 }
 
+// bf16 fast path of the fused SwiGLU + row quantisation: the row's activations stay in registers
+// (CHUNKS groups of eight per thread, 16-byte loads of gate and up, 8-byte stores of the codes)
+constexpr int SWIGLU_Q_THREADS = 512;
+
+template <int CHUNKS>
+__global__ void __launch_bounds__(SWIGLU_Q_THREADS)
+swiglu_quant_rows_bf16_kernel(uint8_t* __restrict__ q, float* __restrict__ scales,
+                              const __nv_bfloat16* __restrict__ gate_up, int ffn) {
+  __shared__ float scratch[32];
+  pdl_trigger();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const int n_chunks = ffn >> 3;
+  const uint4* gate = reinterpret_cast<const uint4*>(gate_up + row * 2 * ffn);
+  const uint4* up = reinterpret_cast<const uint4*>(gate_up + row * 2 * ffn + ffn);
+  uint4 g_raw[CHUNKS], u_raw[CHUNKS];
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int chunk = threadIdx.x + c * SWIGLU_Q_THREADS;
+    g_raw[c] = u_raw[c] = make_uint4(0, 0, 0, 0);
+    if (chunk < n_chunks) {
+      g_raw[c] = gate[chunk];
+      u_raw[c] = up[chunk];
+    }
+  }
+  float v[CHUNKS][8];
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    float u[8];
+    unpack8(g_raw[c], v[c]);
+    unpack8(u_raw[c], u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[c][j] = swiglu_value<__nv_bfloat16>(v[c][j], u[j]);  // swiglu(0, 0) = 0 for the padding chunks
+      amax = fmaxf(amax, fabsf(v[c][j]));
+    }
+  }
+  amax = block_max(amax, scratch);
+  const float scale = fmaxf(amax / 448.0f, 1.0e-12f);
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int chunk = threadIdx.x + c * SWIGLU_Q_THREADS;
+    if (chunk >= n_chunks) continue;
+    uint2 codes;
+    uint8_t* bytes = reinterpret_cast<uint8_t*>(&codes);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bytes[j] = to_e4m3(fminf(fmaxf(__fdiv_rn(v[c][j], scale), -448.0f), 448.0f));
+    *(reinterpret_cast<uint2*>(q + row * ffn) + chunk) = codes;
+  }
+  if (threadIdx.x == 0) scales[row] = scale;
+}
+
 template <typename T>
 __global__ void swiglu_quant_kernel(uint8_t* __restrict__ q, float* __restrict__ scales,
                                     const T* __restrict__ gate_up, int ffn) {
@@ -456,6 +509,91 @@ __global__ void qk_rope_append_kernel(T* __restrict__ q_out, T* __restrict__ k_n
   }
 }
 
+// head_dim 64: one WARP per head (lane l holds dims l and l + 32, i.e. a RoPE pair), eight heads per
+// CTA, reductions by shuffle only. Same arithmetic, in the same order, as the kernel above (the mean
+// square is the sum of the two 32-dim halves, each reduced by the same butterfly).
+template <typename T, typename KV>
+__global__ void __launch_bounds__(256)
+qk_rope_append_d64_kernel(T* __restrict__ q_out, T* __restrict__ k_new, T* __restrict__ v_new,
+                          const T* __restrict__ qkv, const T* __restrict__ q_w, const T* __restrict__ k_w,
+                          const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
+                          const int32_t* __restrict__ positions, const int32_t* __restrict__ slots,
+                          const uint8_t* __restrict__ active, cgym_kv_layout kv, int layer, int n_q_heads, float eps,
+                          int32_t* status) {
+  constexpr int D = 64, HALF = 32;
+  pdl_trigger();
+  const int row = blockIdx.x, lane = threadIdx.x & 31;
+  const int head = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int n_kv = kv.n_kv_heads;
+  const bool valid = head < n_q_heads + n_kv, is_q = head < n_q_heads;
+  // settled before the chain of dependent launches starts: position, RoPE row, norm weights
+  const int pos = positions[row];
+  const float c = Elem<T>::round(rope_cos[static_cast<int64_t>(pos) * HALF + lane]);
+  const float s = Elem<T>::round(rope_sin[static_cast<int64_t>(pos) * HALF + lane]);
+  const T* norm_w = is_q ? q_w : k_w;
+  const float w_lo = Elem<T>::load(norm_w + lane), w_hi = Elem<T>::load(norm_w + lane + HALF);
+  pdl_wait();
+  if (!valid) return;
+  qkv = pdl_fresh(qkv);
+  const int width = (n_q_heads + 2 * n_kv) * D;
+  const T* src = qkv + static_cast<int64_t>(row) * width + head * D;
+  const float x_lo = Elem<T>::load(src + lane), x_hi = Elem<T>::load(src + lane + HALF);
+  const float ms = __fadd_rn(warp_sum(x_lo * x_lo), warp_sum(x_hi * x_hi)) / static_cast<float>(D);
+  const float inv = rsqrtf(ms + eps);
+  const float n_lo = Elem<T>::round(__fmul_rn(Elem<T>::round(__fmul_rn(x_lo, inv)), w_lo));
+  const float n_hi = Elem<T>::round(__fmul_rn(Elem<T>::round(__fmul_rn(x_hi, inv)), w_hi));
+  const float rot_lo = Elem<T>::round(__fsub_rn(Elem<T>::round(__fmul_rn(n_lo, c)), Elem<T>::round(__fmul_rn(n_hi, s))));
+  const float rot_hi = Elem<T>::round(__fadd_rn(Elem<T>::round(__fmul_rn(n_hi, c)), Elem<T>::round(__fmul_rn(n_lo, s))));
+  if (is_q) {
+    T* dst = q_out + (static_cast<int64_t>(row) * n_q_heads + head) * D;
+    Elem<T>::store(dst + lane, rot_lo);
+    Elem<T>::store(dst + lane + HALF, rot_hi);
+    return;
+  }
+  const int kh = head - n_q_heads;
+  const T* v_src = qkv + static_cast<int64_t>(row) * width + (n_q_heads + n_kv + kh) * D;
+  const float v_lo = Elem<T>::load(v_src + lane), v_hi = Elem<T>::load(v_src + lane + HALF);
+  if (k_new != nullptr) {
+    const int64_t o = (static_cast<int64_t>(row) * n_kv + kh) * D;
+    Elem<T>::store(k_new + o + lane, rot_lo);
+    Elem<T>::store(k_new + o + lane + HALF, rot_hi);
+    Elem<T>::store(v_new + o + lane, v_lo);
+    Elem<T>::store(v_new + o + lane + HALF, v_hi);
+  }
+  if (active != nullptr && !active[row]) return;
+  const int slot = slots != nullptr ? slots[row] : row;
+  if (slot < 0) return;
+  const int block = pos / kv.page_size, tok = pos % kv.page_size;
+  const int page = block < kv.max_blocks ? kv.block_table[static_cast<int64_t>(slot) * kv.max_blocks + block] : -1;
+  if (page < 0 || page >= kv.n_pages) {  // uniform across the warp
+    if (lane == 0) atomicOr(status, CGYM_STATUS_BAD_PAGE);
+    return;
+  }
+  KV* pool = static_cast<KV*>(kv.kv_pool);
+  constexpr int EB = static_cast<int>(sizeof(KV));
+  const int64_t k_lo = kv_k_offset(kv, layer, page, kh, tok, lane, EB), k_hi = kv_k_offset(kv, layer, page, kh, tok, lane + HALF, EB);
+  const int64_t o_lo = kv_v_offset(kv, layer, page, kh, tok, lane, EB), o_hi = kv_v_offset(kv, layer, page, kh, tok, lane + HALF, EB);
+  if constexpr (sizeof(KV) == 1) {
+    const float ak = warp_max(fmaxf(fabsf(rot_lo), fabsf(rot_hi)));
+    const float av = warp_max(fmaxf(fabsf(v_lo), fabsf(v_hi)));
+    const float sk = fmaxf(ak / 448.0f, 1.0e-12f), sv = fmaxf(av / 448.0f, 1.0e-12f);
+    uint8_t* bytes = reinterpret_cast<uint8_t*>(pool);
+    bytes[k_lo] = to_e4m3(__fdiv_rn(rot_lo, sk));
+    bytes[k_hi] = to_e4m3(__fdiv_rn(rot_hi, sk));
+    bytes[o_lo] = to_e4m3(__fdiv_rn(v_lo, sv));
+    bytes[o_hi] = to_e4m3(__fdiv_rn(v_hi, sv));
+    if (lane == 0) {
+      kv.kv_scales[kv_scale_offset(kv, layer, page, 0, kh, tok)] = sk;
+      kv.kv_scales[kv_scale_offset(kv, layer, page, 1, kh, tok)] = sv;
+    }
+  } else {
+    Elem<KV>::store(pool + k_lo, rot_lo);
+    Elem<KV>::store(pool + k_hi, rot_hi);
+    Elem<KV>::store(pool + o_lo, v_lo);
+    Elem<KV>::store(pool + o_hi, v_hi);
+  }
+}
+
 // ------------------------------------------------------------------------------------------
 // logit[target] - logsumexp(logits) per row
 // ------------------------------------------------------------------------------------------
@@ -549,6 +687,16 @@ extern "C" int cgym_swiglu_quant(uint8_t* q, float* scales, const void* gate_up,
   CGYM_REQUIRE(rows >= 0 && ffn > 0 && ffn <= 12288, "swiglu_quant: ffn must be in [1, 12288]");
   if (rows == 0) return 0;
   using T = __nv_bfloat16;
+  const int chunks = (ffn / 8 + SWIGLU_Q_THREADS - 1) / SWIGLU_Q_THREADS;
+  if (ffn % 8 == 0 && chunks <= 3 && (reinterpret_cast<uintptr_t>(gate_up) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(q) & 7u) == 0) {
+    const T* in = static_cast<const T*>(gate_up);
+    const dim3 grid(rows), block(SWIGLU_Q_THREADS);
+    if (chunks <= 1) launch_dependent(swiglu_quant_rows_bf16_kernel<1>, grid, block, 0, as_stream(stream), q, scales, in, ffn);
+    else if (chunks == 2) launch_dependent(swiglu_quant_rows_bf16_kernel<2>, grid, block, 0, as_stream(stream), q, scales, in, ffn);
+    else launch_dependent(swiglu_quant_rows_bf16_kernel<3>, grid, block, 0, as_stream(stream), q, scales, in, ffn);
+    return check_launch("swiglu_quant");
+  }
   launch_dependent(swiglu_quant_kernel<T>, dim3(rows), dim3(512), ffn * sizeof(float), as_stream(stream), q, scales,
                    static_cast<const T*>(gate_up), ffn);
   return check_launch("swiglu_quant");
@@ -606,8 +754,16 @@ extern "C" int cgym_qk_norm_rope_append(void* q_out, void* k_new, void* v_new, c
   CGYM_REQUIRE(kv->kv_dtype != CGYM_E4M3 || kv->kv_scales != nullptr, "e4m3 KV needs a scale pool");
   if (rows == 0) return 0;
   CGYM_REQUIRE(n_q_heads + kv->n_kv_heads <= 65535, "too many heads");
-  dim3 grid(rows, n_q_heads + kv->n_kv_heads);
+  const bool per_warp = D == 64;  // one warp per head, eight heads per CTA
+  dim3 grid(rows, per_warp ? (n_q_heads + kv->n_kv_heads + 7) / 8 : n_q_heads + kv->n_kv_heads);
 #define LAUNCH_QK(T, KV)                                                                                   \
+  if (per_warp)                                                                                            \
+    launch_dependent(qk_rope_append_d64_kernel<T, KV>, grid, dim3(256), 0, as_stream(stream),              \
+                     static_cast<T*>(q_out), static_cast<T*>(k_new), static_cast<T*>(v_new),               \
+                     static_cast<const T*>(qkv), static_cast<const T*>(q_norm_w),                          \
+                     static_cast<const T*>(k_norm_w), rope_cos, rope_sin, positions, slots, active, *kv,   \
+                     layer, n_q_heads, eps, status);                                                       \
+  else                                                                                                     \
   launch_dependent(qk_rope_append_kernel<T, KV>, grid, dim3(D), 0, as_stream(stream), static_cast<T*>(q_out),     \
                    static_cast<T*>(k_new), static_cast<T*>(v_new), static_cast<const T*>(qkv),                   \
                    static_cast<const T*>(q_norm_w), static_cast<const T*>(k_norm_w), rope_cos, rope_sin,         \

@@ -109,8 +109,11 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
 
   Pick mine{-INFINITY, 0x7fffffff, -INFINITY, 0.0f};
   const float t_div = fmaxf(temperature, 1.0e-30f);
+  // support of the draw: logits below the row's threshold (top-k / top-p) are never candidates
+  const float floor = (has_state && st.min_logits != nullptr) ? st.min_logits[row] : -INFINITY;
   // Gumbel-max score of element i (x / 1 is exact, so the division is skipped at temperature 1)
   auto consider = [&](int i, float v) {
+    if (v < floor) return;
     float score = v;
     if (temperature > 0.0f) {
       const float u = fmaxf(uniform_from_word(philox_first_word(base + static_cast<uint32_t>(i), k0, k1)), 1.0e-30f);
@@ -234,9 +237,139 @@ static int pick_parts(int rows, int vocab, const float* workspace) {
   return parts < 1 ? 1 : parts;
 }
 
+// ---- top-k / top-p support thresholds ---------------------------------------------------------------
+// Floats map to unsigned keys whose order is the floats' order; the k-th largest logit and the top-p
+// cut are then found bit by bit from the most significant bit down, each probe being one pass over
+// the row with a fixed-tree block reduction (counts, or tempered softmax mass), so the result does not
+// depend on timing. bf16 rows are staged once in shared memory as 16-bit keys (only those 16 bits
+// are searched); fp32 rows are re-read from L2 on every probe (test-sized vocabularies).
+constexpr int FILTER_THREADS = 1024;
+
+__device__ __forceinline__ uint32_t ordered_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key ^ 0x80000000u) : ~key);
+}
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v, uint32_t* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  uint32_t r = lane < nwarps ? scratch[lane] : 0u;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) r = max(r, __shfl_xor_sync(0xffffffffu, r, o));
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(FILTER_THREADS)
+filter_threshold_kernel(float* __restrict__ min_logits, const T* __restrict__ logits,
+                        const float* __restrict__ temperatures, const int32_t* __restrict__ top_k,
+                        const float* __restrict__ top_p, const uint8_t* __restrict__ alive, int vocab) {
+  constexpr bool HALF = sizeof(T) == 2;
+  constexpr int LOW_BIT = HALF ? 16 : 0;  // bf16 keys have no information below bit 16
+  extern __shared__ uint16_t staged[];    // bf16: the row's keys
+  __shared__ float scratch[32];
+  __shared__ uint32_t uscratch[32];
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x;
+  const float temperature = temperatures[row];
+  const int k = top_k != nullptr ? top_k[row] : 0;
+  const float p = top_p != nullptr ? top_p[row] : 1.0f;
+  const bool use_k = k > 0 && k < vocab, use_p = p < 1.0f;
+  if ((alive != nullptr && !alive[row]) || !(temperature > 0.0f) || (!use_k && !use_p)) {  // uniform per CTA
+    if (threadIdx.x == 0) min_logits[row] = -INFINITY;
+    return;
+  }
+  const T* x = logits + static_cast<int64_t>(row) * vocab;
+  if (HALF) {
+    for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) staged[i] = static_cast<uint16_t>(ordered_key(Elem<T>::load(x + i)) >> 16);
+    __syncthreads();
+  }
+  auto key_at = [&](int i) -> uint32_t {
+    if (HALF) return static_cast<uint32_t>(staged[i]) << 16;
+    return ordered_key(Elem<T>::load(x + i));
+  };
+
+  uint32_t tau_k = 0u;  // keys >= tau_k survive top-k
+  if (use_k) {
+    for (int bit = 31; bit >= LOW_BIT; --bit) {
+      const uint32_t probe = tau_k | (1u << bit);
+      float count = 0.0f;  // exact: counts stay far below 2^24
+      for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) count += key_at(i) >= probe ? 1.0f : 0.0f;
+      if (block_sum(count, scratch) >= static_cast<float>(k)) tau_k = probe;  // the k-th largest key is >= probe
+    }
+  }
+  uint32_t tau = tau_k;
+  if (use_p) {
+    uint32_t top = 0u;
+    for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) top = max(top, key_at(i));
+    top = block_max_u32(top, uscratch);
+    const float v_top = key_value(top);
+    auto mass_from = [&](uint32_t floor_key) {  // tempered softmax mass (relative to the maximum) of keys >= floor_key
+      float mass = 0.0f;
+      for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) {
+        const uint32_t key = key_at(i);
+        if (key >= floor_key) mass += expf(__fdiv_rn(key_value(key) - v_top, temperature));
+      }
+      return block_sum(mass, scratch);
+    };
+    const float budget = p * mass_from(tau_k);
+    // the largest key whose tail mass (within the top-k survivors) still exceeds the budget; the
+    // predicate holds for every key <= tau_k and never again once it failed, so the bits can be fixed
+    // from the top
+    uint32_t over = 0u;
+    for (int bit = 31; bit >= LOW_BIT; --bit) {
+      const uint32_t probe = over | (1u << bit);
+      if (mass_from(max(probe, tau_k)) > budget) over = probe;
+    }
+    // every key above `over` has a tail mass within the budget; the most probable value always stays
+    uint32_t tau_p = over + (1u << LOW_BIT);
+    if (tau_p < over || tau_p > top) tau_p = top;
+    tau = max(tau_k, tau_p);
+  }
+  if (threadIdx.x == 0) min_logits[row] = tau == 0u ? -INFINITY : key_value(tau);
+}
+
 }  // namespace cgym
 
 using namespace cgym;
+
+extern "C" int cgym_filter_thresholds(float* min_logits, const void* logits, const float* temperatures,
+                                      const int32_t* top_k, const float* top_p, const uint8_t* alive, int rows,
+                                      int vocab, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(min_logits && logits && temperatures && rows >= 0 && vocab > 0, "filter_thresholds: bad arguments");
+  CGYM_REQUIRE(vocab <= FILTER_THREADS * 64, "filter_thresholds: vocabularies up to %d entries", FILTER_THREADS * 64);
+  if (rows == 0) return 0;
+  if (dtype == CGYM_BF16) {
+    const int smem = vocab * static_cast<int>(sizeof(uint16_t));
+    static std::mutex mutex;
+    static int reserved = 0;
+    {
+      std::lock_guard<std::mutex> lock(mutex);
+      if (smem > reserved) {
+        const cudaError_t rc = cudaFuncSetAttribute(filter_threshold_kernel<__nv_bfloat16>,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        CGYM_REQUIRE(rc == cudaSuccess, "filter_thresholds: cannot reserve %d bytes of shared memory: %s", smem,
+                     cudaGetErrorString(rc));
+        reserved = smem;
+      }
+    }
+    launch_dependent(filter_threshold_kernel<__nv_bfloat16>, dim3(rows), dim3(FILTER_THREADS), smem, as_stream(stream),
+                     min_logits, static_cast<const __nv_bfloat16*>(logits), temperatures, top_k, top_p, alive, vocab);
+  } else if (dtype == CGYM_F32) {
+    launch_dependent(filter_threshold_kernel<float>, dim3(rows), dim3(FILTER_THREADS), 0, as_stream(stream), min_logits,
+                     static_cast<const float*>(logits), temperatures, top_k, top_p, alive, vocab);
+  } else {
+    return fail("filter_thresholds: unsupported logits dtype %d", dtype);
+  }
+  return check_launch("filter_thresholds");
+}
 
 extern "C" int64_t cgym_sample_workspace_bytes(int rows) {
   return (static_cast<int64_t>(rows) * SAMPLE_MAX_PARTS * 4 + rows) * 4;

@@ -21,6 +21,7 @@ from . import _native as nv
 from .config import LFM25SamplingConfig
 from .model import ForwardBuffers, LFM25Runner
 from .paged import PagedHybridCache
+from .text_stops import build_token_sequence_table
 from .types import LFM25GenerationOutput
 
 
@@ -29,7 +30,7 @@ class SlotState:
     src/climbing_gym/inference/lfm25_session.py:147-167) plus the struct the sampler kernel reads."""
 
     def __init__(self, n_slots: int, capacity: int, vocab: int, eos: int, seq_lens: torch.Tensor,
-                 *, stop_states: int = 8):
+                 *, stop_states: int = 32):
         dev = seq_lens.device
         self.n_slots, self.capacity, self.vocab = n_slots, capacity, vocab
 
@@ -54,12 +55,20 @@ class SlotState:
         # sampler scratch: per-(row, slice) partial picks + one arrival counter per row, kept at zero
         self.sample_ws = torch.zeros(int(nv.load().cgym_sample_workspace_bytes(n_slots)) // 4, device=dev,
                                      dtype=torch.float32)
-        self.struct = nv.SlotState(
-            nv.ptr(self.tokens), nv.ptr(self.logprobs), nv.ptr(self.lengths), nv.ptr(self.limits),
-            nv.ptr(self.reasons), nv.ptr(self.alive), nv.ptr(self.pending), nv.ptr(self.input_tokens),
-            nv.ptr(self.stop_states), nv.ptr(self.stop_offsets), nv.ptr(self.stop_table), nv.ptr(self.ignore_eos),
-            nv.ptr(self.rng_positions), nv.ptr(self.seeds), nv.ptr(self.temperatures), nv.ptr(self.rng_offsets),
-            nv.ptr(self.force_eos_at), nv.ptr(seq_lens), capacity, eos)
+        # top-k / top-p per slot and the value thresholds cgym_filter_thresholds derives from them each step
+        self.top_k, self.top_p = rows(torch.int32), rows(torch.float32, 1.0)
+        self.min_logits = rows(torch.float32, float("-inf"))
+
+        def struct(min_logits):
+            return nv.SlotState(
+                nv.ptr(self.tokens), nv.ptr(self.logprobs), nv.ptr(self.lengths), nv.ptr(self.limits),
+                nv.ptr(self.reasons), nv.ptr(self.alive), nv.ptr(self.pending), nv.ptr(self.input_tokens),
+                nv.ptr(self.stop_states), nv.ptr(self.stop_offsets), nv.ptr(self.stop_table), nv.ptr(self.ignore_eos),
+                nv.ptr(self.rng_positions), nv.ptr(self.seeds), nv.ptr(self.temperatures), nv.ptr(self.rng_offsets),
+                nv.ptr(self.force_eos_at), nv.ptr(seq_lens), nv.ptr(min_logits), capacity, eos)
+
+        self.struct = struct(None)                      # full-support sampling
+        self.struct_filtered = struct(self.min_logits)  # draws restricted to logits >= min_logits[slot]
 
     def reset(self) -> None:
         for t in (self.lengths, self.limits, self.reasons, self.alive, self.pending, self.ignore_eos,
@@ -118,6 +127,7 @@ class _DecodeGraph:
     state: SlotState
     bufs: ForwardBuffers
     compact_graphs: dict = field(default_factory=dict)
+    filtered: bool = False  # the step derives top-k / top-p thresholds before it samples
 
 
 class B200Decoder:
@@ -192,23 +202,32 @@ class B200Decoder:
         nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(state.pending), nv.ptr(state.active),
                 None, None, nv.ptr(kv_lens), n, nv.ptr(cache.status), stream)
         self.runner.decode_step(entry.bufs, cache, state.input_tokens, state.active, entry.logits, kv_lens=kv_lens)
-        nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(state.struct), nv.ptr(state.active), None, None,
-                n, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype), nv.ptr(state.sample_ws), stream)
+        self._sample(entry, nv.ptr(state.active), stream)
+
+    def _sample(self, entry: _DecodeGraph, advance, stream) -> None:
+        """Sampler + bookkeeping of one step; filtered entries first turn each row's top-k / top-p into
+        a value threshold (the reference leaves its fused sampler for torch sort / multinomial here,
+        src/climbing_gym/inference/lfm25_cuda.py:311-324)."""
+        state, n, vocab = entry.state, entry.cache.n_slots, self.engine.config.vocab_size
+        dtype = nv.dtype_code(entry.logits.dtype)
+        if entry.filtered:
+            nv.call("cgym_filter_thresholds", nv.ptr(state.min_logits), nv.ptr(entry.logits), nv.ptr(state.temperatures),
+                    nv.ptr(state.top_k), nv.ptr(state.top_p), nv.ptr(state.alive), n, vocab, dtype, stream)
+        struct = state.struct_filtered if entry.filtered else state.struct
+        nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(struct), advance, None, None, n, vocab, dtype,
+                nv.ptr(state.sample_ws), stream)
 
     def _sample_only(self, entry: _DecodeGraph) -> None:
         """First token of freshly prefetched rows: sample from the prefill logits, no forward."""
-        state = entry.state
-        nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(state.struct), None, None, None,
-                entry.cache.n_slots, self.engine.config.vocab_size, nv.dtype_code(entry.logits.dtype),
-                nv.ptr(state.sample_ws), nv.stream_ptr(self.engine.device))
+        self._sample(entry, None, nv.stream_ptr(self.engine.device))
 
     @torch.inference_mode()
-    def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False) -> _DecodeGraph:
+    def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False, filtered: bool = False) -> _DecodeGraph:
         engine = self.engine
         alignment = 32 if batch_size >= 64 else 128
         alignment = max(alignment, self.page_size)
         capacity = min(engine.max_model_len, -(-cache_len // alignment) * alignment)
-        key = (batch_size, capacity, masked)
+        key = (batch_size, capacity, masked, "filtered") if filtered else (batch_size, capacity, masked)
         if key in self.graphs:
             self.graphs.move_to_end(key)
             return self.graphs[key]
@@ -223,7 +242,7 @@ class B200Decoder:
         if batch_size * engine.config.num_key_value_heads < 148:
             splits = min(16, max(1, -(-148 // (batch_size * engine.config.num_key_value_heads))))
         bufs = ForwardBuffers(engine.weights, batch_size, fp8=self.fp8_mlp or self.fp8_lm_head, attn_splits=splits)
-        entry = _DecodeGraph(cache, state.input_tokens, logits, None, state.active, state, bufs)
+        entry = _DecodeGraph(cache, state.input_tokens, logits, None, state.active, state, bufs, filtered=filtered)
         # All rows are dead (alive = pending = 0) while warming up and capturing, so neither run
         # touches KV pages, conv taps, logits or bookkeeping.
         stream, current = self._capture_stream, torch.cuda.current_stream(engine.device)
@@ -265,13 +284,17 @@ class B200Decoder:
         cache_len = int(max_seqlen) + sampling.max_new_tokens
         if cache_len > engine.max_model_len:
             raise ValueError(f"max_seq_len={cache_len} exceeds engine max_model_len={engine.max_model_len}")
-        if sampling.top_k or sampling.top_p != 1.0 or sampling.repetition_penalty != 1.0:
-            raise NotImplementedError("filtered sampling (top-k / top-p / repetition penalty) is not on the fused path")
-        if sampling.stop_token_sequences or sampling.behavior_topk:
-            raise NotImplementedError("stop_token_sequences / behavior_topk are not on the fused path")
+        if sampling.repetition_penalty != 1.0:
+            raise NotImplementedError("repetition penalties are not on the fused path")
+        filtered = sampling.temperature > 0.0 and (0 < sampling.top_k < engine.config.vocab_size or sampling.top_p < 1.0)
+        if sampling.behavior_topk:
+            raise NotImplementedError("behavior_topk heads are not on the fused path")
+        if sampling.stop_token_sequences and sampling.stop_table is not None:
+            raise NotImplementedError("stop_token_sequences together with a stop_table would need their product "
+                                      "automaton; pass one of them")
         flat_ids, prompt_lengths = engine._split_lengths(input_ids, cu_seqlens, max_seqlen)
         n_prompts, batch = len(prompt_lengths), len(prompt_lengths) * repeats
-        entry = self._get_graph(batch, cache_len, masked=self.adaptive_batching)
+        entry = self._get_graph(batch, cache_len, masked=self.adaptive_batching, filtered=filtered)
         cache, state, dev = entry.cache, entry.state, engine.device
         cache.release(torch.ones(batch, device=dev, dtype=torch.uint8))
         cache.conv_state.zero_()
@@ -286,14 +309,18 @@ class B200Decoder:
             cache.fork(src, dst, lens)
             entry.logits[dst.long()] = entry.logits[src.long()]
         stop_offset = 0
-        if sampling.stop_table is not None or sampling.stop_token_ids:
+        if sampling.stop_table is not None or sampling.stop_token_ids or sampling.stop_token_sequences:
             stop_offset = state.add_stop_table(build_token_stop_table(sampling, engine.config.vocab_size, dev))
         vocab = engine.config.vocab_size
         state.configure(list(range(batch)), limits=sampling.max_new_tokens, seeds=int(sampling.seed) & 0x7FFFFFFFFFFFFFFF,
                         temperatures=float(sampling.temperature), ignore_eos=int(sampling.ignore_eos),
                         stop_offsets=stop_offset, rng_offsets=[row * vocab for row in range(batch)],
                         force_eos_at=self.debug_force_eos_at)
-        fixed_length = sampling.ignore_eos and not sampling.stop_token_ids and sampling.stop_table is None
+        if filtered:
+            state.top_k.fill_(int(sampling.top_k))
+            state.top_p.fill_(float(sampling.top_p))
+        fixed_length = (sampling.ignore_eos and not sampling.stop_token_ids and not sampling.stop_token_sequences
+                        and sampling.stop_table is None)
         interval = self.finish_check_interval if batch >= 16 else 1
         self._sample_only(entry)
         timing = self.profile_decode
@@ -345,8 +372,12 @@ class _EagerStep:
 def build_token_stop_table(sampling: LFM25SamplingConfig, vocab: int, device) -> torch.Tensor:
     """Stop ids folded into a (copy of the) stop table as ``matched`` entries, as the reference
     session does (src/climbing_gym/inference/lfm25_session.py:228-241)."""
-    table = (torch.zeros((1, vocab), dtype=torch.int32, device=device) if sampling.stop_table is None
-             else sampling.stop_table.to(device).clone())
+    if sampling.stop_table is not None:
+        table = sampling.stop_table.to(device).clone()
+    elif sampling.stop_token_sequences:  # suffix match on the generated ids, as an automaton over token ids
+        table = build_token_sequence_table(sampling.stop_token_sequences, vocab).to(device)
+    else:
+        table = torch.zeros((1, vocab), dtype=torch.int32, device=device)
     if sampling.stop_token_ids:
         table[:, list(sampling.stop_token_ids)] = 65536
     return table

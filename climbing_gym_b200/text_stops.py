@@ -53,3 +53,29 @@ def build_stop_table(tokenizer, stops, *, vocab_size=None) -> torch.Tensor:
 def advance_text_stops(table, states, tokens, reasons):
     value = table[states, tokens].long()
     return value & 65535, torch.where((reasons == 0) & (value >= 65536), 2, reasons)
+
+
+def build_token_sequence_table(sequences, vocab_size: int) -> torch.Tensor:
+    """The same table format for stop TOKEN sequences (``LFM25SamplingConfig.stop_token_sequences``):
+    generation stops when the generated ids end with any of the sequences, the match the reference
+    makes with ``apply_sequence_stops`` on the token history
+    (src/climbing_gym/inference/lfm25_engine.py:1620-1626). States are the proper prefixes of the
+    sequences (an Aho-Corasick automaton over token ids); only ids that occur in a sequence ever leave
+    state 0, so the table is filled column by column for those ids alone."""
+    patterns = [tuple(int(t) for t in s) for s in sequences]
+    if any(not p for p in patterns):
+        raise ValueError("Stop token sequences must be nonempty")
+    if any(not 0 <= t < vocab_size for p in patterns for t in p):
+        raise ValueError("Stop token outside the model vocabulary")
+    states = sorted({()} | {p[:i] for p in patterns for i in range(1, len(p))}, key=lambda s: (len(s), s))
+    if len(states) >= 65536:
+        raise ValueError("Too many stop-prefix states")
+    index = {state: i for i, state in enumerate(states)}
+    table = np.zeros((len(states), int(vocab_size)), dtype=np.int32)
+    for state in states:
+        for token in {t for p in patterns for t in p}:
+            history = state + (token,)
+            matched = any(history[-len(p):] == p for p in patterns if len(p) <= len(history))
+            longest = next(history[cut:] for cut in range(len(history) + 1) if history[cut:] in index)
+            table[index[state], token] = index[longest] + (65536 if matched else 0)
+    return torch.from_numpy(table)

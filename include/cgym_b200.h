@@ -201,6 +201,8 @@ typedef struct {
   const int64_t* rng_offsets; /* Philox counter base per slot: row*vocab (batch keying) or 0 */
   const int32_t* force_eos_at; /* optional: generated position whose token becomes EOS, -1 none */
   int32_t* seq_lens;      /* cache length per slot; advanced here for rows in `advance` */
+  const float* min_logits; /* optional: per slot, logits below this value cannot be drawn (top-k / top-p
+                              support from cgym_filter_thresholds); they still count in the log-prob */
   int32_t capacity;
   int32_t eos_token_id;
 } cgym_slot_state;
@@ -225,6 +227,19 @@ int cgym_sample(int64_t* tokens, float* logprobs, const void* logits, const int6
 /* Bytes of sampler workspace for `rows` rows (the scores / indices / maxima / totals scratch of
  * lfm25_sampling.py:77-80 plus one arrival counter per row). */
 int64_t cgym_sample_workspace_bytes(int rows);
+
+/* _apply_top_k_top_p (lfm25_engine.py:1759-1775) as a per-row value threshold for the fused sampler:
+ * min_logits[r] = the smallest raw logit that stays drawable after top-k (keep logits >= the k-th
+ * largest; top_k[r] <= 0 or >= vocab disables) and then top-p over the tempered softmax of what is
+ * left (keep the values whose inclusive cumulative probability, in descending order, is <= top_p[r];
+ * the most probable value always stays; top_p[r] >= 1 disables). A group of equal logits at the top-p
+ * boundary is kept or dropped as a whole (torch.sort splits it arbitrarily). Rows with temperature 0
+ * or no filter get -inf. One CTA per row, order-preserving bit-wise search with deterministic block
+ * reductions (no float atomics), vocab <= 65536 per 1024 threads * 64. alive (uint8, optional) skips
+ * dead rows. Feed the result to cgym_sample_record through cgym_slot_state.min_logits. */
+int cgym_filter_thresholds(float* min_logits, const void* logits, const float* temperatures,
+                           const int32_t* top_k, const float* top_p, const uint8_t* alive, int rows,
+                           int vocab, int dtype, cgym_stream_t stream);
 
 /* cgym_sample for callers that cannot hand over a workspace and must not cause a device
  * allocation: it has no counterpart in the reference, whose sampler allocates its slice scratch

@@ -287,3 +287,25 @@ def test_chains_resume_exact_extensions_and_readmit_everything_else():
     assert len(set(seeds)) == len(seeds)  # every (chain, phase) draws from its own stream
     assert adapter.last_session_stats["admitted_requests"] == 4 and log[-1] == ("closed",)
     assert asyncio.run(adapter.generate_chains([], on_result=on_result, max_new_tokens=2)) == []
+
+
+def test_stop_token_sequence_automaton_matches_suffix_search():
+    import random
+
+    from climbing_gym_b200.text_stops import build_token_sequence_table
+
+    patterns = [(5, 6, 7), (6, 8), (9,), (5, 5, 6)]
+    table = build_token_sequence_table(patterns, 16)
+    assert table.dtype == torch.int32 and table.shape[1] == 16
+    rng = random.Random(0)
+    for _ in range(500):
+        history, state = [rng.choice([5, 6, 7, 8, 9, 1]) for _ in range(14)], 0
+        for end, token in enumerate(history, 1):
+            value = int(table[state, token])
+            state = value & 65535
+            want = any(len(p) <= end and tuple(history[end - len(p):end]) == p for p in patterns)
+            assert (value >= 65536) == want, (history, end)
+    with pytest.raises(ValueError, match="nonempty"):
+        build_token_sequence_table([()], 16)
+    with pytest.raises(ValueError, match="vocabulary"):
+        build_token_sequence_table([(3, 99)], 16)

@@ -271,3 +271,31 @@ def test_weight_sync_keeps_addresses_and_validates_first(dev):
     with pytest.raises(ValueError, match="shape mismatch"):
         engine.sync_from_model(Model(broken, cfg))
     assert torch.equal(snapshot, engine.weights.embed_tokens), "nothing may be copied before validation passes"
+
+
+def test_stop_token_sequences_end_generation_at_the_matched_suffix(dev):
+    """Greedy fp32 run, then the same run with stop sequences taken from its own output: every row
+    must stop (reason 2) right after the earliest completed sequence and keep the tokens up to it."""
+    engine = make_engine(dev, dtype=torch.float32)
+    plain = engine.generate(*flat(PROMPTS, dev), repeats=1, sampling=LFM25SamplingConfig(temperature=0.0, max_new_tokens=24))
+    free = plain.token_ids.cpu().numpy()[:, 0]
+    # a bigram of row 0 (positions 5, 6), a trigram of row 3 (positions 9..11) and row 5's very first token
+    stops = (tuple(int(t) for t in free[0, 5:7]), tuple(int(t) for t in free[3, 9:12]), (int(free[5, 0]),))
+    out = engine.generate(*flat(PROMPTS, dev), repeats=1,
+                          sampling=LFM25SamplingConfig(temperature=0.0, max_new_tokens=24, stop_token_sequences=stops))
+    tokens, lengths = out.token_ids.cpu().numpy()[:, 0], out.lengths.cpu().numpy()[:, 0]
+    reasons = out.finish_reasons.cpu().numpy()[:, 0]
+    for row in range(len(PROMPTS)):
+        history, want_len = list(free[row]), 24
+        for end in range(1, 25):
+            if any(len(s) <= end and tuple(history[end - len(s):end]) == s for s in stops):
+                want_len = end
+                break
+        assert lengths[row] == want_len, (row, lengths[row], want_len)
+        assert list(tokens[row, :want_len]) == history[:want_len]
+        assert reasons[row] == (2 if want_len < 24 or any(tuple(history[24 - len(s):24]) == s for s in stops) else 3)
+    assert lengths[0] <= 7 and lengths[3] <= 12 and lengths[5] == 1
+    with pytest.raises(NotImplementedError, match="product"):
+        engine.generate(*flat(PROMPTS, dev), repeats=1, sampling=LFM25SamplingConfig(
+            temperature=0.0, max_new_tokens=4, stop_token_sequences=stops,
+            stop_table=torch.zeros((1, 4096), dtype=torch.int32)))
