@@ -47,12 +47,12 @@ WORKLOADS = {
     "fp8kv-long32x1024": ("1p2b", 32, 16384, 30720, 1024, {"fp8_kv": True}),
 }
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum over the 140 kernels of ONE decode-step
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum over the 139 kernels of ONE decode-step
 # replay, one ncu capture) divided by the step's algorithmic bytes at the captured sequence lengths:
-# 2.9099 GB measured for 2.7678 GB (profiles/decode_step_bf16_b64_dram_traffic.md). Both grow with the
+# 2.9113 GB measured for 2.7678 GB (profiles/decode_step_bf16_b64_dram_traffic.md). Both grow with the
 # same two terms (weights once, KV history once), so `roofline.traffic` scales the full-size
 # algorithmic bytes by this ratio.
-DRAM_TRAFFIC_RATIO = {"bf16-b64x512": 1.0513}
+DRAM_TRAFFIC_RATIO = {"bf16-b64x512": 1.0518}
 
 # Continuous batching through a generation session: a queue of requests served by a fixed number of
 # live slots; a finished request's slot is refilled from the queue at the next poll.
