@@ -336,6 +336,98 @@ filter_threshold_kernel(float* __restrict__ min_logits, const T* __restrict__ lo
   if (threadIdx.x == 0) min_logits[row] = tau == 0u ? -INFINITY : key_value(tau);
 }
 
+// ---- behaviour head: the k most probable tokens of the unfiltered distribution -----------------------
+// Per live row: log Z (max + log-sum-exp), the key of the k-th largest logit by the same bit-wise
+// search, the ties at that key resolved towards the lowest token ids (a second search, on the index),
+// then exactly k candidates are gathered and sorted by (logit descending, id ascending) with a
+// bitonic network in shared memory. Deterministic throughout.
+constexpr int HEAD_MAX_K = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(FILTER_THREADS)
+topk_head_kernel(int32_t* __restrict__ out_ids, float* __restrict__ out_logprobs, const T* __restrict__ logits,
+                 const uint8_t* __restrict__ alive, const int32_t* __restrict__ lengths, int vocab, int capacity,
+                 int k) {
+  constexpr bool HALF = sizeof(T) == 2;
+  constexpr int LOW_BIT = HALF ? 16 : 0;
+  extern __shared__ uint16_t staged[];
+  __shared__ float scratch[32];
+  __shared__ unsigned long long picked[HEAD_MAX_K];
+  __shared__ int n_picked;
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x;
+  const int position = lengths != nullptr ? lengths[row] : 0;
+  if ((alive != nullptr && !alive[row]) || position >= capacity) return;  // uniform per CTA
+  const T* x = logits + static_cast<int64_t>(row) * vocab;
+  if (HALF) {
+    for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) staged[i] = static_cast<uint16_t>(ordered_key(Elem<T>::load(x + i)) >> 16);
+  }
+  if (threadIdx.x < HEAD_MAX_K) picked[threadIdx.x] = 0ull;
+  if (threadIdx.x == 0) n_picked = 0;
+  __syncthreads();
+  auto key_at = [&](int i) -> uint32_t {
+    if (HALF) return static_cast<uint32_t>(staged[i]) << 16;
+    return ordered_key(Elem<T>::load(x + i));
+  };
+  // log Z
+  float top = -INFINITY;
+  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) top = fmaxf(top, key_value(key_at(i)));
+  top = block_max(top, scratch);
+  float mass = 0.0f;
+  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) mass += expf(key_value(key_at(i)) - top);
+  const float log_z = top + logf(block_sum(mass, scratch));
+  // key of the k-th largest logit
+  uint32_t tau = 0u;
+  for (int bit = 31; bit >= LOW_BIT; --bit) {
+    const uint32_t probe = tau | (1u << bit);
+    float count = 0.0f;
+    for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) count += key_at(i) >= probe ? 1.0f : 0.0f;
+    if (block_sum(count, scratch) >= static_cast<float>(k)) tau = probe;
+  }
+  float above = 0.0f;
+  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) above += key_at(i) > tau ? 1.0f : 0.0f;
+  const int need = k - static_cast<int>(block_sum(above, scratch));  // ties at tau to take, >= 1
+  // the largest index such that at most `need` ties lie at or below it: ties are taken in id order
+  int last_tie = 0;
+  for (int bit = 30; bit >= 0; --bit) {
+    const int probe = last_tie | (1 << bit);
+    if (probe >= vocab) continue;
+    float below = 0.0f;  // ties with index < probe
+    for (int i = threadIdx.x; i < vocab && i < probe; i += FILTER_THREADS) below += key_at(i) == tau ? 1.0f : 0.0f;
+    if (block_sum(below, scratch) < static_cast<float>(need)) last_tie = probe;
+  }
+  // gather exactly k candidates as (key, ~index) so that one descending sort orders ties by ascending id
+  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) {
+    const uint32_t key = key_at(i);
+    if (key > tau || (key == tau && i <= last_tie)) {
+      const int slot = atomicAdd(&n_picked, 1);
+      if (slot < HEAD_MAX_K) picked[slot] = (static_cast<unsigned long long>(key) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(i));
+    }
+  }
+  __syncthreads();
+  // bitonic sort of 128 entries, descending (empty entries are 0 and sink to the end)
+  for (int size = 2; size <= HEAD_MAX_K; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (threadIdx.x < HEAD_MAX_K) {
+        const int partner = threadIdx.x ^ stride;
+        if (partner > static_cast<int>(threadIdx.x)) {
+          const bool descending = (threadIdx.x & size) == 0;
+          const unsigned long long a = picked[threadIdx.x], b = picked[partner];
+          if ((a < b) == descending) { picked[threadIdx.x] = b; picked[partner] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x < k) {
+    const unsigned long long entry = picked[threadIdx.x];
+    const int64_t at = (static_cast<int64_t>(row) * capacity + position) * k + threadIdx.x;
+    out_ids[at] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(entry & 0xFFFFFFFFull));
+    out_logprobs[at] = key_value(static_cast<uint32_t>(entry >> 32)) - log_z;
+  }
+}
+
 }  // namespace cgym
 
 using namespace cgym;
@@ -369,6 +461,38 @@ extern "C" int cgym_filter_thresholds(float* min_logits, const void* logits, con
     return fail("filter_thresholds: unsupported logits dtype %d", dtype);
   }
   return check_launch("filter_thresholds");
+}
+
+extern "C" int cgym_topk_head(int32_t* out_ids, float* out_logprobs, const void* logits, const uint8_t* alive,
+                              const int32_t* lengths, int n_slots, int vocab, int capacity, int k, int dtype,
+                              cgym_stream_t stream) {
+  CGYM_REQUIRE(out_ids && out_logprobs && logits && n_slots >= 0 && vocab > 0 && capacity > 0, "topk_head: bad arguments");
+  CGYM_REQUIRE(k > 0 && k <= HEAD_MAX_K && k <= vocab, "topk_head: k must be in [1, min(vocab, %d)]", HEAD_MAX_K);
+  CGYM_REQUIRE(vocab <= FILTER_THREADS * 64, "topk_head: vocabularies up to %d entries", FILTER_THREADS * 64);
+  if (n_slots == 0) return 0;
+  if (dtype == CGYM_BF16) {
+    const int smem = vocab * static_cast<int>(sizeof(uint16_t));
+    static std::mutex mutex;
+    static int reserved = 0;
+    {
+      std::lock_guard<std::mutex> lock(mutex);
+      if (smem > reserved) {
+        const cudaError_t rc = cudaFuncSetAttribute(topk_head_kernel<__nv_bfloat16>,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        CGYM_REQUIRE(rc == cudaSuccess, "topk_head: cannot reserve %d bytes of shared memory: %s", smem,
+                     cudaGetErrorString(rc));
+        reserved = smem;
+      }
+    }
+    launch_dependent(topk_head_kernel<__nv_bfloat16>, dim3(n_slots), dim3(FILTER_THREADS), smem, as_stream(stream), out_ids,
+                     out_logprobs, static_cast<const __nv_bfloat16*>(logits), alive, lengths, vocab, capacity, k);
+  } else if (dtype == CGYM_F32) {
+    launch_dependent(topk_head_kernel<float>, dim3(n_slots), dim3(FILTER_THREADS), 0, as_stream(stream), out_ids,
+                     out_logprobs, static_cast<const float*>(logits), alive, lengths, vocab, capacity, k);
+  } else {
+    return fail("topk_head: unsupported logits dtype %d", dtype);
+  }
+  return check_launch("topk_head");
 }
 
 extern "C" int64_t cgym_sample_workspace_bytes(int rows) {

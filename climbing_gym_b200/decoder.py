@@ -69,6 +69,15 @@ class SlotState:
 
         self.struct = struct(None)                      # full-support sampling
         self.struct_filtered = struct(self.min_logits)  # draws restricted to logits >= min_logits[slot]
+        self.head_k, self.head_ids, self.head_logprobs = 0, None, None
+
+    def allocate_heads(self, k: int, positions: int) -> None:
+        """Behaviour head buffers [slots][positions][k] (ids int32, log-probs fp32), filled by cgym_topk_head;
+        ``positions`` bounds the tokens one request generates, not its context."""
+        dev = self.lengths.device
+        self.head_k, self.head_positions = k, positions
+        self.head_ids = torch.zeros((self.n_slots, positions, k), device=dev, dtype=torch.int32)
+        self.head_logprobs = torch.zeros((self.n_slots, positions, k), device=dev, dtype=torch.float32)
 
     def reset(self) -> None:
         for t in (self.lengths, self.limits, self.reasons, self.alive, self.pending, self.ignore_eos,
@@ -77,6 +86,9 @@ class SlotState:
             t.zero_()
         self.force_eos_at.fill_(-1)
         self.stop_table_used = self.vocab
+        if self.head_k:
+            self.head_ids.zero_()
+            self.head_logprobs.zero_()
 
     def add_stop_table(self, table: torch.Tensor) -> int:
         """Append a [states, vocab] int32 table to the arena; returns its element offset."""
@@ -210,6 +222,9 @@ class B200Decoder:
         src/climbing_gym/inference/lfm25_cuda.py:311-324)."""
         state, n, vocab = entry.state, entry.cache.n_slots, self.engine.config.vocab_size
         dtype = nv.dtype_code(entry.logits.dtype)
+        if state.head_k:  # behaviour head of the unfiltered distribution, recorded at the row's current length
+            nv.call("cgym_topk_head", nv.ptr(state.head_ids), nv.ptr(state.head_logprobs), nv.ptr(entry.logits),
+                    nv.ptr(state.alive), nv.ptr(state.lengths), n, vocab, state.head_positions, state.head_k, dtype, stream)
         if entry.filtered:
             nv.call("cgym_filter_thresholds", nv.ptr(state.min_logits), nv.ptr(entry.logits), nv.ptr(state.temperatures),
                     nv.ptr(state.top_k), nv.ptr(state.top_p), nv.ptr(state.alive), n, vocab, dtype, stream)
@@ -222,12 +237,15 @@ class B200Decoder:
         self._sample(entry, None, nv.stream_ptr(self.engine.device))
 
     @torch.inference_mode()
-    def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False, filtered: bool = False) -> _DecodeGraph:
+    def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False, filtered: bool = False,
+                   head_k: int = 0, head_positions: int = 0) -> _DecodeGraph:
         engine = self.engine
         alignment = 32 if batch_size >= 64 else 128
         alignment = max(alignment, self.page_size)
         capacity = min(engine.max_model_len, -(-cache_len // alignment) * alignment)
-        key = (batch_size, capacity, masked, "filtered") if filtered else (batch_size, capacity, masked)
+        head_positions = min(capacity, -(-head_positions // 64) * 64) if head_k else 0
+        key = (batch_size, capacity, masked) + (("filtered",) if filtered else ())
+        key += (f"head{head_k}x{head_positions}",) if head_k else ()
         if key in self.graphs:
             self.graphs.move_to_end(key)
             return self.graphs[key]
@@ -237,6 +255,8 @@ class B200Decoder:
         cache = engine._empty_cache(max_slots=batch_size, max_seq_len=capacity, fp8_kv=self.fp8_kv,
                                     page_size=self.page_size)
         state = SlotState(batch_size, capacity, engine.config.vocab_size, int(engine.config.eos_token_id), cache.seq_lens)
+        if head_k:
+            state.allocate_heads(head_k, head_positions)
         logits = torch.zeros((batch_size, engine.config.vocab_size), device=engine.device, dtype=engine.dtype)
         splits = 1
         if batch_size * engine.config.num_key_value_heads < 148:
@@ -287,14 +307,16 @@ class B200Decoder:
         if sampling.repetition_penalty != 1.0:
             raise NotImplementedError("repetition penalties are not on the fused path")
         filtered = sampling.temperature > 0.0 and (0 < sampling.top_k < engine.config.vocab_size or sampling.top_p < 1.0)
-        if sampling.behavior_topk:
-            raise NotImplementedError("behavior_topk heads are not on the fused path")
+        head_k = sampling.behavior_topk
+        if head_k > engine.config.vocab_size:
+            raise ValueError("Behavior head exceeds the vocabulary")
         if sampling.stop_token_sequences and sampling.stop_table is not None:
             raise NotImplementedError("stop_token_sequences together with a stop_table would need their product "
                                       "automaton; pass one of them")
         flat_ids, prompt_lengths = engine._split_lengths(input_ids, cu_seqlens, max_seqlen)
         n_prompts, batch = len(prompt_lengths), len(prompt_lengths) * repeats
-        entry = self._get_graph(batch, cache_len, masked=self.adaptive_batching, filtered=filtered)
+        entry = self._get_graph(batch, cache_len, masked=self.adaptive_batching, filtered=filtered, head_k=head_k,
+                                head_positions=sampling.max_new_tokens)
         cache, state, dev = entry.cache, entry.state, engine.device
         cache.release(torch.ones(batch, device=dev, dtype=torch.uint8))
         cache.conv_state.zero_()
@@ -345,7 +367,9 @@ class B200Decoder:
             token_ids=state.tokens[:, :n_new].reshape(*shape, n_new).clone(),
             lengths=state.lengths.reshape(shape).clone(),
             logprobs=state.logprobs[:, :n_new].reshape(*shape, n_new).clone() if sampling.return_logprobs else None,
-            finish_reasons=reasons.reshape(shape))
+            finish_reasons=reasons.reshape(shape),
+            topk_token_ids=state.head_ids[:, :n_new].reshape(*shape, n_new, head_k).clone() if head_k else None,
+            topk_logprobs=state.head_logprobs[:, :n_new].reshape(*shape, n_new, head_k).clone() if head_k else None)
 
 
 class _StepGraph:

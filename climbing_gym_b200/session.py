@@ -70,10 +70,9 @@ class LFM25GenerationSession:
         self.batch_size, self.max_new_tokens = max_batch_size, max_new_tokens
         if type(behavior_topk) is not int or not 0 <= behavior_topk <= min(128, self.engine.config.vocab_size):
             raise ValueError("behavior_topk must be an integer between 0 and min(vocab, 128)")
-        if behavior_topk:
-            raise NotImplementedError("behavior_topk heads are not on the fused path")
         self.behavior_topk = behavior_topk
-        self.entry = decoder._get_graph(max_batch_size, cache_len or self.engine.max_model_len, masked=True)
+        self.entry = decoder._get_graph(max_batch_size, cache_len or self.engine.max_model_len, masked=True,
+                                        head_k=behavior_topk, head_positions=max_new_tokens)
         self.state, self.cache = self.entry.state, self.entry.cache
         self.cache.release(torch.ones(max_batch_size, device=self.engine.device, dtype=torch.uint8))
         self.cache.conv_state.zero_()
@@ -307,9 +306,12 @@ class LFM25GenerationSession:
             ids = tuple(ids[:length])
             handle = LFM25ContinuationHandle(self, slot, request.version, request.prompt + ids)
             request.handle = handle
+            k = request.sampling.behavior_topk
+            head = (BehaviorTopK(self.state.head_ids[slot, :length, :k].cpu(),
+                                 self.state.head_logprobs[slot, :length, :k].cpu()) if k else None)
             results.append(LFM25SessionResult(handle, request.prompt, ids,
                                               tuple(probs[:length]) if request.sampling.return_logprobs else None,
-                                              reasons[slot], None))
+                                              reasons[slot], head))
         return results
 
     @torch.inference_mode()

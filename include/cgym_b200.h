@@ -260,6 +260,16 @@ int cgym_sample_static(int64_t* tokens, float* logprobs, const void* logits, con
                        const int64_t* steps, const float* temperatures, const int64_t* rng_offsets,
                        int rows, int vocab, int dtype, cgym_stream_t stream);
 
+/* behavior_topk + _record_head (lfm25_sampling.py:127-149, lfm25_session.py:22-31): for every live
+ * slot, the k <= 128 most probable tokens of the UNFILTERED distribution, as ids (int32) and
+ * log-probs (logit - logsumexp), sorted by descending logit (equal logits by ascending id), written
+ * at out[slot][lengths[slot]][0..k) of buffers shaped [n_slots][capacity][k]. Run it before
+ * cgym_sample_record of the same step (which advances lengths). alive / lengths optional (all live /
+ * position 0). The head is metadata: it never changes the draw. */
+int cgym_topk_head(int32_t* out_ids, float* out_logprobs, const void* logits, const uint8_t* alive,
+                   const int32_t* lengths, int n_slots, int vocab, int capacity, int k, int dtype,
+                   cgym_stream_t stream);
+
 /* Chunked-head completion scoring (lfm25_engine.py:1150-1154): logit[target] - logsumexp. */
 int cgym_target_logprobs(float* out, const void* logits, const int64_t* targets, int rows,
                          int vocab, int dtype, cgym_stream_t stream);

@@ -126,3 +126,25 @@ def record_sample(sampled, logp, st, *, eos, vocab):
         st["alive"][row] = reason == 0
         st["pending"][row] = reason == 0
         st["input"][row] = token
+
+
+def behavior_head(logits, selected, logp, k):
+    """lfm25_sampling.py:127-149: the k largest logits of every row (descending; torch.topk leaves the
+    order of equal values open, this restatement takes the lowest ids first) and their log-probs
+    against the partition function the sampler already produced: log Z = logit[selected] - logp."""
+    logits = np.asarray(logits, np.float32)
+    if not 0 < k <= min(logits.shape[1], 128):
+        raise ValueError("Behavior head exceeds the vocabulary or supported size")
+    ids = np.stack([np.lexsort((np.arange(row.size), -row))[:k] for row in logits]).astype(np.int32)
+    values = np.take_along_axis(logits, ids, 1)
+    log_z = logits[np.arange(len(logits)), np.asarray(selected)] - np.asarray(logp, np.float32)
+    return ids, (values - log_z[:, None]).astype(np.float32)
+
+
+def record_head(ids, probs, out_ids, out_probs, lengths, alive):
+    """lfm25_session.py:20-30: live rows store their head at [row, lengths[row]] (before record_sample
+    advances the length)."""
+    for row in range(len(ids)):
+        if alive[row]:
+            out_ids[row, int(lengths[row])] = ids[row]
+            out_probs[row, int(lengths[row])] = probs[row]

@@ -254,13 +254,46 @@ def kernel_vectors():
     return out
 
 
+def head_vectors():
+    """Reference behaviour head (torch.topk + its Triton log-prob kernel) and the session's head recorder,
+    fed by the reference sampler's own tokens and log-probs. Rows of distinct logits, so that the order
+    torch.topk returns is determined."""
+    from climbing_gym.inference import lfm25_sampling as ref
+    from climbing_gym.inference import lfm25_session as ss
+
+    rng = np.random.default_rng(8)
+    batch, vocab = 5, 9000
+    logits = torch.from_numpy((rng.standard_normal((batch, vocab)) * 2.0).astype(np.float32))
+    parts = -(-vocab // 4096)
+    scores = torch.empty((batch, parts)); indices = torch.empty((batch, parts), dtype=torch.int32)
+    maxima = torch.empty_like(scores); totals = torch.empty_like(scores)
+    tokens = torch.empty(batch, dtype=torch.long); logp = torch.empty(batch)
+    key = (21 + 3 * 0x9E3779B97F4A7C15) & 0x7FFFFFFFFFFFFFFF
+    ref._partial_sample[(batch, parts)](logits, scores, indices, maxima, totals, key, vocab, parts, 1.0, True, 4096)
+    ref._finish_sample[(batch,)](logits, scores, indices, maxima, totals, tokens, logp, vocab, parts, True, 4)
+    out = {"batch": batch, "vocab": vocab, "seed": 21, "step": 3, "tokens": tokens.tolist(),
+           "logprobs": [round(float(x), 6) for x in logp], "heads": []}
+    for k in (1, 5, 128):
+        ids, probs = ref.behavior_topk(logits, tokens, logp, k)
+        out["heads"].append(dict(k=k, ids=ids.tolist(), logprobs=[[round(float(x), 6) for x in row] for row in probs]))
+    k, cap = 5, 4
+    ids, probs = ref.behavior_topk(logits, tokens, logp, k)
+    lengths = torch.tensor([0, 3, 1, 2, 0], dtype=torch.int32)
+    alive = torch.tensor([True, True, False, True, True])
+    out_ids = torch.zeros((batch, cap, k), dtype=torch.int32); out_probs = torch.zeros((batch, cap, k))
+    ss._record_head[(batch,)](ids.to(torch.int32), probs, out_ids, out_probs, lengths, alive, k, cap, 8)
+    out["record_head"] = dict(k=k, capacity=cap, lengths=lengths.tolist(), alive=alive.tolist(), ids=out_ids.tolist(),
+                              logprobs=[[[round(float(x), 6) for x in r] for r in slot] for slot in out_probs])
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default="/root/reference/src")
     parser.add_argument("--only", default="")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
-    jobs = dict(model=model_vectors, sampler=sampler_vectors, kernels=kernel_vectors)
+    jobs = dict(model=model_vectors, sampler=sampler_vectors, kernels=kernel_vectors, head=head_vectors)
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
             continue

@@ -145,6 +145,27 @@ def test_sampler_matches_reference_kernels(golden):
         assert np.allclose(logp, case["logprobs"], atol=3e-6), case
 
 
+def test_behavior_head_matches_reference(golden):
+    g = golden("head")
+    batch, vocab = g["batch"], g["vocab"]
+    logits = (np.random.default_rng(8).standard_normal((batch, vocab)) * 2.0).astype(np.float32)
+    tokens, logp = OracleEngine.sample(None, logits, temperature=1.0, seed=g["seed"], step=g["step"])
+    assert tokens.tolist() == g["tokens"] and np.allclose(logp, g["logprobs"], atol=3e-6)
+    for case in g["heads"]:
+        ids, probs = ok.behavior_head(logits, tokens, logp, case["k"])
+        assert ids.tolist() == case["ids"], case["k"]
+        assert np.allclose(probs, case["logprobs"], atol=5e-6), case["k"]
+    rec = g["record_head"]
+    ids, probs = ok.behavior_head(logits, tokens, logp, rec["k"])
+    out_ids = np.zeros((batch, rec["capacity"], rec["k"]), np.int32)
+    out_probs = np.zeros(out_ids.shape, np.float32)
+    ok.record_head(ids, probs, out_ids, out_probs, np.array(rec["lengths"]), np.array(rec["alive"]))
+    assert out_ids.tolist() == rec["ids"]
+    assert np.allclose(out_probs, rec["logprobs"], atol=5e-6)
+    with pytest.raises(ValueError):
+        ok.behavior_head(logits, tokens, logp, 129)
+
+
 def test_philox_known_answer():
     # Random123 known-answer: counter 0, key 0 -> first word of philox4x32-10
     assert int(philox.philox4x32_10(np.array([0]), 0)[0]) == 0x6627E8D5
