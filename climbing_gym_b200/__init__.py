@@ -11,6 +11,7 @@ _LAZY = {
     "LFM25Engine": "engine", "flatten_token_batches": "engine",
     "LFM25PackedWeights": "weights", "describe_lfm25_checkpoint": "weights",
     "LFM25GenerationSession": "session", "LFM25ContinuationHandle": "session", "LFM25SessionResult": "session",
+    "LFM25PrefixSnapshot": "session",
     "LFM25GenerationOutput": "types", "LFM25PrefixBatch": "types", "LFM25DecodeBatch": "types",
     "LFM25StepOutput": "types", "GenerationOutput": "types", "GenerationResult": "types", "BehaviorTopK": "types",
     "PagedHybridCache": "paged", "LFM25HybridCache": "paged",

@@ -295,6 +295,11 @@ filter_threshold_kernel(float* __restrict__ min_logits, const T* __restrict__ lo
     if (HALF) return static_cast<uint32_t>(staged[i]) << 16;
     return ordered_key(Elem<T>::load(x + i));
   };
+  // a 16-bit key stands for a bf16 value: keys of negative values are complemented bits, so the 16
+  // dropped low bits come back as ones before the key is turned into its float again
+  auto value_of = [&](uint32_t key) -> float {
+    return key_value((HALF && !(key & 0x80000000u)) ? (key | 0xFFFFu) : key);
+  };
 
   uint32_t tau_k = 0u;  // keys >= tau_k survive top-k
   if (use_k) {
@@ -310,12 +315,12 @@ filter_threshold_kernel(float* __restrict__ min_logits, const T* __restrict__ lo
     uint32_t top = 0u;
     for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) top = max(top, key_at(i));
     top = block_max_u32(top, uscratch);
-    const float v_top = key_value(top);
+    const float v_top = value_of(top);
     auto mass_from = [&](uint32_t floor_key) {  // tempered softmax mass (relative to the maximum) of keys >= floor_key
       float mass = 0.0f;
       for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) {
         const uint32_t key = key_at(i);
-        if (key >= floor_key) mass += expf(__fdiv_rn(key_value(key) - v_top, temperature));
+        if (key >= floor_key) mass += expf(__fdiv_rn(value_of(key) - v_top, temperature));
       }
       return block_sum(mass, scratch);
     };
@@ -333,7 +338,7 @@ filter_threshold_kernel(float* __restrict__ min_logits, const T* __restrict__ lo
     if (tau_p < over || tau_p > top) tau_p = top;
     tau = max(tau_k, tau_p);
   }
-  if (threadIdx.x == 0) min_logits[row] = tau == 0u ? -INFINITY : key_value(tau);
+  if (threadIdx.x == 0) min_logits[row] = tau == 0u ? -INFINITY : value_of(tau);
 }
 
 // ---- behaviour head: the k most probable tokens of the unfiltered distribution -----------------------
@@ -370,12 +375,17 @@ topk_head_kernel(int32_t* __restrict__ out_ids, float* __restrict__ out_logprobs
     if (HALF) return static_cast<uint32_t>(staged[i]) << 16;
     return ordered_key(Elem<T>::load(x + i));
   };
+  // a 16-bit key stands for a bf16 value: keys of negative values are complemented bits, so the 16
+  // dropped low bits come back as ones before the key is turned into its float again
+  auto value_of = [&](uint32_t key) -> float {
+    return key_value((HALF && !(key & 0x80000000u)) ? (key | 0xFFFFu) : key);
+  };
   // log Z
   float top = -INFINITY;
-  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) top = fmaxf(top, key_value(key_at(i)));
+  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) top = fmaxf(top, value_of(key_at(i)));
   top = block_max(top, scratch);
   float mass = 0.0f;
-  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) mass += expf(key_value(key_at(i)) - top);
+  for (int i = threadIdx.x; i < vocab; i += FILTER_THREADS) mass += expf(value_of(key_at(i)) - top);
   const float log_z = top + logf(block_sum(mass, scratch));
   // key of the k-th largest logit
   uint32_t tau = 0u;
@@ -424,7 +434,7 @@ topk_head_kernel(int32_t* __restrict__ out_ids, float* __restrict__ out_logprobs
     const unsigned long long entry = picked[threadIdx.x];
     const int64_t at = (static_cast<int64_t>(row) * capacity + position) * k + threadIdx.x;
     out_ids[at] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(entry & 0xFFFFFFFFull));
-    out_logprobs[at] = key_value(static_cast<uint32_t>(entry >> 32)) - log_z;
+    out_logprobs[at] = value_of(static_cast<uint32_t>(entry >> 32)) - log_z;
   }
 }
 

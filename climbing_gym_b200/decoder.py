@@ -149,7 +149,7 @@ class B200Decoder:
                  max_prefill_tokens: int = 4096, finish_check_interval: int = 32,
                  skip_finished_attention: bool = True, fp8_mlp: bool = False, fp8_kv: bool = False,
                  adaptive_batching: bool = False, fp8_lm_head: bool = False, page_size: int = 64,
-                 use_cuda_graphs: bool = True):
+                 use_cuda_graphs: bool = True, snapshot_rows: int = 32, snapshot_pages: int | None = None):
         if engine.device.type != "cuda" or engine.dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("LFM2.5 CUDA graphs require CUDA and bfloat16 (or float32) weights")
         cfg = engine.config
@@ -178,6 +178,11 @@ class B200Decoder:
         self.adaptive_batching, self.fp8_lm_head = bool(adaptive_batching), bool(fp8_lm_head)
         self.page_size = page_size
         self.use_cuda_graphs = use_cuda_graphs
+        if snapshot_rows < 0 or (snapshot_pages is not None and snapshot_pages < 0):
+            raise ValueError("snapshot_rows and snapshot_pages must be >= 0")
+        # session caches park prefix snapshots in spare rows of the paged cache; the page reserve defaults to
+        # eight full-length prefixes plus one private tail page per snapshot
+        self.snapshot_rows, self.snapshot_pages = int(snapshot_rows), snapshot_pages
         self.use_pdl = os.environ.get("CGYM_PDL", "1") != "0"
         self.runner = LFM25Runner(engine.weights, engine._rope_cos, engine._rope_sin, fp8_mlp=self.fp8_mlp,
                                   fp8_lm_head=self.fp8_lm_head)
@@ -252,8 +257,13 @@ class B200Decoder:
         if len(self.graphs) >= self.max_graphs:
             self.graphs.popitem(last=False)
         self.runner.prepare_fp8()
+        spare, n_pages = (self.snapshot_rows if masked else 0), None
+        if spare:
+            blocks = -(-capacity // self.page_size)
+            reserve = self.snapshot_pages if self.snapshot_pages is not None else 8 * blocks + spare
+            n_pages = batch_size * blocks + reserve
         cache = engine._empty_cache(max_slots=batch_size, max_seq_len=capacity, fp8_kv=self.fp8_kv,
-                                    page_size=self.page_size)
+                                    page_size=self.page_size, n_pages=n_pages, spare_rows=spare)
         state = SlotState(batch_size, capacity, engine.config.vocab_size, int(engine.config.eos_token_id), cache.seq_lens)
         if head_k:
             state.allocate_heads(head_k, head_positions)

