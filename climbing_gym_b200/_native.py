@@ -74,6 +74,7 @@ SIGNATURES = {
     "cgym_sample_static": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "cgym_filter_thresholds": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "cgym_topk_head": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
+    "cgym_repetition_penalty": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "cgym_target_logprobs": [_P, _P, _P, _I, _I, _I, _P],
     "cgym_step_begin": [C.POINTER(PagePool), _P, _P, _P, _P, _P, _P, _I, _P, _P],
     "cgym_pages_reserve": [C.POINTER(PagePool), _P, _P, _I, _P, _P],

@@ -438,9 +438,78 @@ topk_head_kernel(int32_t* __restrict__ out_ids, float* __restrict__ out_logprobs
   }
 }
 
+// ---- repetition penalty ---------------------------------------------------------------------------------
+// out[row][i] = fp32 logit, with the logits of tokens the row has seen (its prompt and everything it
+// generated) multiplied by the penalty when negative and divided by it otherwise. `seen` is one byte per
+// (row, token); the row's latest token (tokens[row][lengths[row] - 1]) is folded in here and marked for
+// the steps to come, so the sampler needs no hook of its own. grid (ceil(vocab / 2048), rows).
+constexpr int PENALTY_THREADS = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(PENALTY_THREADS)
+repetition_penalty_kernel(float* __restrict__ out, const T* __restrict__ logits, uint8_t* __restrict__ seen,
+                          const int64_t* __restrict__ tokens, const int32_t* __restrict__ lengths,
+                          const uint8_t* __restrict__ alive, const float* __restrict__ penalties, int vocab,
+                          int capacity) {
+  pdl_trigger();
+  pdl_wait();
+  logits = pdl_fresh(logits);  // written by the kernels before this one: no load may move above the wait
+  tokens = pdl_fresh(tokens);
+  lengths = pdl_fresh(lengths);
+  alive = pdl_fresh(alive);
+  const int row = blockIdx.y;
+  if (alive != nullptr && !alive[row]) return;
+  const float penalty = penalties[row];
+  const int length = lengths != nullptr ? min(lengths[row], capacity) : 0;
+  const int latest = (tokens != nullptr && length > 0) ? static_cast<int>(tokens[static_cast<int64_t>(row) * capacity + length - 1]) : -1;
+  const T* x = logits + static_cast<int64_t>(row) * vocab;
+  uint8_t* mark = seen + static_cast<int64_t>(row) * vocab;
+  float* y = out + static_cast<int64_t>(row) * vocab;
+  auto penalised = [&](int i, float v, uint8_t flag) {
+    if (!flag && i != latest) return v;
+    return v < 0.0f ? v * penalty : __fdiv_rn(v, penalty);
+  };
+  const int begin = (blockIdx.x * PENALTY_THREADS + threadIdx.x) * 8;
+  if (begin >= vocab) return;
+  if ((vocab & 7) == 0) {
+    float v[8];
+    load8(x + begin, v);
+    const uint2 flags = *reinterpret_cast<const uint2*>(mark + begin);
+    const uint8_t* f = reinterpret_cast<const uint8_t*>(&flags);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = penalised(begin + j, v[j], f[j]);
+    *reinterpret_cast<float4*>(y + begin) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(y + begin + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    for (int i = begin; i < min(vocab, begin + 8); ++i) y[i] = penalised(i, Elem<T>::load(x + i), mark[i]);
+  }
+  // exactly one thread owns the latest token's byte: it is the one that just read it
+  if (latest >= begin && latest < begin + 8 && latest < vocab) mark[latest] = 1;
+}
+
 }  // namespace cgym
 
 using namespace cgym;
+
+extern "C" int cgym_repetition_penalty(float* out, const void* logits, uint8_t* seen, const int64_t* tokens,
+                                       const int32_t* lengths, const uint8_t* alive, const float* penalties,
+                                       int rows, int vocab, int capacity, int dtype, cgym_stream_t stream) {
+  CGYM_REQUIRE(out && logits && seen && penalties && rows >= 0 && vocab > 0, "repetition_penalty: bad arguments");
+  CGYM_REQUIRE(tokens == nullptr || (lengths != nullptr && capacity > 0),
+               "repetition_penalty: tokens need lengths and a capacity");
+  if (rows == 0) return 0;
+  const dim3 grid((vocab + PENALTY_THREADS * 8 - 1) / (PENALTY_THREADS * 8), rows);
+  if (dtype == CGYM_BF16) {
+    launch_dependent(repetition_penalty_kernel<__nv_bfloat16>, grid, dim3(PENALTY_THREADS), 0, as_stream(stream), out,
+                     static_cast<const __nv_bfloat16*>(logits), seen, tokens, lengths, alive, penalties, vocab, capacity);
+  } else if (dtype == CGYM_F32) {
+    launch_dependent(repetition_penalty_kernel<float>, grid, dim3(PENALTY_THREADS), 0, as_stream(stream), out,
+                     static_cast<const float*>(logits), seen, tokens, lengths, alive, penalties, vocab, capacity);
+  } else {
+    return fail("repetition_penalty: unsupported logits dtype %d", dtype);
+  }
+  return check_launch("repetition_penalty");
+}
 
 extern "C" int cgym_filter_thresholds(float* min_logits, const void* logits, const float* temperatures,
                                       const int32_t* top_k, const float* top_p, const uint8_t* alive, int rows,

@@ -70,6 +70,15 @@ class SlotState:
         self.struct = struct(None)                      # full-support sampling
         self.struct_filtered = struct(self.min_logits)  # draws restricted to logits >= min_logits[slot]
         self.head_k, self.head_ids, self.head_logprobs = 0, None, None
+        self.penalties, self.seen, self.penalised = None, None, None
+
+    def allocate_penalty(self) -> None:
+        """Repetition-penalty buffers: per-slot factor, one seen byte per (slot, token) and the penalised
+        fp32 copy of the step's logits that the sampler reads (cgym_repetition_penalty)."""
+        dev = self.lengths.device
+        self.penalties = torch.ones(self.n_slots, device=dev, dtype=torch.float32)
+        self.seen = torch.zeros((self.n_slots, self.vocab), device=dev, dtype=torch.uint8)
+        self.penalised = torch.zeros((self.n_slots, self.vocab), device=dev, dtype=torch.float32)
 
     def allocate_heads(self, k: int, positions: int) -> None:
         """Behaviour head buffers [slots][positions][k] (ids int32, log-probs fp32), filled by cgym_topk_head;
@@ -89,6 +98,9 @@ class SlotState:
         if self.head_k:
             self.head_ids.zero_()
             self.head_logprobs.zero_()
+        if self.penalties is not None:
+            self.penalties.fill_(1.0)
+            self.seen.zero_()
 
     def add_stop_table(self, table: torch.Tensor) -> int:
         """Append a [states, vocab] int32 table to the arena; returns its element offset."""
@@ -226,15 +238,20 @@ class B200Decoder:
         a value threshold (the reference leaves its fused sampler for torch sort / multinomial here,
         src/climbing_gym/inference/lfm25_cuda.py:311-324)."""
         state, n, vocab = entry.state, entry.cache.n_slots, self.engine.config.vocab_size
-        dtype = nv.dtype_code(entry.logits.dtype)
+        logits, dtype = entry.logits, nv.dtype_code(entry.logits.dtype)
         if state.head_k:  # behaviour head of the unfiltered distribution, recorded at the row's current length
-            nv.call("cgym_topk_head", nv.ptr(state.head_ids), nv.ptr(state.head_logprobs), nv.ptr(entry.logits),
+            nv.call("cgym_topk_head", nv.ptr(state.head_ids), nv.ptr(state.head_logprobs), nv.ptr(logits),
                     nv.ptr(state.alive), nv.ptr(state.lengths), n, vocab, state.head_positions, state.head_k, dtype, stream)
+        if state.penalties is not None:  # everything after this reads the penalised fp32 copy of the logits
+            nv.call("cgym_repetition_penalty", nv.ptr(state.penalised), nv.ptr(logits), nv.ptr(state.seen),
+                    nv.ptr(state.tokens), nv.ptr(state.lengths), nv.ptr(state.alive), nv.ptr(state.penalties), n, vocab,
+                    state.capacity, dtype, stream)
+            logits, dtype = state.penalised, nv.F32
         if entry.filtered:
-            nv.call("cgym_filter_thresholds", nv.ptr(state.min_logits), nv.ptr(entry.logits), nv.ptr(state.temperatures),
+            nv.call("cgym_filter_thresholds", nv.ptr(state.min_logits), nv.ptr(logits), nv.ptr(state.temperatures),
                     nv.ptr(state.top_k), nv.ptr(state.top_p), nv.ptr(state.alive), n, vocab, dtype, stream)
         struct = state.struct_filtered if entry.filtered else state.struct
-        nv.call("cgym_sample_record", nv.ptr(entry.logits), C.byref(struct), advance, None, None, n, vocab, dtype,
+        nv.call("cgym_sample_record", nv.ptr(logits), C.byref(struct), advance, None, None, n, vocab, dtype,
                 nv.ptr(state.sample_ws), stream)
 
     def _sample_only(self, entry: _DecodeGraph) -> None:
@@ -243,7 +260,7 @@ class B200Decoder:
 
     @torch.inference_mode()
     def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False, filtered: bool = False,
-                   head_k: int = 0, head_positions: int = 0) -> _DecodeGraph:
+                   head_k: int = 0, head_positions: int = 0, penalised: bool = False) -> _DecodeGraph:
         engine = self.engine
         alignment = 32 if batch_size >= 64 else 128
         alignment = max(alignment, self.page_size)
@@ -251,6 +268,7 @@ class B200Decoder:
         head_positions = min(capacity, -(-head_positions // 64) * 64) if head_k else 0
         key = (batch_size, capacity, masked) + (("filtered",) if filtered else ())
         key += (f"head{head_k}x{head_positions}",) if head_k else ()
+        key += ("penalised",) if penalised else ()
         if key in self.graphs:
             self.graphs.move_to_end(key)
             return self.graphs[key]
@@ -267,6 +285,8 @@ class B200Decoder:
         state = SlotState(batch_size, capacity, engine.config.vocab_size, int(engine.config.eos_token_id), cache.seq_lens)
         if head_k:
             state.allocate_heads(head_k, head_positions)
+        if penalised:
+            state.allocate_penalty()
         logits = torch.zeros((batch_size, engine.config.vocab_size), device=engine.device, dtype=engine.dtype)
         splits = 1
         if batch_size * engine.config.num_key_value_heads < 148:
@@ -314,8 +334,7 @@ class B200Decoder:
         cache_len = int(max_seqlen) + sampling.max_new_tokens
         if cache_len > engine.max_model_len:
             raise ValueError(f"max_seq_len={cache_len} exceeds engine max_model_len={engine.max_model_len}")
-        if sampling.repetition_penalty != 1.0:
-            raise NotImplementedError("repetition penalties are not on the fused path")
+        penalised = float(sampling.repetition_penalty) != 1.0
         filtered = sampling.temperature > 0.0 and (0 < sampling.top_k < engine.config.vocab_size or sampling.top_p < 1.0)
         head_k = sampling.behavior_topk
         if head_k > engine.config.vocab_size:
@@ -326,7 +345,7 @@ class B200Decoder:
         flat_ids, prompt_lengths = engine._split_lengths(input_ids, cu_seqlens, max_seqlen)
         n_prompts, batch = len(prompt_lengths), len(prompt_lengths) * repeats
         entry = self._get_graph(batch, cache_len, masked=self.adaptive_batching, filtered=filtered, head_k=head_k,
-                                head_positions=sampling.max_new_tokens)
+                                head_positions=sampling.max_new_tokens, penalised=penalised)
         cache, state, dev = entry.cache, entry.state, engine.device
         cache.release(torch.ones(batch, device=dev, dtype=torch.uint8))
         cache.conv_state.zero_()
@@ -351,6 +370,15 @@ class B200Decoder:
         if filtered:
             state.top_k.fill_(int(sampling.top_k))
             state.top_p.fill_(float(sampling.top_p))
+        if penalised:
+            # every sample of a prompt starts out having seen the prompt's tokens
+            # (reference: src/climbing_gym/inference/lfm25_engine.py:933-958)
+            state.penalties.fill_(float(sampling.repetition_penalty))
+            first_rows = torch.arange(n_prompts, device=dev) * repeats
+            token_rows = torch.repeat_interleave(first_rows, torch.tensor(prompt_lengths, device=dev))
+            state.seen.index_put_((token_rows, flat_ids), torch.ones((), device=dev, dtype=torch.uint8))
+            if repeats > 1:
+                state.seen[dst.long()] = state.seen[src.long()]
         fixed_length = (sampling.ignore_eos and not sampling.stop_token_ids and not sampling.stop_token_sequences
                         and sampling.stop_table is None)
         interval = self.finish_check_interval if batch >= 16 else 1

@@ -270,6 +270,19 @@ int cgym_topk_head(int32_t* out_ids, float* out_logprobs, const void* logits, co
                    const int32_t* lengths, int n_slots, int vocab, int capacity, int k, int dtype,
                    cgym_stream_t stream);
 
+/* _apply_repetition_penalty + the seen-token mask of generate (lfm25_engine.py:1777-1791, :933-958,
+ * lfm25_cuda.py:336-337): out[row][i] (fp32, [rows][vocab]) = logits[row][i], and for every token the
+ * row has seen, logit * penalty when negative, logit / penalty otherwise. seen is one byte per
+ * (row, token), set by the caller for the prompt's tokens; the row's latest generated token
+ * (tokens[row][lengths[row] - 1], rows of `capacity` tokens; tokens may be NULL) counts as seen and its
+ * byte is set here, so calling this once per step before the sampler keeps the mask current. Dead
+ * rows (alive[row] == 0; alive optional) are left untouched. Feed `out` to cgym_filter_thresholds /
+ * cgym_sample_record as CGYM_F32 logits: the recorded log-prob is then that of the penalised
+ * distribution, as in the reference. */
+int cgym_repetition_penalty(float* out, const void* logits, uint8_t* seen, const int64_t* tokens,
+                            const int32_t* lengths, const uint8_t* alive, const float* penalties, int rows,
+                            int vocab, int capacity, int dtype, cgym_stream_t stream);
+
 /* Chunked-head completion scoring (lfm25_engine.py:1150-1154): logit[target] - logsumexp. */
 int cgym_target_logprobs(float* out, const void* logits, const int64_t* targets, int rows,
                          int vocab, int dtype, cgym_stream_t stream);

@@ -148,3 +148,15 @@ def record_head(ids, probs, out_ids, out_probs, lengths, alive):
         if alive[row]:
             out_ids[row, int(lengths[row])] = ids[row]
             out_probs[row, int(lengths[row])] = probs[row]
+
+
+def apply_repetition_penalty(logits, seen, penalty):
+    """lfm25_engine.py:1777-1791: fp32 logits of seen tokens are multiplied by the penalty when negative
+    and divided by it otherwise."""
+    logits = np.asarray(logits, np.float32)
+    if seen is None or penalty == 1.0:
+        return logits
+    if penalty <= 0.0:
+        raise ValueError("repetition penalty must be > 0")
+    p = np.float32(penalty)
+    return np.where(np.asarray(seen, bool), np.where(logits < 0, logits * p, logits / p), logits).astype(np.float32)

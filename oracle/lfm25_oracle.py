@@ -66,6 +66,7 @@ class OracleSampling:
     ignore_eos: bool = False
     # test hook: generated position at which each flat row's token is replaced by EOS
     force_eos_at: tuple | None = None
+    repetition_penalty: float = 1.0
 
 
 @dataclass
@@ -380,6 +381,14 @@ class OracleEngine:
                 states.append(st.clone())
                 first.append(logits)
         bsz = len(states)
+        # seen-token mask of the repetition penalty: the prompt's tokens, then every sampled token
+        # (lfm25_engine.py:933-958, lfm25_cuda.py:336-337)
+        seen = None
+        if sampling.repetition_penalty != 1.0:
+            from .kernels import apply_repetition_penalty
+            seen = np.zeros((bsz, self.cfg.vocab_size), bool)
+            for p, prompt in enumerate(prompts):
+                seen[p * repeats:(p + 1) * repeats, list(prompt)] = True
         logits = np.stack(first)
         tokens = np.zeros((bsz, n_new), np.int64)
         logprobs = np.zeros((bsz, n_new), np.float32)
@@ -388,7 +397,11 @@ class OracleEngine:
         alive = np.ones(bsz, bool)
         fixed = sampling.ignore_eos and not sampling.stop_token_ids
         for step in range(n_new):
+            if seen is not None:  # the draw and its log-prob both come from the penalised fp32 logits
+                logits = apply_repetition_penalty(logits, seen, sampling.repetition_penalty)
             sampled, lp = self.sample(logits, temperature=sampling.temperature, seed=sampling.seed, step=step)
+            if seen is not None:
+                seen[np.arange(bsz), sampled] = True
             if sampling.force_eos_at is not None:
                 forced = np.asarray(sampling.force_eos_at) == step
                 if forced.any():

@@ -287,13 +287,40 @@ def head_vectors():
     return out
 
 
+def penalty_vectors():
+    """Reference repetition penalty: the elementwise rule on random logits, and greedy generation of the
+    tiny model under a penalty (the reference's eager CPU engine; prompt tokens count as seen)."""
+    from climbing_gym.inference import lfm25_engine as ref
+
+    rng = np.random.default_rng(9)
+    logits = torch.from_numpy((rng.standard_normal((4, 512)) * 2.0).astype(np.float32))
+    seen = torch.from_numpy(rng.random((4, 512)) < 0.3)
+    out = {"rule": []}
+    for penalty in (1.3, 0.8):
+        y = ref._apply_repetition_penalty(logits.clone(), seen_token_mask=seen, penalty=penalty)
+        out["rule"].append(dict(penalty=penalty, bits=y.view(torch.int32).tolist()))
+    cfg = synthetic.tiny_config()
+    state = synthetic.make_state_dict(cfg, seed=0, untied_head=True)
+    prompts = synthetic.uniform_prompts(8, 8, 64, cfg.vocab_size, seed=0)[:4]
+    engine = ref_engine(None, cfg, state, torch.float32)
+    for penalty in (1.3, 0.8):
+        got = engine.generate(*ref.flatten_token_batches(prompts), repeats=2,
+                              sampling=ref.LFM25SamplingConfig(temperature=0.0, max_new_tokens=24,
+                                                               repetition_penalty=penalty, ignore_eos=True))
+        out[f"generate_fp32_{penalty}"] = dict(
+            penalty=penalty, token_ids=got.token_ids.tolist(),
+            logprobs=[[[round(float(x), 6) for x in r] for r in p] for p in got.logprobs.tolist()])
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default="/root/reference/src")
     parser.add_argument("--only", default="")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
-    jobs = dict(model=model_vectors, sampler=sampler_vectors, kernels=kernel_vectors, head=head_vectors)
+    jobs = dict(model=model_vectors, sampler=sampler_vectors, kernels=kernel_vectors, head=head_vectors,
+                penalty=penalty_vectors)
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
             continue

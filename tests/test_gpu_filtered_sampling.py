@@ -160,5 +160,3 @@ def test_degenerate_filters_are_greedy_decoding_and_filtered_runs_are_reproducib
     b, _ = run(temperature=1.0, top_k=40, top_p=0.9)
     full, _ = run(temperature=1.0)
     assert np.array_equal(a, b) and not np.array_equal(a, full)
-    with pytest.raises(NotImplementedError, match="repetition"):
-        run(temperature=1.0, repetition_penalty=1.2)

@@ -170,3 +170,15 @@ def test_philox_known_answer():
     # Random123 known-answer: counter 0, key 0 -> first word of philox4x32-10
     assert int(philox.philox4x32_10(np.array([0]), 0)[0]) == 0x6627E8D5
     assert int(philox.philox4x32_10(np.array([0xFFFFFFFF]), 0)[0]) != 0x6627E8D5
+
+
+def test_repetition_penalty_rule_is_bit_exact(golden):
+    rng = np.random.default_rng(9)
+    logits = (rng.standard_normal((4, 512)) * 2.0).astype(np.float32)
+    seen = rng.random((4, 512)) < 0.3
+    for case in golden("penalty")["rule"]:
+        got = ok.apply_repetition_penalty(logits, seen, case["penalty"])
+        assert got.view(np.int32).tolist() == case["bits"]
+    assert ok.apply_repetition_penalty(logits, None, 1.3) is not None
+    with pytest.raises(ValueError):
+        ok.apply_repetition_penalty(logits, seen, 0.0)

@@ -98,3 +98,15 @@ def test_fp8_paths_stay_close_to_bf16():
     same = a["token_ids"] == b["token_ids"]
     assert same.mean() > 0.5
     assert np.abs(a["logprobs"][same] - b["logprobs"][same]).max() < 0.25
+
+
+@pytest.mark.parametrize("penalty", [1.3, 0.8])
+def test_generate_with_repetition_penalty_matches_reference(golden, penalty):
+    want = golden("penalty")[f"generate_fp32_{penalty}"]
+    _, engine = build(True, "fp32")
+    got = engine.generate(PROMPTS[:4], 2, OracleSampling(temperature=0.0, max_new_tokens=24, ignore_eos=True,
+                                                         repetition_penalty=penalty))
+    assert got["token_ids"].tolist() == want["token_ids"]
+    assert np.allclose(got["logprobs"], np.array(want["logprobs"]), atol=1e-4)
+    plain = engine.generate(PROMPTS[:4], 2, OracleSampling(temperature=0.0, max_new_tokens=24, ignore_eos=True))
+    assert plain["token_ids"].tolist() != want["token_ids"], "the penalty must change the greedy path"
