@@ -21,7 +21,7 @@ from . import _native as nv
 from .config import LFM25SamplingConfig
 from .model import ForwardBuffers, LFM25Runner
 from .paged import PagedHybridCache
-from .text_stops import build_token_sequence_table
+from .text_stops import build_token_sequence_table, product_stop_table
 from .types import LFM25GenerationOutput
 
 
@@ -339,9 +339,6 @@ class B200Decoder:
         head_k = sampling.behavior_topk
         if head_k > engine.config.vocab_size:
             raise ValueError("Behavior head exceeds the vocabulary")
-        if sampling.stop_token_sequences and sampling.stop_table is not None:
-            raise NotImplementedError("stop_token_sequences together with a stop_table would need their product "
-                                      "automaton; pass one of them")
         flat_ids, prompt_lengths = engine._split_lengths(input_ids, cu_seqlens, max_seqlen)
         n_prompts, batch = len(prompt_lengths), len(prompt_lengths) * repeats
         entry = self._get_graph(batch, cache_len, masked=self.adaptive_batching, filtered=filtered, head_k=head_k,
@@ -436,6 +433,8 @@ def build_token_stop_table(sampling: LFM25SamplingConfig, vocab: int, device) ->
     session does (src/climbing_gym/inference/lfm25_session.py:228-241)."""
     if sampling.stop_table is not None:
         table = sampling.stop_table.to(device).clone()
+        if sampling.stop_token_sequences:  # both kinds of stop: their product automaton
+            table = product_stop_table(table, build_token_sequence_table(sampling.stop_token_sequences, vocab))
     elif sampling.stop_token_sequences:  # suffix match on the generated ids, as an automaton over token ids
         table = build_token_sequence_table(sampling.stop_token_sequences, vocab).to(device)
     else:

@@ -79,3 +79,20 @@ def build_token_sequence_table(sequences, vocab_size: int) -> torch.Tensor:
             longest = next(history[cut:] for cut in range(len(history) + 1) if history[cut:] in index)
             table[index[state], token] = index[longest] + (65536 if matched else 0)
     return torch.from_numpy(table)
+
+
+def product_stop_table(first: torch.Tensor, second: torch.Tensor) -> torch.Tensor:
+    """Two stop automata advanced in lock step as one table: state ``a * states(second) + b``, matched
+    when either matches. This is what a request with both a ``stop_table`` and ``stop_token_sequences``
+    means in the reference's loop, which advances the text table and then tests the token suffixes
+    (src/climbing_gym/inference/lfm25_cuda.py:343-347)."""
+    if first.ndim != 2 or second.ndim != 2 or first.size(1) != second.size(1):
+        raise ValueError("stop tables must be [states, vocab] over the same vocabulary")
+    n_first, n_second = first.size(0), second.size(0)
+    if n_first * n_second >= 65536:
+        raise ValueError("Too many stop-prefix states")
+    second = second.to(first.device)
+    a, b = first.to(torch.int64)[:, None, :], second.to(torch.int64)[None, :, :]
+    state = (a & 65535) * n_second + (b & 65535)
+    matched = ((a >> 16) | (b >> 16)) != 0
+    return (state + matched * 65536).reshape(n_first * n_second, -1).to(torch.int32)

@@ -309,3 +309,24 @@ def test_stop_token_sequence_automaton_matches_suffix_search():
         build_token_sequence_table([()], 16)
     with pytest.raises(ValueError, match="vocabulary"):
         build_token_sequence_table([(3, 99)], 16)
+
+
+def test_product_of_two_stop_automata_matches_when_either_does():
+    import random
+
+    from climbing_gym_b200.text_stops import build_token_sequence_table, product_stop_table
+
+    first = build_token_sequence_table([(1, 2, 3), (4, 4)], 8)
+    second = build_token_sequence_table([(2, 3, 5), (7,)], 8)
+    both = product_stop_table(first, second)
+    assert both.dtype == torch.int32 and both.shape == (first.size(0) * second.size(0), 8)
+    rng = random.Random(1)
+    for _ in range(300):
+        a = b = state = 0
+        for token in (rng.randrange(8) for _ in range(12)):
+            va, vb, value = int(first[a, token]), int(second[b, token]), int(both[state, token])
+            a, b, state = va & 65535, vb & 65535, value & 65535
+            assert state == a * second.size(0) + b
+            assert (value >= 65536) == (va >= 65536 or vb >= 65536)
+    with pytest.raises(ValueError, match="same vocabulary"):
+        product_stop_table(first, build_token_sequence_table([(1,)], 9))

@@ -295,7 +295,22 @@ def test_stop_token_sequences_end_generation_at_the_matched_suffix(dev):
         assert list(tokens[row, :want_len]) == history[:want_len]
         assert reasons[row] == (2 if want_len < 24 or any(tuple(history[24 - len(s):24]) == s for s in stops) else 3)
     assert lengths[0] <= 7 and lengths[3] <= 12 and lengths[5] == 1
-    with pytest.raises(NotImplementedError, match="product"):
-        engine.generate(*flat(PROMPTS, dev), repeats=1, sampling=LFM25SamplingConfig(
-            temperature=0.0, max_new_tokens=4, stop_token_sequences=stops,
-            stop_table=torch.zeros((1, 4096), dtype=torch.int32)))
+    # the same stops together with a stop table (here: "row 6's tokens 2, 3 in a row"): the two automata
+    # advance in lock step and a row ends when either matches
+    a, b = int(free[6, 2]), int(free[6, 3])
+    table = torch.zeros((2, 4096), dtype=torch.int32)
+    table[:, a] = 1
+    table[1, b] = 65536
+    both = engine.generate(*flat(PROMPTS, dev), repeats=1, sampling=LFM25SamplingConfig(
+        temperature=0.0, max_new_tokens=24, stop_token_sequences=stops, stop_table=table))
+    both_lengths = both.lengths.cpu().numpy()[:, 0]
+    for row in range(len(PROMPTS)):
+        history, state, want_len = list(free[row]), 0, int(lengths[row])
+        for end, token in enumerate(history[:want_len], 1):
+            value = int(table[state, token])
+            state = value & 65535
+            if value >= 65536:
+                want_len = end
+                break
+        assert both_lengths[row] == want_len, (row, both_lengths[row], want_len)
+    assert both_lengths[6] == 4 and both.finish_reasons.cpu().numpy()[6, 0] == 2
