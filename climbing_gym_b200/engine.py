@@ -451,12 +451,39 @@ class LFM25Engine:
         if repeats == 1 and cache_len == source.max_seq_len and source.max_slots == n:
             cache = source
         else:
-            raise NotImplementedError("fork with repeats > 1 goes through generate(repeats=...), which shares prefix pages")
+            cache = self._fork_into_new_cache(prefix, int(repeats), cache_len)
         dev = self.device
         return LFM25DecodeBatch(cache=cache, active_slot_ids=torch.arange(total, device=dev),
                                 prompt_indices=torch.arange(n, device=dev).repeat_interleave(repeats),
                                 repeat_indices=torch.arange(repeats, device=dev).repeat(n),
                                 alive=torch.ones(total, device=dev, dtype=torch.bool))
+
+    def _fork_into_new_cache(self, prefix: LFM25PrefixBatch, repeats: int, cache_len: int) -> PagedHybridCache:
+        """A cache of ``batch x repeats`` slots whose slot ``p * repeats + r`` continues prompt ``p``: the
+        prefix pages are copied page by page into the first sample of each group (two caches never share a
+        pool), the other samples of the group then share them by reference (reference: the dense
+        repeat_interleave copy of lfm25_engine.py:735-790)."""
+        source, dev, n = prefix.cache, self.device, prefix.batch_size
+        rows = (prefix.slots if prefix.slots is not None else torch.arange(n, device=dev)).long()
+        cache = self._empty_cache(max_slots=n * repeats, max_seq_len=cache_len, fp8_kv=source.fp8_kv,
+                                  page_size=source.page_size)
+        lens = source.seq_lens.index_select(0, rows)
+        first = torch.arange(n, device=dev, dtype=torch.int32) * repeats
+        cache.reserve(first, lens)
+        held = torch.arange(source.max_blocks, device=dev)[None, :] * source.page_size < lens[:, None]
+        src_pages = source.block_table.index_select(0, rows)[held].long()
+        dst_pages = cache.block_table.index_select(0, first.long())[:, :source.max_blocks][held].long()
+        cache.kv_pool[:, dst_pages] = source.kv_pool[:, src_pages]
+        if cache.kv_scales is not None:
+            cache.kv_scales[:, dst_pages] = source.kv_scales[:, src_pages]
+        cache.conv_state[:, first.long()] = source.conv_state[:, rows]
+        cache.row_lens.index_copy_(0, first.long(), lens)
+        if repeats > 1:
+            src = first.repeat_interleave(repeats - 1)
+            dst = (first[:, None] + torch.arange(1, repeats, device=dev, dtype=torch.int32)[None, :]).reshape(-1)
+            cache.fork(src, dst.contiguous(), lens.repeat_interleave(repeats - 1).contiguous())
+        cache.check_status()
+        return cache
 
     @torch.inference_mode()
     def decode_step(self, state: LFM25DecodeBatch, input_tokens: torch.Tensor,
