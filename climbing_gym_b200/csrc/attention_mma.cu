@@ -72,6 +72,12 @@ __device__ __forceinline__ uint32_t att_lds32(uint32_t addr) {
   asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ void att_lds128(uint32_t addr, uint32_t (&v)[4]) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(addr));
+}
+__device__ __forceinline__ void att_lds128f(uint32_t addr, float (&v)[4]) {
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "r"(addr));
+}
 __device__ __forceinline__ float att_lds_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
@@ -108,6 +114,12 @@ __device__ __forceinline__ uint32_t att_e4m3x2_to_f16x2(uint32_t two_codes) {
   return out;
 }
 
+// four e4m3 codes -> two packed fp16x2 (exact): codes 0, 1 and codes 2, 3
+__device__ __forceinline__ void att_e4m3x4_to_f16x4(uint32_t four_codes, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi) : "r"(four_codes));
+}
+
 // Geometry of one staged (page, head) block for cache element size EB, head_dim D, page size P.
 template <int EB, int D, int P>
 struct BlockGeom {
@@ -121,7 +133,7 @@ struct BlockGeom {
   static constexpr int STAGE_BYTES = BLOCK_BYTES + SCALE_BYTES;
   // token held in column c of S n-tile t (see the fragment notes in the file header of the C ABI docs)
   static __device__ __forceinline__ int token_of(int t, int c) {
-    if constexpr (EB == 1) return 16 * (t >> 1) + 4 * (c >> 1) + 2 * (t & 1) + (c & 1);
+    if constexpr (EB == 1) return 16 * (c >> 1) + 4 * (t >> 1) + 2 * (t & 1) + (c & 1);
     else return 8 * t + c;
   }
 };
@@ -141,8 +153,8 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qa)[D / 16][4], const TQ
       float v[4] = {0.f, 0.f, 0.f, 0.f};
       if (R < n_rows) {
         const TQ* src = q_base + (static_cast<int64_t>(R / G) * n_q_heads + head0 + (R % G)) * D;
-        // bf16 path: k = 16s + 2j + {0,1} and + 8; e4m3 path: dims 16s + 4j + {0,1} and {2,3}
-        const int d0 = F16 ? 16 * s + 4 * j : 16 * s + 2 * j;
+        // bf16 path: k = 16s + 2j + {0,1} and + 8; e4m3 path: dims 16j + 4s + {0,1} and {2,3}
+        const int d0 = F16 ? 16 * j + 4 * s : 16 * s + 2 * j;
         const int d1 = F16 ? d0 + 2 : d0 + 8;
         v[0] = Elem<TQ>::load(src + d0); v[1] = Elem<TQ>::load(src + d0 + 1);
         v[2] = Elem<TQ>::load(src + d1); v[3] = Elem<TQ>::load(src + d1 + 1);
@@ -155,53 +167,91 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qa)[D / 16][4], const TQ
 
 // One page for one m-tile: S = Q K^T (scaled, masked), online softmax update, O += P V.
 // limit_lo / limit_hi: number of cache positions rows row_lo / row_hi may see (0 masks the row).
-template <int EB, int D, int P>
+// HI = false: rows 8..15 of the m-tile are padding (a decode row with at most 8 query heads per KV
+// head), so their softmax arithmetic is skipped and their P fragments are zero.
+//
+// e4m3 pages: a lane reads one whole 16-byte chunk of a K row (or V^T row) per n-tile (or output
+// tile) and feeds the four K steps from its four words; the contraction index of an MMA is only a
+// label, so Q is loaded with dims 16 j + 4 s + {0..3} in K step s to match, and the token a score
+// column stands for (BlockGeom::token_of) is chosen such that the P fragments line up with 16
+// consecutive tokens of a V^T row. The per-token scales of a lane's columns are then four
+// consecutive floats: one 16-byte load per pair of n-tiles.
+template <int EB, int D, int P, bool HI>
 __device__ __forceinline__ void attend_page(const uint32_t (&qa)[D / 16][4], float (&o)[D / 8][4], float (&m)[2],
                                             float (&l)[2], uint32_t stage, int page_token0, int limit_lo,
                                             int limit_hi, float scale_log2, int lane) {
   using Geo = BlockGeom<EB, D, P>;
   constexpr bool F16 = EB == 1;
   constexpr int NT = P / 8, KS = D / 16, OT = D / 8, PS = P / 16;
+  static_assert(!F16 || (D == 64 && P == 64), "the e4m3 fragment layout is built for 64 x 64 blocks");
   const int c8 = lane >> 2, j = lane & 3;
   float s[NT][4];
 #pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.f;
-    const int tok = Geo::token_of(t, c8);  // K row this thread feeds for column c8
-    const uint32_t row_addr = stage + tok * Geo::K_ROW;
+  for (int t = 0; t < NT; ++t) s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.f;
+  if constexpr (F16) {
 #pragma unroll
-    for (int k = 0; k < KS; ++k) {
-      uint32_t b0, b1;
-      if constexpr (F16) {
-        const uint32_t w = att_lds32(row_addr + kv_swizzle(tok, k, Geo::K_CPR) * 16 + 4 * j);
-        b0 = att_e4m3x2_to_f16x2(w & 0xFFFFu);
-        b1 = att_e4m3x2_to_f16x2(w >> 16);
-      } else {
-        b0 = att_lds32(row_addr + kv_swizzle(tok, 2 * k, Geo::K_CPR) * 16 + 4 * j);
-        b1 = att_lds32(row_addr + kv_swizzle(tok, 2 * k + 1, Geo::K_CPR) * 16 + 4 * j);
+    for (int t0 = 0; t0 < NT; t0 += 4) {  // four n-tiles at a time: independent accumulators between dependent MMAs
+      uint32_t kw[4][4];
+#pragma unroll
+      for (int tt = 0; tt < 4; ++tt) {
+        const int tok = Geo::token_of(t0 + tt, c8);  // K row this thread feeds for column c8
+        att_lds128(stage + tok * Geo::K_ROW + kv_swizzle(tok, j, Geo::K_CPR) * 16, kw[tt]);
       }
-      att_mma<F16>(s[t], qa[k], b0, b1);
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt) {
+          uint32_t b0, b1;
+          att_e4m3x4_to_f16x4(kw[tt][k], b0, b1);
+          att_mma<F16>(s[t0 + tt], qa[k], b0, b1);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int tok = Geo::token_of(t, c8);
+      const uint32_t row_addr = stage + tok * Geo::K_ROW;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        const uint32_t b0 = att_lds32(row_addr + kv_swizzle(tok, 2 * k, Geo::K_CPR) * 16 + 4 * j);
+        const uint32_t b1 = att_lds32(row_addr + kv_swizzle(tok, 2 * k + 1, Geo::K_CPR) * 16 + 4 * j);
+        att_mma<F16>(s[t], qa[k], b0, b1);
+      }
     }
   }
   // scale (x per-token K scale for e4m3), causal / length mask, page maximum per row
+  const bool masked = page_token0 + P > (HI ? min(limit_lo, limit_hi) : limit_lo);  // warp-uniform per m-tile row pair
   float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-  for (int t = 0; t < NT; ++t) {
+  for (int a = 0; a < NT / 2; ++a) {
+    float ks4[4] = {scale_log2, scale_log2, scale_log2, scale_log2};
+    if constexpr (F16) {
+      att_lds128f(stage + Geo::BLOCK_BYTES + 4 * (16 * j + 4 * a), ks4);  // tokens 16 j + 4 a + {0..3}
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int tok = Geo::token_of(t, 2 * j + i);
-      float ks = scale_log2;
-      if constexpr (F16) ks *= att_lds_f32(stage + Geo::BLOCK_BYTES + 4 * tok);
-      const int pos = page_token0 + tok;
-      s[t][i] = pos < limit_lo ? s[t][i] * ks : -INFINITY;
-      s[t][2 + i] = pos < limit_hi ? s[t][2 + i] * ks : -INFINITY;
-      mx[0] = fmaxf(mx[0], s[t][i]);
-      mx[1] = fmaxf(mx[1], s[t][2 + i]);
+      for (int q = 0; q < 4; ++q) ks4[q] *= scale_log2;
+    }
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 2 * a + e;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float ks = ks4[2 * e + i];
+        s[t][i] *= ks;
+        if constexpr (HI) s[t][2 + i] *= ks;
+        if (masked) {
+          const int pos = page_token0 + Geo::token_of(t, 2 * j + i);
+          if (pos >= limit_lo) s[t][i] = -INFINITY;
+          if constexpr (HI) { if (pos >= limit_hi) s[t][2 + i] = -INFINITY; }
+        }
+        mx[0] = fmaxf(mx[0], s[t][i]);
+        if constexpr (HI) mx[1] = fmaxf(mx[1], s[t][2 + i]);
+      }
     }
   }
-  float alpha[2];
+  float alpha[2] = {1.f, 1.f};
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
+  for (int h = 0; h < (HI ? 2 : 1); ++h) {
     mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
     mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
     const float m_new = fmaxf(m[h], mx[h]);
@@ -212,48 +262,64 @@ __device__ __forceinline__ void attend_page(const uint32_t (&qa)[D / 16][4], flo
 #pragma unroll
   for (int u = 0; u < OT; ++u) {
     o[u][0] *= alpha[0]; o[u][1] *= alpha[0];
-    o[u][2] *= alpha[1]; o[u][3] *= alpha[1];
+    if constexpr (HI) { o[u][2] *= alpha[1]; o[u][3] *= alpha[1]; }
   }
   // P = exp2(S - m); fp32 row sums; P (x V scale) rounded to the MMA input type
   const float m0 = (m[0] == -INFINITY) ? 0.f : m[0], m1 = (m[1] == -INFINITY) ? 0.f : m[1];
+  uint32_t pa[PS][4];
 #pragma unroll
-  for (int t = 0; t < NT; ++t) {
+  for (int a = 0; a < NT / 2; ++a) {
+    float vs4[4] = {1.f, 1.f, 1.f, 1.f};
+    if constexpr (F16) att_lds128f(stage + Geo::BLOCK_BYTES + 4 * P + 4 * (16 * j + 4 * a), vs4);
+    float p_lo[4], p_hi[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      float p0 = exp2f(s[t][i] - m0), p1 = exp2f(s[t][2 + i] - m1);  // exp2(-inf) = 0 for masked entries
+    for (int q = 0; q < 4; ++q) {  // q = 2 e + i: n-tile 2 a + e, column 2 j + i
+      const int t = 2 * a + (q >> 1), i = q & 1;
+      const float p0 = exp2f(s[t][i] - m0);  // exp2(-inf) = 0 for masked entries
       l[0] += p0;
-      l[1] += p1;
-      if constexpr (F16) {
-        const float vs = att_lds_f32(stage + Geo::BLOCK_BYTES + 4 * P + 4 * Geo::token_of(t, 2 * j + i));
-        p0 *= vs;
-        p1 *= vs;
+      p_lo[q] = F16 ? p0 * vs4[q] : p0;
+      if constexpr (HI) {
+        const float p1 = exp2f(s[t][2 + i] - m1);
+        l[1] += p1;
+        p_hi[q] = F16 ? p1 * vs4[q] : p1;
       }
-      s[t][i] = p0;
-      s[t][2 + i] = p1;
     }
+    pa[a][0] = att_pack<F16>(p_lo[0], p_lo[1]);
+    pa[a][2] = att_pack<F16>(p_lo[2], p_lo[3]);
+    pa[a][1] = HI ? att_pack<F16>(p_hi[0], p_hi[1]) : 0u;
+    pa[a][3] = HI ? att_pack<F16>(p_hi[2], p_hi[3]) : 0u;
   }
   const uint32_t vt = stage + Geo::K_BYTES;
+  if constexpr (F16) {
 #pragma unroll
-  for (int k = 0; k < PS; ++k) {
-    uint32_t pa[4];
-    pa[0] = att_pack<F16>(s[2 * k][0], s[2 * k][1]);
-    pa[1] = att_pack<F16>(s[2 * k][2], s[2 * k][3]);
-    pa[2] = att_pack<F16>(s[2 * k + 1][0], s[2 * k + 1][1]);
-    pa[3] = att_pack<F16>(s[2 * k + 1][2], s[2 * k + 1][3]);
+    for (int u0 = 0; u0 < OT; u0 += 4) {
+      uint32_t vw[4][4];
 #pragma unroll
-    for (int u = 0; u < OT; ++u) {
-      const int dim = 8 * u + c8;  // V^T row this thread feeds for output column c8
-      const uint32_t row_addr = vt + dim * Geo::V_ROW;
-      uint32_t b0, b1;
-      if constexpr (F16) {
-        const uint32_t w = att_lds32(row_addr + kv_swizzle(dim, k, Geo::V_CPR) * 16 + 4 * j);
-        b0 = att_e4m3x2_to_f16x2(w & 0xFFFFu);
-        b1 = att_e4m3x2_to_f16x2(w >> 16);
-      } else {
-        b0 = att_lds32(row_addr + kv_swizzle(dim, 2 * k, Geo::V_CPR) * 16 + 4 * j);
-        b1 = att_lds32(row_addr + kv_swizzle(dim, 2 * k + 1, Geo::V_CPR) * 16 + 4 * j);
+      for (int uu = 0; uu < 4; ++uu) {
+        const int dim = 8 * (u0 + uu) + c8;  // V^T row this thread feeds for output column c8
+        att_lds128(vt + dim * Geo::V_ROW + kv_swizzle(dim, j, Geo::V_CPR) * 16, vw[uu]);
       }
-      att_mma<F16>(o[u], pa, b0, b1);
+#pragma unroll
+      for (int k = 0; k < PS; ++k) {
+#pragma unroll
+        for (int uu = 0; uu < 4; ++uu) {
+          uint32_t b0, b1;
+          att_e4m3x4_to_f16x4(vw[uu][k], b0, b1);
+          att_mma<F16>(o[u0 + uu], pa[k], b0, b1);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < PS; ++k) {
+#pragma unroll
+      for (int u = 0; u < OT; ++u) {
+        const int dim = 8 * u + c8;
+        const uint32_t row_addr = vt + dim * Geo::V_ROW;
+        const uint32_t b0 = att_lds32(row_addr + kv_swizzle(dim, 2 * k, Geo::V_CPR) * 16 + 4 * j);
+        const uint32_t b1 = att_lds32(row_addr + kv_swizzle(dim, 2 * k + 1, Geo::V_CPR) * 16 + 4 * j);
+        att_mma<F16>(o[u], pa[k], b0, b1);
+      }
     }
   }
 }
@@ -270,8 +336,12 @@ __device__ __forceinline__ void stage_block(uint32_t dst, uint32_t bar, const ui
 // NST = pages in flight per warp. A CTA spends about 3 us outside its page loop (q and block-table
 // fetch, first page latency, merge, store), so the SM is better used by several short-ring CTAs whose
 // fixed phases overlap than by one CTA with a deep ring: NST = 1 -> 64 KB (bf16) and 3 CTAs per SM.
-template <typename TQ, int EB, int D, int P, int NST>
-__global__ void __launch_bounds__(128, NST == 1 ? 3 : 1)
+// e4m3 pages are half the size, so two of them per warp still leave room for 3 CTAs per SM (NST = 2).
+template <int EB, int NST>
+constexpr int decode_ctas_per_sm() { return (NST == 1 || (EB == 1 && NST == 2)) ? 3 : 1; }
+
+template <typename TQ, int EB, int D, int P, int NST, bool HI>
+__global__ void __launch_bounds__(128, decode_ctas_per_sm<EB, NST>())
 decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, const int32_t* __restrict__ kv_lens,
                             const int32_t* __restrict__ slots, const uint8_t* __restrict__ active,
                             cgym_kv_layout kv, int layer, int n_q_heads, float scale, int n_splits,
@@ -333,7 +403,7 @@ decode_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, cons
   for (int i = 0; i < n_mine; ++i) {
     if (!att_bar_wait(att_smem_u32(&bars[warp][i % NST]), (i / NST) & 1, &abort_flag)) break;
     const int token0 = (page_begin + warp + 4 * i) * P;
-    attend_page<EB, D, P>(qa, o, m, l, ring + (i % NST) * Geo::STAGE_BYTES, token0, len, len, scale_log2, lane);
+    attend_page<EB, D, P, HI>(qa, o, m, l, ring + (i % NST) * Geo::STAGE_BYTES, token0, len, len, scale_log2, lane);
     __syncwarp();  // every lane is done reading this stage before lane 0 refills it
     if (issued < n_mine) { issue(issued); ++issued; }
   }
@@ -473,7 +543,7 @@ prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, Pre
       if (i * P < warp_limit) {
 #pragma unroll
         for (int t = 0; t < MT; ++t)
-          attend_page<EB, D, P>(qa[t], o[t], m[t], l[t], ring + s * Geo::STAGE_BYTES, i * P, limit[t][0], limit[t][1],
+          attend_page<EB, D, P, true>(qa[t], o[t], m[t], l[t], ring + s * Geo::STAGE_BYTES, i * P, limit[t][0], limit[t][1],
                                 scale_log2, lane);
       }
       __syncwarp();
@@ -521,7 +591,7 @@ static int set_smem(K kernel, int bytes) {
   return 0;
 }
 
-template <int EB, int D, int NST>
+template <int EB, int D, int NST, bool HI>
 static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots, const uint8_t* active,
                          const cgym_kv_layout* kv, int layer, int rows, int n_q_heads, float scale, int n_splits,
                          float* workspace, int32_t* status, cudaStream_t stream) {
@@ -529,7 +599,7 @@ static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const
   using Geo = BlockGeom<EB, D, 64>;
   constexpr int ring = 4 * NST * Geo::STAGE_BYTES, merge = (4 * 16 * D + 2 * 4 * 16) * 4;
   constexpr int smem = ring > merge ? ring : merge;
-  auto kernel = decode_attention_mma_kernel<T, EB, D, 64, NST>;
+  auto kernel = decode_attention_mma_kernel<T, EB, D, 64, NST, HI>;
   static bool configured = false;
   if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
   const cudaError_t rc = launch_dependent(kernel, dim3(rows, kv->n_kv_heads, n_splits), dim3(128), smem, stream,
@@ -544,14 +614,22 @@ int launch_decode_attention_mma(void* out, const void* q, const int32_t* kv_lens
                                 float scale, int n_splits, float* workspace, int32_t* status, cudaStream_t stream) {
   const bool fp8 = kv->kv_dtype == CGYM_E4M3;
   // More CTAs than one per SM: short rings, several CTAs per SM. Fewer: one deep ring per SM.
-  static const int forced = [] {  // tuning aid: CGYM_ATTN_STAGES=1|3
+  static const int forced = [] {  // tuning aid: CGYM_ATTN_STAGES=1|2|3 (2: e4m3 caches only)
     const char* v = std::getenv("CGYM_ATTN_STAGES");
     return v != nullptr ? std::atoi(v) : 0;
   }();
   const bool shallow = forced ? forced == 1 : static_cast<int64_t>(rows) * kv->n_kv_heads * n_splits > 148;
-#define CGYM_DECODE(EB, NST) \
-  launch_decode<EB, 64, NST>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, workspace, status, stream)
-  if (fp8) return shallow ? CGYM_DECODE(1, 1) : CGYM_DECODE(1, 3);
+  // rows 8..15 of the 16-row MMA tile carry query heads only when more than 8 heads share a KV head
+  const bool hi = n_q_heads / kv->n_kv_heads > 8;
+#define CGYM_DECODE(EB, NST)                                                                                          \
+  (hi ? launch_decode<EB, 64, NST, true>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, \
+                                         workspace, status, stream)                                                   \
+      : launch_decode<EB, 64, NST, false>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, \
+                                          workspace, status, stream))
+  if (fp8) {
+    if (forced == 1) return CGYM_DECODE(1, 1);
+    return (shallow || forced == 2) ? CGYM_DECODE(1, 2) : CGYM_DECODE(1, 3);
+  }
   return shallow ? CGYM_DECODE(2, 1) : CGYM_DECODE(2, 3);
 #undef CGYM_DECODE
 }

@@ -243,14 +243,20 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
 // RING_KB bounds the TMA ring: 192 fills the SM for one CTA (large token tiles); 96 lets two CTAs
 // share an SM, so the CTAs of the NEXT kernel of a dependent-launch chain become resident - and
 // stream their first weight tiles - while this kernel's CTAs are still computing.
-template <int UN, bool FP8, int RING_KB>
+// FM = feature sub-tiles of 128 per CTA. FM = 2 (unsplit GEMMs over more than 128 tokens) runs two MMAs
+// per K step against the same token tile, into two TMEM accumulators: the activation tile is fetched
+// once for 256 features, which halves its share of the L2 -> shared-memory traffic that bounds these
+// shapes.
+template <int UN, bool FP8, int RING_KB, int FM = 1>
 __global__ void __launch_bounds__(GEMM_THREADS, RING_KB <= 96 ? 2 : 1)
 gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     GemmEpilogue ep) {
-  constexpr int STAGE_BYTES = (UM + UN) * SLICE_BYTES;
+  constexpr int W_BYTES = FM * UM * SLICE_BYTES;  // weight part of a stage; the token tile follows it
+  constexpr int STAGE_BYTES = W_BYTES + UN * SLICE_BYTES;
   constexpr int STAGES = (RING_KB * 1024 / STAGE_BYTES) > 8 ? 8 : (RING_KB * 1024 / STAGE_BYTES);
   constexpr int ELEMS_PER_SLICE = FP8 ? 128 : 64;
-  constexpr int TMEM_COLS = UN < 32 ? 32 : UN;
+  constexpr int TMEM_COLS = FM * UN < 32 ? 32 : FM * UN;
+  static_assert(TMEM_COLS <= 512, "two accumulators of UN columns must fit the 512 TMEM columns");
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[STAGES];
   __shared__ __align__(8) uint64_t bar_empty[STAGES];
@@ -262,7 +268,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   if (threadIdx.x == 0) CGYM_STAMP(0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t tiles = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const int n0 = blockIdx.x * UM, m0 = blockIdx.y * UN;
+  const int n0 = blockIdx.x * (UM * FM), m0 = blockIdx.y * UN;
   const int total_kb = (ep.K + ELEMS_PER_SLICE - 1) / ELEMS_PER_SLICE;
   const int per_split = (total_kb + gridDim.z - 1) / gridDim.z;
   const int kb_begin = blockIdx.z * per_split;
@@ -298,12 +304,15 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     for (int i = 0; i < prefetch; ++i) {
       const uint32_t full = smem_u32(&bar_full[i]);
       mbar_expect_tx(full, STAGE_BYTES);
-      tma_load_2d(tiles + i * STAGE_BYTES, &tmap_w, full, (kb_begin + i) * ELEMS_PER_SLICE, n0);
+#pragma unroll
+      for (int f = 0; f < FM; ++f)
+        tma_load_2d(tiles + i * STAGE_BYTES + f * UM * SLICE_BYTES, &tmap_w, full, (kb_begin + i) * ELEMS_PER_SLICE,
+                    n0 + f * UM);
     }
     pdl_wait();
     CGYM_STAMP(1);
     for (int i = 0; i < prefetch; ++i) {
-      tma_load_2d(tiles + i * STAGE_BYTES + UM * SLICE_BYTES, &tmap_x, smem_u32(&bar_full[i]),
+      tma_load_2d(tiles + i * STAGE_BYTES + W_BYTES, &tmap_x, smem_u32(&bar_full[i]),
                   (kb_begin + i) * ELEMS_PER_SLICE, m0);
       issued = i + 1;
     }
@@ -313,9 +322,10 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
       if (!mbar_wait(smem_u32(&bar_empty[s]), parity, &abort_flag)) break;
       const uint32_t full = smem_u32(&bar_full[s]);
       mbar_expect_tx(full, STAGE_BYTES);
-      const uint32_t a_dst = tiles + s * STAGE_BYTES, b_dst = a_dst + UM * SLICE_BYTES;
+      const uint32_t a_dst = tiles + s * STAGE_BYTES, b_dst = a_dst + W_BYTES;
       const int k_elem = (kb_begin + i) * ELEMS_PER_SLICE;
-      tma_load_2d(a_dst, &tmap_w, full, k_elem, n0);
+#pragma unroll
+      for (int f = 0; f < FM; ++f) tma_load_2d(a_dst + f * UM * SLICE_BYTES, &tmap_w, full, k_elem, n0 + f * UM);
       tma_load_2d(b_dst, &tmap_x, full, k_elem, m0);
       issued = i + 1;
     }
@@ -333,13 +343,17 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
       const int s = i % STAGES;
       if (!mbar_wait(smem_u32(&bar_full[s]), (i / STAGES) & 1, &abort_flag)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a_src = tiles + s * STAGE_BYTES, b_src = a_src + UM * SLICE_BYTES;
+      const uint32_t a_src = tiles + s * STAGE_BYTES, b_src = a_src + W_BYTES;
       const uint64_t da = umma_smem_desc(a_src), db = umma_smem_desc(b_src);
 #pragma unroll
       for (int k = 0; k < SLICE_BYTES / 32; ++k) {  // one MMA consumes 32 bytes of K per row
         const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-        if (FP8) umma_fp8(tmem_acc, da + 2 * k, db + 2 * k, idesc, acc);
-        else umma_bf16(tmem_acc, da + 2 * k, db + 2 * k, idesc, acc);
+#pragma unroll
+        for (int f = 0; f < FM; ++f) {  // feature sub-tile f: its weight rows, its accumulator columns
+          const uint64_t dw = da + static_cast<uint64_t>(f * (UM * SLICE_BYTES / 16) + 2 * k);
+          if (FP8) umma_fp8(tmem_acc + f * UN, dw, db + 2 * k, idesc, acc);
+          else umma_bf16(tmem_acc + f * UN, dw, db + 2 * k, idesc, acc);
+        }
       }
       umma_commit(smem_u32(&bar_empty[s]));
     }
@@ -347,13 +361,15 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   } else if (warp >= 2) {
     // ---- epilogue: TMEM lane = output feature, column = token ----
     const int quarter = warp & 3;  // a warp may only touch TMEM lanes [32 * (warp % 4), +32)
-    const int n_local = quarter * 32 + lane, n = n0 + n_local;
     pdl_wait();  // scales / row mask come from earlier kernels of the step
     if (n_kb > 0) mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps agree on abort_flag
     if (warp == 2 && lane == 0) CGYM_STAMP(2);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (abort_flag == 0 || ep.partial) {
+#pragma unroll 1
+      for (int f = 0; f < FM; ++f) {
+      const int n_local = quarter * 32 + lane, n = n0 + f * UM + n_local;
       const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
       // partial tile [UN][128]: in this CTA's shared memory (the ring is idle now) or in the workspace
       float* part = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)));
@@ -363,7 +379,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
       for (int c = 0; c < UN / 32; ++c) {
         uint32_t v[32];
         if (n_kb > 0 && abort_flag == 0) {
-          tmem_load32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, v);
+          tmem_load32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + f * UN + c * 32, v);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0u;
@@ -377,11 +393,12 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
             const int m = m0 + c * 32 + j;
             if (m >= ep.M) break;
             if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
-            float f = __uint_as_float(v[j]);
-            if (ep.x_scales != nullptr) f = __fmul_rn(__fmul_rn(f, ep.x_scales[m]), ws);
-            ep.y[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(f);
+            float val = __uint_as_float(v[j]);
+            if (ep.x_scales != nullptr) val = __fmul_rn(__fmul_rn(val, ep.x_scales[m]), ws);
+            ep.y[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(val);
           }
         }
+      }
       }
     }
   }
@@ -462,16 +479,16 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box
   return 0;
 }
 
-template <int UN, bool FP8, int RING_KB>
+template <int UN, bool FP8, int RING_KB, int FM = 1>
 static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmEpilogue& ep, dim3 grid,
                        cudaStream_t stream) {
-  constexpr int STAGE_BYTES = (UM + UN) * SLICE_BYTES;
+  constexpr int STAGE_BYTES = (UM * FM + UN) * SLICE_BYTES;
   constexpr int STAGES = (RING_KB * 1024 / STAGE_BYTES) > 8 ? 8 : (RING_KB * 1024 / STAGE_BYTES);
   constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
   static_assert(UN * UM * 4 <= STAGES * STAGE_BYTES, "the split-K partial tile must fit in the idle ring");
   static bool configured = false;  // per instantiation; the attribute is per function, set once
   if (!configured) {
-    const cudaError_t rc = cudaFuncSetAttribute(gemm_tcgen05_kernel<UN, FP8, RING_KB>,
+    const cudaError_t rc = cudaFuncSetAttribute(gemm_tcgen05_kernel<UN, FP8, RING_KB, FM>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     CGYM_REQUIRE(rc == cudaSuccess, "gemm: cannot reserve %d bytes of shared memory: %s", SMEM, cudaGetErrorString(rc));
     configured = true;
@@ -497,7 +514,7 @@ static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
   }
   config.attrs = attrs;
   config.numAttrs = n_attrs;
-  const cudaError_t rc = cudaLaunchKernelEx(&config, gemm_tcgen05_kernel<UN, FP8, RING_KB>, mw, mx, ep);
+  const cudaError_t rc = cudaLaunchKernelEx(&config, gemm_tcgen05_kernel<UN, FP8, RING_KB, FM>, mw, mx, ep);
   CGYM_REQUIRE(rc == cudaSuccess, "gemm(tcgen05): launch failed: %s", cudaGetErrorString(rc));
   return 0;
 }
@@ -533,7 +550,28 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
     const char* v = std::getenv("CGYM_GEMM_WIDE_FROM");
     return v != nullptr && std::atoi(v) > 0 ? std::atoi(v) : 257;
   }();
-  const int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M < wide_from ? 128 : 256));
+  int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M < wide_from ? 128 : 256));
+  // Two feature sub-tiles per CTA (one fetch of the token tile serves 256 features) for unsplit GEMMs
+  // over more than 128 tokens. With 256-token tiles (prefill) it pays unless halving the CTA count costs
+  // more in the last, partly filled wave than the saved traffic gains; for a decode batch of 129..256
+  // rows only the LM head is large enough, and it then takes the 256-token tile as well.
+  static const int fm_mode = [] {  // tuning aid: CGYM_GEMM_FM=1 never, 2 wherever the shape allows
+    const char* v = std::getenv("CGYM_GEMM_FM");
+    return v != nullptr ? std::atoi(v) : 0;
+  }();
+  bool dual = false;
+  if (M > 128 && N % (2 * UM) == 0 && force_splits <= 1 && fm_mode != 1) {
+    auto wave_fill = [](int ctas) { return static_cast<double>(ctas) / (148.0 * ((ctas + 147) / 148)); };
+    if (fm_mode == 2) {
+      dual = true;
+    } else if (un == 256) {
+      const int single = (N / UM) * ((M + 255) / 256);
+      dual = wave_fill(single / 2) >= wave_fill(single) - 0.1;
+    } else if (N / (2 * UM) >= 148) {
+      un = 256;
+      dual = true;
+    }
+  }
   const int n_tiles = (N + UM - 1) / UM, m_tiles = (M + un - 1) / un;
   const int total_kb = (K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
   // decode-sized token tiles take the half-SM ring (two CTAs per SM), larger ones the full ring
@@ -558,6 +596,7 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
     const int v = std::atoi(forced);
     if (v >= 1) splits = v;
   }
+  if (dual) splits = 1;
   if (splits > 8) splits = 8;
   if (splits > total_kb) splits = total_kb;
   splits = splits >= 8 ? 8 : (splits >= 4 ? 4 : (splits >= 2 ? 2 : 1));  // cluster sizes the reduction is built for
@@ -579,18 +618,22 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   if (int rc = make_map(&mx, x, M, K, un, fp8)) return rc;
   GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0,
                   split_ws};
-  dim3 grid(n_tiles, m_tiles, splits);
+  dim3 grid(dual ? n_tiles / 2 : n_tiles, m_tiles, splits);
 #ifdef CGYM_TRACE
   ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 8192ull : nullptr;
 #endif
   int rc = 0;
 #define LAUNCH_UN(U, R)                                                                 \
   rc = fp8 ? launch_tile<U, true, R>(mw, mx, ep, grid, stream) : launch_tile<U, false, R>(mw, mx, ep, grid, stream)
-  if (un == 32) { if (half_ring) LAUNCH_UN(32, 96); else LAUNCH_UN(32, 192); }
+#define LAUNCH_DUAL(U)                                                                       \
+  rc = fp8 ? launch_tile<U, true, 192, 2>(mw, mx, ep, grid, stream) : launch_tile<U, false, 192, 2>(mw, mx, ep, grid, stream)
+  if (dual) { if (un == 128) LAUNCH_DUAL(128); else LAUNCH_DUAL(256); }
+  else if (un == 32) { if (half_ring) LAUNCH_UN(32, 96); else LAUNCH_UN(32, 192); }
   else if (un == 64) { if (half_ring) LAUNCH_UN(64, 96); else LAUNCH_UN(64, 192); }
   else if (un == 128) { if (half_ring) LAUNCH_UN(128, 96); else LAUNCH_UN(128, 192); }
   else LAUNCH_UN(256, 192);
 #undef LAUNCH_UN
+#undef LAUNCH_DUAL
   if (rc) return rc;
   return check_launch("gemm_tcgen05");
 }

@@ -407,7 +407,8 @@ def test_gemm_simt_fp32_and_bf16(dev, shape):
 
 
 @pytest.mark.parametrize("shape", [(1, 128, 64), (8, 256, 256), (64, 512, 2048), (33, 384, 320), (128, 1536, 256),
-                                   (200, 256, 768), (300, 4096, 256), (64, 100, 192)])
+                                   (200, 256, 768), (300, 4096, 256), (64, 100, 192),
+                                   (200, 37888, 64), (300, 16384, 128)])  # the last two: two feature sub-tiles per CTA
 def test_gemm_tcgen05_matches_fp32_accumulation(dev, shape):
     m, n, k = shape
     rng = np.random.default_rng(n + k)
@@ -443,7 +444,8 @@ def test_gemm_tcgen05_split_k_is_deterministic_and_correct(dev):
 
 
 @pytest.mark.parametrize("impl", [1, 2])
-@pytest.mark.parametrize("shape", [(5, 128, 256), (64, 256, 1024), (100, 384, 512)])
+@pytest.mark.parametrize("shape", [(5, 128, 256), (64, 256, 1024), (100, 384, 512),
+                                   (256, 37888, 128), (300, 16384, 128)])  # the last two: two feature sub-tiles per CTA
 def test_gemm_fp8_scaled_epilogue(dev, impl, shape):
     m, n, k = shape
     rng = np.random.default_rng(k)
