@@ -17,6 +17,12 @@ through the public API with pinned-host prompts and a device->host read of token
 lengths inside the timed region (the reference benchmark's convention). ``roofline`` is the decode
 step graph: algorithmic bytes (weights + KV history per step) over its CUDA-event duration against
 the measured HBM copy bandwidth. ``cpu_baseline`` times the CPU oracle on a bounded sample.
+
+After the default workload the same process also runs the FP8 rollout configuration once
+("fp8-queue2048x256": FP8 W8A8 MLP + e4m3 KV, 2048 queued requests over 256 live slots through a
+generation session; one short warm-up pass, one full timed pass) and attaches its numbers as
+``fp8_rollout`` (``--fp8-rollout off`` skips it; ``--workload fp8-queue2048x256`` runs it as the
+line itself, every step being one pass over the whole queue).
 """
 from __future__ import annotations
 
@@ -36,6 +42,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "generated tokens/s"
 UNIT = "tokens/s"
+DEFAULT_WORKLOAD = "bf16-b64x512"
+FP8_ROLLOUT_WORKLOAD = "fp8-queue2048x256"  # also measured (one pass) after the default workload: `fp8_rollout`
 
 WORKLOADS = {
     # name: (model, batch, prompt_low, prompt_high, new_tokens, graph options)
@@ -277,6 +285,16 @@ def run_ours(args) -> dict:
     }
     if broadcast_ms is not None:
         result["weight_broadcast"] = {"ms": round(broadcast_ms, 2), "bytes": int(moved)}
+    if args.fp8_rollout == "on" or (args.fp8_rollout == "auto" and args.workload == DEFAULT_WORKLOAD
+                                    and not args.batch and not args.new_tokens):
+        # the FP8 continuous-batching configuration next to the headline line: one short warm-up pass and
+        # one full timed pass of the request queue on the same GPU(s), device-timed like the line itself
+        del engine, decoder, ids_dev, cu_dev
+        torch.cuda.empty_cache()
+        nested = argparse.Namespace(**{**vars(args), "workload": FP8_ROLLOUT_WORKLOAD, "steps": 1, "warmup": 0})
+        extra = run_queue(nested, nested=True)
+        result["fp8_rollout"] = {key: extra[key] for key in ("value", "unit", "ms_per_step", "dtype", "config", "roofline",
+                                                             "gpu_launches", "clocks", "warmup_note")}
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(model, seconds_budget=args.cpu_seconds)
     if world > 1:
@@ -299,8 +317,10 @@ def queue_requests(name: str, vocab: int, seed: int):
     return prompts, [int(v) for v in limits]
 
 
-def run_queue(args) -> dict:
-    """One step = the whole request queue through one generation session."""
+def run_queue(args, *, nested: bool = False) -> dict:
+    """One step = the whole request queue through one generation session. ``nested``: called from another
+    workload's run inside its process group - one short warm-up pass over the first slots' worth of requests
+    (to capture the graphs and size the buffers), no host-buffer pass, and the result on every rank."""
     import torch
     import torch.distributed as dist
     from climbing_gym_b200 import _native as nv
@@ -313,7 +333,7 @@ def run_queue(args) -> dict:
         raise RuntimeError("bench.py needs a CUDA device: the engine has no CPU path")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    if world > 1:
+    if world > 1 and not nested:
         dist.init_process_group("nccl", device_id=device)
     model, options, n_requests, slots, max_len, cap, mean_out, median, sigma, clip, poll_steps = QUEUE_WORKLOADS[args.workload]
     engine, cfg = build_engine(model, device, options, max_model_len=max_len)
@@ -321,11 +341,17 @@ def run_queue(args) -> dict:
         broadcast_policy_weights(engine, src=0)
     prompts, limits = queue_requests(args.workload, cfg.vocab_size, seed=2000 + rank)
     staged = [torch.tensor(p, device=device, dtype=torch.int64) for p in prompts]
-    samplings = [LFM25SamplingConfig(temperature=1.0, top_k=0, top_p=1.0, max_new_tokens=limit, seed=index,
-                                     ignore_eos=True, return_logprobs=True) for index, limit in enumerate(limits)]
+    queue_samplings = [LFM25SamplingConfig(temperature=1.0, top_k=0, top_p=1.0, max_new_tokens=limit, seed=index,
+                                           ignore_eos=True, return_logprobs=True) for index, limit in enumerate(limits)]
+    n_queue = n_requests
 
-    def one_pass(on_device: bool) -> dict:
+    def one_pass(on_device: bool, *, short: bool = False) -> dict:
         generated, next_request, live = 0, 0, 0
+        n_requests, samplings = n_queue, queue_samplings
+        if short:  # warm-up: the first slots' worth of requests, a few tokens each
+            n_requests = min(slots, n_queue)
+            samplings = [LFM25SamplingConfig(temperature=1.0, max_new_tokens=min(limit, 2 * poll_steps), seed=index,
+                                             ignore_eos=True) for index, limit in enumerate(limits[:n_requests])]
         with engine.generation_session(max_batch_size=slots, max_new_tokens=cap, profile_timings=True) as session:
             def admit(count, into=None):
                 nonlocal next_request, live
@@ -374,11 +400,13 @@ def run_queue(args) -> dict:
 
     for _ in range(args.warmup):
         one_pass(True)
+    if nested:
+        one_pass(True, short=True)
     launches_before = nv.launch_count()
     with ClockSampler(local_rank) as clocks:
         total_ms, passes = timed(True, args.steps)
     launches = nv.launch_count() - launches_before
-    e2e_ms, _ = timed(False, args.steps)
+    e2e_ms = timed(False, args.steps)[0] if not nested else total_ms
     expected = sum(limits)
     if any(p["generated"] != expected for p in passes):
         raise RuntimeError("a pass did not deliver every request's output budget")
@@ -419,6 +447,10 @@ def run_queue(args) -> dict:
                 "d2h_bytes_per_step": int(expected * 12 + replays / poll_steps * slots), "ms_per_step": round(e2e_ms / args.steps, 3)},
         "gpu_launches": int(launches), "clocks": clocks.summary(), "roofline": roofline,
     }
+    if nested:
+        del result["e2e"]
+        result["warmup_note"] = "one short pass (first slots' worth of requests, a few tokens each), then one full timed pass"
+        return result
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(model, seconds_budget=args.cpu_seconds)
     if world > 1:
@@ -490,7 +522,10 @@ def main():
     parser.add_argument("--steps", type=int, default=3)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    parser.add_argument("--workload", default="bf16-b64x512", choices=sorted([*WORKLOADS, *QUEUE_WORKLOADS]))
+    parser.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted([*WORKLOADS, *QUEUE_WORKLOADS]))
+    parser.add_argument("--fp8-rollout", default="auto", choices=["auto", "on", "off"],
+                        help="append one timed pass of the FP8 continuous-batching queue as `fp8_rollout` "
+                             "(auto: with the default workload at its default size)")
     parser.add_argument("--batch", type=int, default=0, help="override prompts per GPU")
     parser.add_argument("--new-tokens", type=int, default=0, help="override sampled tokens per prompt")
     parser.add_argument("--no-cpu-baseline", action="store_true")
