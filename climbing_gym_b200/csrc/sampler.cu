@@ -230,11 +230,20 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
 
 static int pick_parts(int rows, int vocab, const float* workspace) {
   if (workspace == nullptr || vocab < 8192) return 1;
-  int parts = (2 * 148 + rows - 1) / rows;  // about two CTAs per SM in flight
-  const int by_vocab = vocab / 4096;
-  if (parts > by_vocab) parts = by_vocab;
-  if (parts > SAMPLE_MAX_PARTS) parts = SAMPLE_MAX_PARTS;
-  return parts < 1 ? 1 : parts;
+  // Two 512-thread CTAs fit an SM (62 registers per thread), i.e. 296 CTAs run at once. The kernel's time
+  // is the number of such waves times a slice's share of the row, so pick the slice count that minimises
+  // waves / parts (64 rows: 4 slices fill one wave where 5 would start a second; 256 rows: 8 slices leave
+  // a short last wave), with a small charge per slice for its part of the final merge.
+  int by_vocab = vocab / 4096;
+  if (by_vocab > SAMPLE_MAX_PARTS) by_vocab = SAMPLE_MAX_PARTS;
+  int best = 1;
+  double best_cost = 1.0e30;
+  for (int parts = 1; parts <= by_vocab; ++parts) {
+    const int waves = (rows * parts + 2 * 148 - 1) / (2 * 148);
+    const double cost = static_cast<double>(waves) / parts + 0.01 * parts;
+    if (cost < best_cost) { best_cost = cost; best = parts; }
+  }
+  return best;
 }
 
 // ---- top-k / top-p support thresholds ---------------------------------------------------------------
