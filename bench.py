@@ -517,6 +517,8 @@ def run_reference(args) -> dict:
 
 
 def main():
+    # stdout carries the one JSON line and nothing else: NCCL's banner / debug lines go to stderr
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=3)

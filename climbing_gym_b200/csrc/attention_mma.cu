@@ -3,7 +3,8 @@
 // Data movement: a (page, kv_head) block of the cache - K as [token][dim] followed by V^T as
 // [dim][token], 16-byte chunks already XOR-swizzled in global memory - is brought into shared memory
 // by ONE cp.async.bulk (TMA bulk copy, mbarrier completion), e4m3 caches add one 512-byte copy of the
-// per-token scales. Fragment loads are then plain 32-bit shared loads without bank conflicts.
+// per-token scales. Fragment loads are bank-conflict free: ldmatrix.x4 on bf16 pages, one 16-byte load
+// per K row / V^T row on e4m3 pages (32-bit loads remain where registers are short).
 //
 // Math: S = Q.K^T and O += P.V on mma.sync m16n8k16 with fp32 accumulation; an m-tile is 16
 // (token, head) rows of one GQA group, so the G query heads that share a KV head reuse every staged
@@ -12,11 +13,11 @@
 // per-token K scale multiplies the score, the V scale multiplies P before its rounding.
 //
 // decode kernel : one query token per row, grid (rows, kv_heads, splits); the four warps of a CTA
-//                 take pages round-robin, each with its own 2-stage bulk-copy ring and softmax
+//                 take pages round-robin, each with its own 1- to 3-page bulk-copy ring and softmax
 //                 state, merged through shared memory (and splits through an fp32 workspace).
 // prefill kernel: a CTA owns up to 128 / G consecutive query tokens of one sequence for one KV head;
 //                 a producer warp streams the causal range of pages through a 4-stage ring that the
-//                 four consumer warps (two m-tiles each) share.
+//                 eight consumer warps (one m-tile each) share.
 // Every mbarrier wait is bounded; on expiry the CTA flags CGYM_STATUS_WAIT_TIMEOUT and drains.
 #include <cuda_fp16.h>
 
@@ -77,6 +78,11 @@ __device__ __forceinline__ void att_lds128(uint32_t addr, uint32_t (&v)[4]) {
 }
 __device__ __forceinline__ void att_lds128f(uint32_t addr, float (&v)[4]) {
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "r"(addr));
+}
+// four 8 x 8 b16 matrices; lane l supplies the address of row l % 8 of matrix l / 8
+__device__ __forceinline__ void att_ldmatrix_x4(uint32_t addr, uint32_t (&v)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(addr));
 }
 __device__ __forceinline__ float att_lds_f32(uint32_t addr) {
   float v;
@@ -176,7 +182,7 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qa)[D / 16][4], const TQ
 // column stands for (BlockGeom::token_of) is chosen such that the P fragments line up with 16
 // consecutive tokens of a V^T row. The per-token scales of a lane's columns are then four
 // consecutive floats: one 16-byte load per pair of n-tiles.
-template <int EB, int D, int P, bool HI>
+template <int EB, int D, int P, bool HI, bool LDM = !HI>
 __device__ __forceinline__ void attend_page(const uint32_t (&qa)[D / 16][4], float (&o)[D / 8][4], float (&m)[2],
                                             float (&l)[2], uint32_t stage, int page_token0, int limit_lo,
                                             int limit_hi, float scale_log2, int lane) {
@@ -207,7 +213,9 @@ __device__ __forceinline__ void attend_page(const uint32_t (&qa)[D / 16][4], flo
         }
       }
     }
-  } else {
+  } else if constexpr (!LDM) {
+    // bf16 pages, plain 32-bit fragment loads (kept for callers whose register budget the ldmatrix form
+    // below would overflow: two m-tiles per warp)
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       const int tok = Geo::token_of(t, c8);
@@ -217,6 +225,29 @@ __device__ __forceinline__ void attend_page(const uint32_t (&qa)[D / 16][4], flo
         const uint32_t b0 = att_lds32(row_addr + kv_swizzle(tok, 2 * k, Geo::K_CPR) * 16 + 4 * j);
         const uint32_t b1 = att_lds32(row_addr + kv_swizzle(tok, 2 * k + 1, Geo::K_CPR) * 16 + 4 * j);
         att_mma<F16>(s[t], qa[k], b0, b1);
+      }
+    }
+  } else {
+    // bf16 pages: ldmatrix.x4 fetches the B fragments of two K steps of one n-tile at once (matrix m of
+    // the four = 16-byte chunk 4 h + m of the K rows 8 t .. 8 t + 7, one row address per lane)
+    static_assert(KS % 2 == 0 && NT % 2 == 0, "fragment loads pair K steps and n-tiles");
+    const int lrow = lane & 7, lmat = lane >> 3;
+    constexpr int TG = HI ? 1 : 2;  // n-tiles in flight: independent accumulators between dependent MMAs
+#pragma unroll
+    for (int t0 = 0; t0 < NT; t0 += TG) {
+      uint32_t kb[TG][KS / 2][4];
+#pragma unroll
+      for (int tt = 0; tt < TG; ++tt) {
+        const int tok = 8 * (t0 + tt) + lrow;
+#pragma unroll
+        for (int h = 0; h < KS / 2; ++h)
+          att_ldmatrix_x4(stage + tok * Geo::K_ROW + kv_swizzle(tok, 4 * h + lmat, Geo::K_CPR) * 16, kb[tt][h]);
+      }
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+#pragma unroll
+        for (int tt = 0; tt < TG; ++tt)
+          att_mma<F16>(s[t0 + tt], qa[k], kb[tt][k >> 1][2 * (k & 1)], kb[tt][k >> 1][2 * (k & 1) + 1]);
       }
     }
   }
@@ -309,16 +340,37 @@ __device__ __forceinline__ void attend_page(const uint32_t (&qa)[D / 16][4], flo
         }
       }
     }
-  } else {
+  } else if constexpr (!LDM) {
 #pragma unroll
     for (int k = 0; k < PS; ++k) {
 #pragma unroll
       for (int u = 0; u < OT; ++u) {
-        const int dim = 8 * u + c8;
+        const int dim = 8 * u + c8;  // V^T row this thread feeds for output column c8
         const uint32_t row_addr = vt + dim * Geo::V_ROW;
         const uint32_t b0 = att_lds32(row_addr + kv_swizzle(dim, 2 * k, Geo::V_CPR) * 16 + 4 * j);
         const uint32_t b1 = att_lds32(row_addr + kv_swizzle(dim, 2 * k + 1, Geo::V_CPR) * 16 + 4 * j);
         att_mma<F16>(o[u], pa[k], b0, b1);
+      }
+    }
+  } else {
+    static_assert(PS % 2 == 0 && OT % 2 == 0, "fragment loads pair K steps and output tiles");
+    const int lrow = lane & 7, lmat = lane >> 3;
+    constexpr int UG = HI ? 1 : 2;
+#pragma unroll
+    for (int u0 = 0; u0 < OT; u0 += UG) {
+      uint32_t vb[UG][PS / 2][4];
+#pragma unroll
+      for (int uu = 0; uu < UG; ++uu) {
+        const int dim = 8 * (u0 + uu) + lrow;  // V^T row (one head dim), 16-byte chunks of 8 tokens
+#pragma unroll
+        for (int h = 0; h < PS / 2; ++h)
+          att_ldmatrix_x4(vt + dim * Geo::V_ROW + kv_swizzle(dim, 4 * h + lmat, Geo::V_CPR) * 16, vb[uu][h]);
+      }
+#pragma unroll
+      for (int k = 0; k < PS; ++k) {
+#pragma unroll
+        for (int uu = 0; uu < UG; ++uu)
+          att_mma<F16>(o[u0 + uu], pa[k], vb[uu][k >> 1][2 * (k & 1)], vb[uu][k >> 1][2 * (k & 1) + 1]);
       }
     }
   }
@@ -471,12 +523,13 @@ struct PrefillTiles {
   const int32_t* pos0;   // cache position of the tile's first query token
 };
 
-template <typename TQ, int EB, int D, int P>
-__global__ void __launch_bounds__(160, 1)
+// MT = m-tiles (16 rows) per consumer warp; the 128 rows of a CTA take 8 / MT consumer warps plus the producer.
+template <typename TQ, int EB, int D, int P, int MT>
+__global__ void __launch_bounds__(32 * (8 / MT + 1), 1)
 prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, PrefillTiles tiles, cgym_kv_layout kv,
                              int layer, int n_q_heads, float scale, int32_t* __restrict__ status) {
   using Geo = BlockGeom<EB, D, P>;
-  constexpr int OT = D / 8, STAGES = 4, MT = 2;
+  constexpr int OT = D / 8, STAGES = 4, CW = 8 / MT;  // CW consumer warps
   extern __shared__ __align__(128) uint8_t att_smem[];
   __shared__ __align__(8) uint64_t bar_full[STAGES];
   __shared__ __align__(8) uint64_t bar_empty[STAGES];
@@ -489,14 +542,14 @@ prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, Pre
   const int n_pages = (pos0 + ntok + P - 1) / P;  // causal range of the tile's last token
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int s = 0; s < STAGES; ++s) { att_bar_init(att_smem_u32(&bar_full[s]), 1); att_bar_init(att_smem_u32(&bar_empty[s]), 4); }
+    for (int s = 0; s < STAGES; ++s) { att_bar_init(att_smem_u32(&bar_full[s]), 1); att_bar_init(att_smem_u32(&bar_empty[s]), CW); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   const uint32_t ring = att_smem_u32(att_smem);
   const int32_t* table = kv.block_table + static_cast<int64_t>(slot) * kv.max_blocks;
 
-  if (warp == 4) {
+  if (warp == CW) {
     // ---- producer ----
     if (lane == 0) {
       const uint8_t* pool = static_cast<const uint8_t*>(kv.kv_pool);
@@ -516,7 +569,7 @@ prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, Pre
           att_bar_wait(att_smem_u32(&bar_full[i % STAGES]), (i / STAGES) & 1, &abort_flag);
     }
   } else {
-    // ---- consumers: warp w owns rows [32 w, 32 w + 32) as two m-tiles ----
+    // ---- consumers: warp w owns rows [16 MT w, 16 MT (w + 1)) as MT m-tiles ----
     uint32_t qa[MT][D / 16][4];
     float o[MT][OT][4], m[MT][2], l[MT][2];
     int limit[MT][2];
@@ -524,7 +577,7 @@ prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, Pre
     int warp_limit = 0;
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
-      const int r_lo = warp * 32 + t * 16 + (lane >> 2), r_hi = r_lo + 8;
+      const int r_lo = warp * (16 * MT) + t * 16 + (lane >> 2), r_hi = r_lo + 8;
       load_q_frags<EB, D, TQ>(qa[t], q_base, r_lo, r_hi, n_rows, G, n_q_heads, kh * G, lane);
       limit[t][0] = r_lo < n_rows ? pos0 + r_lo / G + 1 : 0;
       limit[t][1] = r_hi < n_rows ? pos0 + r_hi / G + 1 : 0;
@@ -543,7 +596,7 @@ prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, Pre
       if (i * P < warp_limit) {
 #pragma unroll
         for (int t = 0; t < MT; ++t)
-          attend_page<EB, D, P, true>(qa[t], o[t], m[t], l[t], ring + s * Geo::STAGE_BYTES, i * P, limit[t][0], limit[t][1],
+          attend_page<EB, D, P, true, MT == 1>(qa[t], o[t], m[t], l[t], ring + s * Geo::STAGE_BYTES, i * P, limit[t][0], limit[t][1],
                                 scale_log2, lane);
       }
       __syncwarp();
@@ -558,7 +611,7 @@ prefill_attention_mma_kernel(TQ* __restrict__ out, const TQ* __restrict__ q, Pre
         float sum = l[t][h];
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        const int R = warp * 32 + t * 16 + (lane >> 2) + 8 * h;
+        const int R = warp * (16 * MT) + t * 16 + (lane >> 2) + 8 * h;
         if (R < n_rows) {
           const float inv = 1.0f / fmaxf(sum, 1.0e-20f);
           TQ* dst = out + (static_cast<int64_t>(row0 + R / G) * n_q_heads + kh * G + (R % G)) * D;
@@ -640,11 +693,23 @@ static int launch_prefill(void* out, const void* q, const PrefillTiles& tiles, c
   using T = __nv_bfloat16;
   using Geo = BlockGeom<EB, D, 64>;
   constexpr int smem = 4 * Geo::STAGE_BYTES;
-  auto kernel = prefill_attention_mma_kernel<T, EB, D, 64>;
-  static bool configured = false;
-  if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
-  kernel<<<dim3(n_tiles, kv->n_kv_heads), 160, smem, stream>>>(static_cast<T*>(out), static_cast<const T*>(q), tiles, *kv,
-                                                               layer, n_q_heads, scale, status);
+  static const int mt = [] {  // tuning aid: CGYM_PREFILL_MT=1|2 m-tiles per consumer warp
+    const char* v = std::getenv("CGYM_PREFILL_MT");
+    return v != nullptr && std::atoi(v) == 2 ? 2 : 1;
+  }();
+  if (mt == 2) {
+    auto kernel = prefill_attention_mma_kernel<T, EB, D, 64, 2>;
+    static bool configured = false;
+    if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
+    kernel<<<dim3(n_tiles, kv->n_kv_heads), 160, smem, stream>>>(static_cast<T*>(out), static_cast<const T*>(q), tiles,
+                                                                 *kv, layer, n_q_heads, scale, status);
+  } else {
+    auto kernel = prefill_attention_mma_kernel<T, EB, D, 64, 1>;
+    static bool configured = false;
+    if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
+    kernel<<<dim3(n_tiles, kv->n_kv_heads), 288, smem, stream>>>(static_cast<T*>(out), static_cast<const T*>(q), tiles,
+                                                                 *kv, layer, n_q_heads, scale, status);
+  }
   return 0;
 }
 
