@@ -2,7 +2,7 @@
 
 Run from the repository root in a container where the reference checkout is mounted:
 
-    python tests/golden/make_golden.py --reference /root/reference/src
+    python tests/golden/make_golden.py --reference <reference checkout>/src
 
 The reference is imported read-only and executed as-is: its eager ``LFM25Engine`` for the
 model-level vectors, and its Triton kernels under Triton's CPU interpreter
@@ -315,7 +315,7 @@ def penalty_vectors():
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference/src")
+    parser.add_argument("--reference", required=True, help="the src/ directory of a reference checkout")
     parser.add_argument("--only", default="")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
