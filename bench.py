@@ -517,8 +517,6 @@ def run_reference(args) -> dict:
 
 
 def main():
-    # stdout carries the one JSON line and nothing else: NCCL's banner / debug lines go to stderr
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=3)
@@ -533,12 +531,17 @@ def main():
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=25.0)
     args = parser.parse_args()
+    # stdout carries the one JSON line and nothing else: file descriptor 1 is pointed at stderr for the
+    # run (NCCL prints its version banner there from C), and the line goes to a duplicate of the real one
+    sys.stdout.flush()
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         result = run_reference(args)
     else:
         result = run_queue(args) if args.workload in QUEUE_WORKLOADS else run_ours(args)
     if result:
-        print(json.dumps(result), flush=True)
+        print(json.dumps(result), file=json_out, flush=True)
 
 
 if __name__ == "__main__":
