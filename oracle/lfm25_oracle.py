@@ -94,12 +94,16 @@ class OracleEngine:
     """
 
     def __init__(self, cfg: OracleConfig, state_dict: dict, *, dtype: str = "fp32",
-                 max_model_len: int = 4096, fp8_mlp: bool = False, fp8_kv: bool = False):
+                 max_model_len: int = 4096, fp8_mlp: bool = False, fp8_kv: bool = False,
+                 weights_exact: bool = False, fp8_lm_head: bool = False):
+        """``weights_exact``: the arrays of ``state_dict`` are already representable in the model
+        dtype (e.g. copied from a bf16 checkpoint), so the load-time cast is skipped: at 1.2 B
+        parameters the numpy cast alone takes minutes."""
         self.cfg, self.dtype = cfg, dtype
         self.rd = rounder(dtype)
-        self.fp8_mlp, self.fp8_kv = bool(fp8_mlp), bool(fp8_kv)
+        self.fp8_mlp, self.fp8_kv, self.fp8_lm_head = bool(fp8_mlp), bool(fp8_kv), bool(fp8_lm_head)
         self.max_model_len = int(max_model_len)
-        rd = self.rd
+        rd = (lambda a: a) if weights_exact else self.rd
 
         def t(key):
             return rd(np.asarray(state_dict[key], dtype=np.float32))
@@ -124,12 +128,12 @@ class OracleEngine:
                 layer.update(conv_in=t(f"{p}.conv.in_proj.weight"), conv_w=t(f"{p}.conv.conv.weight")[:, 0, :],
                              conv_out=t(f"{p}.conv.out_proj.weight"), cache_index=n_conv)
                 n_conv += 1
-            if self.fp8_mlp:
-                # PackedFP8Weight.from_weight: per-output-channel row quantisation (lfm25_fp8.py:127-131)
-                for name in ("w13", "w2"):
-                    codes, scales = quantize_rows_e4m3(layer[name])
-                    layer[name + "_q"], layer[name + "_s"] = decode_e4m3(codes), scales
             self.layers.append(layer)
+        if self.fp8_mlp:
+            self.prepare_fp8()
+        if self.fp8_lm_head:  # the vocabulary head joins the FP8 copies (lfm25_cuda.py:103-105)
+            codes, self.head_s = quantize_rows_e4m3(self.head)
+            self.head_q = decode_e4m3(codes)
         self.n_attn, self.n_conv = n_attn, n_conv
         half = cfg.head_dim // 2
         inv_freq = (1.0 / (np.float32(cfg.rope_theta) ** (np.arange(0, cfg.head_dim, 2, dtype=np.float32)
@@ -137,6 +141,16 @@ class OracleEngine:
         freqs = np.arange(self.max_model_len, dtype=np.float32)[:, None] * inv_freq[None, :]
         self.rope_cos, self.rope_sin = np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
         assert self.rope_cos.shape[1] == half
+
+    def prepare_fp8(self) -> None:
+        """FP8 copies of w13 / w2: per-output-channel row quantisation (PackedFP8Weight.from_weight,
+        lfm25_fp8.py:127-131). Idempotent, so one engine can serve bf16 and FP8 runs by switching
+        ``fp8_mlp`` / ``fp8_kv`` between them."""
+        for layer in self.layers:
+            for name in ("w13", "w2"):
+                if name + "_q" not in layer:
+                    codes, scales = quantize_rows_e4m3(layer[name])
+                    layer[name + "_q"], layer[name + "_s"] = decode_e4m3(codes), scales
 
     # ------------------------------------------------------------------ primitives
     def linear(self, x, w):
@@ -321,7 +335,11 @@ class OracleEngine:
             hidden = rd(hidden + self.mlp(layer, y, decode=True))
         for s in states:
             s.length += 1
-        return self.linear(self.rms_norm(hidden, self.final_norm), self.head)
+        final = self.rms_norm(hidden, self.final_norm)
+        if self.fp8_lm_head:  # decode-time FP8 head: quantised final norm output (lfm25_cuda.py:181-191)
+            codes, a_s = quantize_rows_e4m3(final)
+            return rd((decode_e4m3(codes) @ self.head_q.T) * a_s[:, None] * self.head_s[None, :])
+        return self.linear(final, self.head)
 
     # ------------------------------------------------------------------ sampler
     def sample(self, logits, *, temperature: float, seed: int, step: int, rows=None):
@@ -431,6 +449,43 @@ class OracleEngine:
         shape = (len(prompts), repeats)
         return dict(token_ids=tokens.reshape(*shape, n_new), lengths=lengths.reshape(shape),
                     logprobs=logprobs.reshape(*shape, n_new), finish_reasons=reasons.reshape(shape))
+
+    # ------------------------------------------------------------------ teacher forcing
+    def teacher_forced(self, prompts: Sequence[Sequence[int]], tokens, *, probe=None) -> dict:
+        """Decode a GIVEN continuation and report what this engine thinks of every token of it.
+
+        ``tokens`` [B, N] are the continuations another implementation produced for ``prompts`` (greedy or
+        sampled). Row b is prefilled with prompts[b]; step s scores tokens[b, s] against this engine's
+        logits for that position and then feeds it as the next decode input, exactly like the generate
+        loop (lfm25_cuda.py:315-372), so every step is comparable even after the two implementations
+        would have chosen different tokens. Returns fp32 arrays [B, N]: ``logprobs`` of the given tokens,
+        this engine's greedy choice ``argmax``, its top logit ``top_logit`` and the given token's logit
+        ``given_logit`` (top_logit - given_logit is the margin by which this engine prefers its own
+        choice; 0 where the choices agree). ``probe`` [B, N] (optional) names one more token per step
+        whose logit is reported as ``probe_logit`` (e.g. a third implementation's choice)."""
+        tokens = np.asarray(tokens, dtype=np.int64)
+        bsz, n_new = tokens.shape
+        states, first = [], []
+        for prompt in prompts:
+            st, logits = self.prefill(prompt)
+            states.append(st)
+            first.append(logits)
+        logits = np.stack(first).astype(np.float32)
+        out = dict(logprobs=np.zeros((bsz, n_new), np.float32), argmax=np.zeros((bsz, n_new), np.int64),
+                   top_logit=np.zeros((bsz, n_new), np.float32), given_logit=np.zeros((bsz, n_new), np.float32),
+                   probe_logit=np.zeros((bsz, n_new), np.float32))
+        rows = np.arange(bsz)
+        for step in range(n_new):
+            given = tokens[:, step]
+            out["logprobs"][:, step] = self.logprob_of(logits, given)
+            out["argmax"][:, step] = np.argmax(logits, axis=-1)
+            out["top_logit"][:, step] = logits.max(-1)
+            out["given_logit"][:, step] = logits[rows, given]
+            if probe is not None:
+                out["probe_logit"][:, step] = logits[rows, np.asarray(probe, dtype=np.int64)[:, step]]
+            if step + 1 < n_new:
+                logits = self.decode(states, given).astype(np.float32)
+        return out
 
     # ------------------------------------------------------------------ scoring
     def score_completions(self, prompts, completions):

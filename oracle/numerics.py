@@ -83,8 +83,9 @@ E4M3_VALUES = _e4m3_table()
 _POS = E4M3_VALUES[:0x7F].astype(np.float64)  # 0 .. 448, ascending
 
 
-def encode_e4m3(x: np.ndarray) -> np.ndarray:
-    """fp32 -> e4m3fn code (uint8), round-to-nearest-even, saturating to +-448."""
+def encode_e4m3_search(x: np.ndarray) -> np.ndarray:
+    """fp32 -> e4m3fn code by searching the table of code points (slow; the definition the bit-wise
+    encoder below is checked against)."""
     x = np.asarray(x, dtype=np.float32)
     mag = np.minimum(np.abs(x.astype(np.float64)), E4M3_MAX)
     hi = np.searchsorted(_POS, mag, side="left").clip(0, len(_POS) - 1)
@@ -97,6 +98,22 @@ def encode_e4m3(x: np.ndarray) -> np.ndarray:
     return code
 
 
+def encode_e4m3(x: np.ndarray) -> np.ndarray:
+    """fp32 -> e4m3fn code (uint8), round-to-nearest-even, saturating to +-448.
+
+    Bit-wise: above 2^-6 the fp32 mantissa is rounded to three bits (the carry runs into the exponent
+    field, as it must) and the exponent re-biased from 127 to 7; below it the value is a multiple of
+    2^-9, rounded half-to-even. Same codes as encode_e4m3_search, two orders of magnitude faster."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    mag = np.minimum(np.abs(x), np.float32(E4M3_MAX))
+    bits = mag.view(np.uint32)
+    lsb = (bits >> np.uint32(20)) & np.uint32(1)
+    normal = ((bits + np.uint32(0x7FFFF) + lsb) >> np.uint32(20)).astype(np.int32) - np.int32(960)
+    subnormal = np.rint(mag * np.float32(512.0)).astype(np.int32)
+    code = np.where(mag < np.float32(2.0 ** -6), subnormal, normal).astype(np.uint8)
+    return np.where(np.signbit(x), code | np.uint8(0x80), code).astype(np.uint8)
+
+
 def decode_e4m3(code: np.ndarray) -> np.ndarray:
     return E4M3_VALUES[np.asarray(code, dtype=np.uint8)]
 
@@ -105,8 +122,24 @@ def quantize_rows_e4m3(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """Per-row dynamic scale: scale = max(absmax/448, 1e-12); q = e4m3(clamp(x/scale)).
 
     Follows src/climbing_gym/inference/lfm25_fp8.py:16-23. Returns (codes uint8, scales fp32).
+    Matrices of more than a few million elements are cut into row blocks that run on a thread pool
+    (numpy releases the GIL inside its loops); rows are independent, so the result is the same.
     """
     x = np.asarray(x, dtype=np.float32)
+    if x.ndim == 2 and x.size > (1 << 22):
+        import os
+        from concurrent.futures import ThreadPoolExecutor
+
+        workers = min(32, os.cpu_count() or 1)
+        bounds = np.linspace(0, x.shape[0], 4 * workers + 1).astype(int)
+        blocks = [x[a:b] for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
+        with ThreadPoolExecutor(workers) as pool:
+            parts = list(pool.map(_quantize_rows_block, blocks))
+        return np.concatenate([p[0] for p in parts]), np.concatenate([p[1] for p in parts])
+    return _quantize_rows_block(x)
+
+
+def _quantize_rows_block(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     absmax = np.max(np.abs(x), axis=-1)
     scale = np.maximum(absmax / np.float32(448.0), np.float32(1.0e-12)).astype(np.float32)
     q = np.clip(x / scale[..., None], -448.0, 448.0).astype(np.float32)

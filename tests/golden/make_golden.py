@@ -313,6 +313,50 @@ def penalty_vectors():
     return out
 
 
+FULL_SIZE_PROMPT_SEED = 21
+
+
+def full_size_inputs():
+    """Seeded inputs of the 1.2B-size cases; tests rebuild them from here (numpy only)."""
+    cfg = synthetic.lfm25_1p2b_config()
+    prompts = synthetic.uniform_prompts(8, 64, 256, cfg.vocab_size, seed=FULL_SIZE_PROMPT_SEED)
+    score_prompts = synthetic.uniform_prompts(6, 32, 128, cfg.vocab_size, seed=FULL_SIZE_PROMPT_SEED + 1)
+    completions = synthetic.uniform_prompts(6, 8, 24, cfg.vocab_size, seed=FULL_SIZE_PROMPT_SEED + 2)
+    long_prompt = synthetic.uniform_prompts(1, 9300, 9300, cfg.vocab_size, seed=FULL_SIZE_PROMPT_SEED + 3)[0]
+    return cfg, prompts, score_prompts, completions, long_prompt
+
+
+def full_size_vectors():
+    """The reference's eager CPU engine on the LFM2.5-1.2B architecture in bf16 (the benchmarked size):
+    greedy generation, completion scoring and the next-token logits of one 9300-token prompt (prefilled
+    in one piece; the engine under test chunks it). Weights: synthetic.make_state_dict_streams(seed 0).
+    Takes tens of minutes on a handful of cores."""
+    import time
+    from climbing_gym.inference.lfm25_engine import LFM25SamplingConfig, flatten_token_batches
+
+    cfg, prompts, score_prompts, completions, long_prompt = full_size_inputs()
+    state = synthetic.make_state_dict_streams(cfg, seed=0)
+    engine = ref_engine(None, cfg, state, torch.bfloat16, max_model_len=9344)
+    del state
+    out, t0 = {}, time.time()
+    got = engine.generate(*flatten_token_batches(prompts), repeats=1,
+                          sampling=LFM25SamplingConfig(temperature=0.0, max_new_tokens=32, ignore_eos=True))
+    out["generate_bf16"] = dict(token_ids=got.token_ids[:, 0].tolist(),
+                                logprobs=[[round(float(x), 6) for x in row] for row in got.logprobs[:, 0].tolist()])
+    print("generate", round(time.time() - t0, 1), flush=True)
+    scores = engine.score_completions(score_prompts, completions)
+    out["score_bf16"] = [[round(float(x), 6) for x in row] for row in scores]
+    print("score", round(time.time() - t0, 1), flush=True)
+    prefix = engine.prefill(*flatten_token_batches([long_prompt]))
+    logits = prefix.next_token_logits.float()[0]
+    top = torch.topk(logits, 8)
+    out["long_prefill_bf16"] = dict(length=len(long_prompt), lse=round(float(torch.logsumexp(logits, -1)), 6),
+                                    top_ids=top.indices.tolist(), top_logits=[round(float(x), 6) for x in top.values],
+                                    every_256th=[round(float(x), 6) for x in logits[::256]])
+    print("long prefill", round(time.time() - t0, 1), flush=True)
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="the src/ directory of a reference checkout")
@@ -320,10 +364,10 @@ def main():
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
     jobs = dict(model=model_vectors, sampler=sampler_vectors, kernels=kernel_vectors, head=head_vectors,
-                penalty=penalty_vectors)
+                penalty=penalty_vectors, model_1p2b=full_size_vectors)
     for name, fn in jobs.items():
-        if args.only and name not in args.only.split(","):
-            continue
+        if (args.only and name not in args.only.split(",")) or (name == "model_1p2b" and not args.only):
+            continue  # the full-size vectors take tens of minutes: only on request (--only model_1p2b)
         payload = fn()
         (OUT / f"{name}.json").write_text(json.dumps(payload, separators=(",", ":")) + "\n")
         print("wrote", name)

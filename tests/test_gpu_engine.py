@@ -142,6 +142,21 @@ def test_generate_fp8_mlp_and_kv_within_tolerance(dev):
                       oracle["logprobs"][:, 0], atol=5e-2, min_identical=0.0)  # FP8: log-prob tolerance only
 
 
+def test_generate_fp8_lm_head_within_tolerance(dev):
+    """FP8 vocabulary head (with and without the FP8 MLP): the decode steps quantise the final norm's output
+    per row and run the head as an e4m3 GEMM; the first token still comes from the bf16 prefill head."""
+    for extra in ({}, {"fp8_mlp": True, "fp8_kv": True}):
+        engine = make_engine(dev, dtype=torch.bfloat16, fp8_lm_head=True, **extra)
+        out = engine.generate(*flat(PROMPTS, dev), repeats=1, sampling=LFM25SamplingConfig(temperature=0.0, max_new_tokens=16))
+        oracle = make_oracle("bf16", fp8_lm_head=True, **extra)
+        tokens = out.token_ids.cpu().numpy()[:, 0]
+        lengths = out.lengths.cpu().numpy()[:, 0]
+        trace = oracle.teacher_forced(PROMPTS, np.where(tokens < 0, 0, tokens))
+        logprobs = out.logprobs.cpu().numpy()[:, 0]
+        for row, n in enumerate(lengths):
+            assert np.abs(logprobs[row, :n] - trace["logprobs"][row, :n]).max() <= 5e-2, (extra, row)
+
+
 def test_sampled_generate_fp32_matches_oracle_draws(dev):
     engine = make_engine(dev, dtype=torch.float32)
     sampling = LFM25SamplingConfig(temperature=1.0, max_new_tokens=12, seed=1234, ignore_eos=True)

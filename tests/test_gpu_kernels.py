@@ -287,6 +287,34 @@ def test_paged_attention_matches_softmax_reference(dev, mode, impl, page, splits
 
 
 @pytest.mark.parametrize("mode", ["bf16", "e4m3"])
+@pytest.mark.parametrize("splits", [1, 4, 16])
+def test_paged_attention_long_contexts_with_splits(dev, mode, splits):
+    """The long-context decode shapes: 32 query / 8 KV heads, rows of 8 K - 12 K cached tokens next to short
+    ones (the deep page rings, many pages per warp, and the split / combine path with up to 16 splits)."""
+    rng = np.random.default_rng(17)
+    hq, hkv, d = 32, 8, 64
+    lens = [8192 + 17, 300, 12000, 9000, 64, 8192]
+    rows = len(lens)
+    cache = make_cache(dev, fp8=mode == "e4m3", slots=rows, max_len=12032, page=64, hkv=hkv, d=d, layers=1)
+    cache.reserve(torch.arange(rows, device=dev, dtype=torch.int32), torch.tensor(lens, device=dev, dtype=torch.int32))
+    stored = fill_cache(cache, lens, hkv, d, round_bf16, mode == "e4m3", rng)
+    q_np = round_bf16(rng.standard_normal((rows, hq, d)))
+    q = bf(q_np, dev)
+    out = torch.full((rows, hq, d), 7.0, device=dev, dtype=torch.bfloat16)
+    ws = torch.empty(rows * hq * splits * (d + 2), device=dev, dtype=torch.float32)
+    kv_lens = torch.tensor(lens, device=dev, dtype=torch.int32)
+    nv.call("cgym_paged_attention", nv.ptr(out), nv.ptr(q), nv.ptr(kv_lens), None, None, cache.kv, 0, rows, hq,
+            d ** -0.5, splits, nv.ptr(ws), nv.BF16, 2, nv.ptr(cache.status), stream())
+    got = f32(out)
+    assert int(cache.status.item()) == 0
+    for row, n in enumerate(lens):
+        k, v, ks, vs = stored[row]
+        want = attention_reference(q_np[row], k, v, d ** -0.5, ks, vs, round_bf16)
+        err = np.abs(got[row].reshape(hq, d) - want).max()
+        assert err <= 0.012, f"row {row} len {n} splits {splits}: {err}"
+
+
+@pytest.mark.parametrize("mode", ["bf16", "e4m3"])
 @pytest.mark.parametrize("hq,hkv", [(8, 2), (4, 4), (6, 2)])
 def test_prefill_attention_tensor_core_causal_with_prefix(dev, mode, hq, hkv):
     """Packed query tiles against the paged cache: a fresh prompt, a chunk continuing a cached prefix
@@ -460,6 +488,47 @@ def test_gemm_fp8_scaled_epilogue(dev, impl, shape):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     assert_gemm_close(f32(y), want, exact_fraction=0.97, what=f"fp8 gemm impl {impl}")
+
+
+# The decode step's own launches: the 1.2B model's projection shapes at the batch sizes that are benchmarked,
+# with the engine's workspace size (2 x 148 resident CTAs, one [token tile][128] fp32 partial tile each), so the
+# launcher takes the grids the step takes: cluster split-K up to 8 ways over an 8192-deep contraction, and two
+# 128-token tiles at 256 rows.
+DECODE_WS_BYTES = 2 * 148 * 128 * 128 * 4
+
+
+@pytest.mark.parametrize("shape", [(256, 2048, 8192), (256, 16384, 2048), (64, 2048, 8192), (128, 2048, 8192),
+                                   (17, 2048, 8192)])
+def test_gemm_fp8_at_decode_shapes_with_auto_split_k(dev, shape):
+    m, n, k = shape
+    rng = np.random.default_rng(m + n)
+    xq, xs = ok.quantize_rows(round_bf16(rng.standard_normal((m, k))))
+    wq, wsc = ok.quantize_rows(round_bf16(rng.standard_normal((n, k)) * 0.05))
+    want = ok.fp8_matmul(xq, xs, wq, wsc)
+    args = [torch.from_numpy(a).to(dev) for a in (xq, xs, wq, wsc)]
+    ws = torch.zeros(DECODE_WS_BYTES, device=dev, dtype=torch.uint8)
+    status = torch.zeros(1, device=dev, dtype=torch.int32)
+    runs = []
+    for _ in range(2):
+        y = torch.full((m, n), -3.0, device=dev, dtype=torch.bfloat16)
+        nv.call("cgym_gemm_fp8", nv.ptr(y), nv.ptr(args[0]), nv.ptr(args[1]), nv.ptr(args[2]), nv.ptr(args[3]), None,
+                m, n, k, 0, nv.ptr(ws), ws.numel(), nv.ptr(status), stream())
+        torch.cuda.synchronize()
+        runs.append(f32(y))
+    assert int(status.item()) == 0
+    assert np.array_equal(runs[0], runs[1]), "split-K must be deterministic"
+    assert_gemm_close(runs[0], want, exact_fraction=0.97, what=f"fp8 gemm {shape}")
+
+
+@pytest.mark.parametrize("shape", [(256, 2048, 2048), (256, 6144, 2048), (256, 3072, 2048), (64, 2048, 8192),
+                                   (256, 2048, 8192), (512, 2048, 2048)])
+def test_gemm_bf16_at_decode_shapes_with_auto_split_k(dev, shape):
+    m, n, k = shape
+    rng = np.random.default_rng(m + k)
+    x_np, w_np = round_bf16(rng.standard_normal((m, k))), round_bf16(rng.standard_normal((n, k)) * 0.05)
+    want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
+    y = gemm_call(dev, bf(x_np, dev), bf(w_np, dev), impl=0, ws_bytes=DECODE_WS_BYTES)
+    assert_gemm_close(f32(y), want, exact_fraction=0.97, what=f"bf16 gemm {shape}")
 
 
 # ------------------------------------------------------------------------------------------ sampler
