@@ -69,6 +69,9 @@ SIGNATURES = {
     "cgym_scatter_kv_dense": [_P, _P, C.POINTER(KVLayout), _I, _I, _I, _I, _P],
     "cgym_gemm": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_fp8": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
+    "cgym_gemm_scatter": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
+    "cgym_gemm_fp8_scatter": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
+    "cgym_step_begin_rows": [C.POINTER(PagePool), _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P],
     "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_sample": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_sample_static": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],

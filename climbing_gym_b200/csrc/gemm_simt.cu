@@ -22,7 +22,7 @@ template <typename TIN, typename TOUT>
 __global__ void __launch_bounds__(256)
 gemm_simt_kernel(TOUT* __restrict__ y, const TIN* __restrict__ x, const TIN* __restrict__ w,
                  const float* __restrict__ x_scales, const float* __restrict__ w_scales,
-                 const uint8_t* __restrict__ row_mask, int M, int N, int K) {
+                 const uint8_t* __restrict__ row_mask, const int32_t* __restrict__ row_map, int M, int N, int K) {
   __shared__ float xs[ST_BK][ST_BM + 1];
   __shared__ float ws[ST_BK][ST_BN + 1];
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
@@ -53,32 +53,35 @@ gemm_simt_kernel(TOUT* __restrict__ y, const TIN* __restrict__ x, const TIN* __r
   for (int i = 0; i < 4; ++i) {
     const int gm = m0 + ty * 4 + i;
     if (gm >= M || (row_mask != nullptr && !row_mask[gm])) continue;
+    const int out_row = row_map != nullptr ? row_map[gm] : gm;  // scattered output rows; negative: not written
+    if (out_row < 0) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
       float v = acc[i][j];
       if (x_scales != nullptr) v = __fmul_rn(__fmul_rn(v, x_scales[gm]), w_scales[gn]);
-      Elem<TOUT>::store(y + static_cast<int64_t>(gm) * N + gn, v);
+      Elem<TOUT>::store(y + static_cast<int64_t>(out_row) * N + gn, v);
     }
   }
 }
 
 int launch_gemm_simt(void* y, const void* x, const void* w, const float* x_scales, const float* w_scales,
-                     const uint8_t* row_mask, int M, int N, int K, int in_dtype, cudaStream_t stream) {
+                     const uint8_t* row_mask, const int32_t* row_map, int M, int N, int K, int in_dtype,
+                     cudaStream_t stream) {
   dim3 grid((N + ST_BN - 1) / ST_BN, (M + ST_BM - 1) / ST_BM);
   if (in_dtype == CGYM_F32)
     gemm_simt_kernel<float, float><<<grid, 256, 0, stream>>>(static_cast<float*>(y), static_cast<const float*>(x),
                                                              static_cast<const float*>(w), nullptr, nullptr,
-                                                             row_mask, M, N, K);
+                                                             row_mask, row_map, M, N, K);
   else if (in_dtype == CGYM_BF16)
     gemm_simt_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, stream>>>(
         static_cast<__nv_bfloat16*>(y), static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
-        nullptr, nullptr, row_mask, M, N, K);
+        nullptr, nullptr, row_mask, row_map, M, N, K);
   else if (in_dtype == CGYM_E4M3)
     gemm_simt_kernel<uint8_t, __nv_bfloat16><<<grid, 256, 0, stream>>>(
         static_cast<__nv_bfloat16*>(y), static_cast<const uint8_t*>(x), static_cast<const uint8_t*>(w), x_scales,
-        w_scales, row_mask, M, N, K);
+        w_scales, row_mask, row_map, M, N, K);
   else
     return fail("gemm: unsupported dtype %d", in_dtype);
   return check_launch("gemm_simt");

@@ -124,6 +124,7 @@ struct GemmEpilogue {
   const float* x_scales;   // per token, fp8 only
   const float* w_scales;   // per output feature, fp8 only
   const uint8_t* row_mask; // optional
+  const int32_t* row_map;  // optional: token row m is written to output row row_map[m] (negative: not written)
   int32_t* status;
   int M, N, K;
   int partial;             // 1: split-K over a cluster of gridDim.z CTAs
@@ -212,6 +213,8 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
     const int m = m0 + static_cast<int>(rank) + (quarter + 4 * i) * SPLITS;
     if (m >= ep.M) continue;
     if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
+    const int out_row = ep.row_map != nullptr ? ep.row_map[m] : m;
+    if (out_row < 0) continue;
     float total[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int sp = 0; sp < SPLITS; ++sp) {
@@ -225,7 +228,7 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
 #pragma unroll
       for (int j = 0; j < 4; ++j) total[j] = __fmul_rn(__fmul_rn(total[j], xs), ws[j]);
     }
-    __nv_bfloat16* dst = ep.y + static_cast<int64_t>(m) * ep.N + n;
+    __nv_bfloat16* dst = ep.y + static_cast<int64_t>(out_row) * ep.N + n;
     if (n + 3 < ep.N && (ep.N & 3) == 0) {
       uint2 packed;
       *reinterpret_cast<__nv_bfloat162*>(&packed.x) = __floats2bfloat162_rn(total[0], total[1]);
@@ -393,9 +396,11 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
             const int m = m0 + c * 32 + j;
             if (m >= ep.M) break;
             if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
+            const int out_row = ep.row_map != nullptr ? ep.row_map[m] : m;
+            if (out_row < 0) continue;
             float val = __uint_as_float(v[j]);
             if (ep.x_scales != nullptr) val = __fmul_rn(__fmul_rn(val, ep.x_scales[m]), ws);
-            ep.y[static_cast<int64_t>(m) * ep.N + n] = __float2bfloat16_rn(val);
+            ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
           }
         }
       }
@@ -538,8 +543,9 @@ bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const v
 }
 
 int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_scales, const float* w_scales,
-                        const uint8_t* row_mask, int M, int N, int K, bool fp8, void* workspace,
-                        int64_t workspace_bytes, int32_t* status, int force_splits, cudaStream_t stream) {
+                        const uint8_t* row_mask, const int32_t* row_map, int M, int N, int K, bool fp8,
+                        void* workspace, int64_t workspace_bytes, int32_t* status, int force_splits,
+                        cudaStream_t stream) {
   CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
                "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
   CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
@@ -616,8 +622,8 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   CUtensorMap mw, mx;
   if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
   if (int rc = make_map(&mx, x, M, K, un, fp8)) return rc;
-  GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, status, M, N, K, splits > 1 ? 1 : 0,
-                  split_ws};
+  GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, row_map, status, M, N, K,
+                  splits > 1 ? 1 : 0, split_ws};
   dim3 grid(dual ? n_tiles / 2 : n_tiles, m_tiles, splits);
 #ifdef CGYM_TRACE
   ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 8192ull : nullptr;

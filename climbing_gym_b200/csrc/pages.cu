@@ -39,31 +39,53 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* scra
   return scratch[warp] + inc - v;
 }
 
+// What a step over a compact set of rows (row e = slot slot_ids[e], -1 = padding) gathers per row from the
+// per-slot request state, next to the per-slot copy of the row mask that the sampler's bookkeeping reads.
+struct CompactRows {
+  const int64_t* input_tokens;  // [n_slots] next decode input per slot
+  int64_t* row_tokens;          // [rows]
+  int32_t* row_positions;       // [rows] seq_lens[slot]
+  uint8_t* slot_active;         // [n_state_slots] cleared, then 1 for the slots whose input is consumed this step
+  int n_state_slots;
+};
+
 // Entries e < n ask that slot_e can hold need_e tokens. One CTA.
 //   step mode   (need_tokens == nullptr): entry = batch row, need = seq_lens[slot] + 1 for active rows;
-//                also snapshots pending -> active_out when given.
+//                also snapshots pending -> active_out when given (pending is indexed by row, or by slot
+//                when `compact` is given).
 //   reserve mode: entry e = (slot_ids[e], need_tokens[e]).
 __global__ void __launch_bounds__(POOL_THREADS)
 pages_reserve_kernel(cgym_page_pool pool, const int32_t* __restrict__ slot_ids,
                      const int32_t* __restrict__ need_tokens, const int32_t* __restrict__ seq_lens,
                      const uint8_t* __restrict__ active, const uint8_t* __restrict__ pending_in,
                      uint8_t* __restrict__ active_out, int32_t* __restrict__ kv_lens_out, int n,
-                     int32_t* __restrict__ status) {
+                     int32_t* __restrict__ status, CompactRows compact = CompactRows{}) {
   __shared__ int s_excl[POOL_THREADS + 1];
   __shared__ int s_old[POOL_THREADS];
   __shared__ int s_slot[POOL_THREADS];
   __shared__ int scratch[33];
   const int e = threadIdx.x;
   int cnt = 0, slot = -1, old = 0;
+  if (compact.slot_active != nullptr) {
+    for (int i = e; i < compact.n_state_slots; i += POOL_THREADS) compact.slot_active[i] = 0;
+    __syncthreads();
+  }
   if (e < n) {
     bool act = true;
-    if (pending_in != nullptr) {
+    slot = slot_ids != nullptr ? slot_ids[e] : e;
+    const bool valid = slot >= 0 && slot < pool.n_slots;
+    if (compact.slot_active != nullptr) {
+      act = valid && pending_in[slot] != 0;
+      active_out[e] = act ? 1 : 0;
+      if (act) compact.slot_active[slot] = 1;
+      compact.row_tokens[e] = valid ? compact.input_tokens[slot] : 0;
+      compact.row_positions[e] = valid ? seq_lens[slot] : 0;
+    } else if (pending_in != nullptr) {
       act = pending_in[e] != 0;
       if (active_out != nullptr) active_out[e] = act ? 1 : 0;
     } else if (active != nullptr) {
       act = active[e] != 0;
     }
-    slot = slot_ids != nullptr ? slot_ids[e] : e;
     // attention length of the row this step: its cached tokens plus the one being appended
     if (kv_lens_out != nullptr) kv_lens_out[e] = (slot >= 0 && slot < pool.n_slots) ? seq_lens[slot] + 1 : 0;
     if (act && slot >= 0 && slot < pool.n_slots) {
@@ -258,6 +280,24 @@ extern "C" int cgym_step_begin(const cgym_page_pool* pool, const int32_t* seq_le
   pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, slots, nullptr, seq_lens, active, pending,
                                                                   active_out, kv_lens_out, rows, status);
   return check_launch("step_begin");
+}
+
+extern "C" int cgym_step_begin_rows(const cgym_page_pool* pool, const int32_t* seq_lens, const uint8_t* pending,
+                                    const int64_t* input_tokens, const int32_t* slots, uint8_t* row_active_out,
+                                    uint8_t* slot_active_out, int64_t* row_tokens_out, int32_t* row_positions_out,
+                                    int32_t* kv_lens_out, int rows, int n_state_slots, int32_t* status,
+                                    cgym_stream_t stream) {
+  if (int rc = check_pool(pool)) return rc;
+  CGYM_REQUIRE(seq_lens && pending && input_tokens && slots && row_active_out && slot_active_out && row_tokens_out &&
+                   row_positions_out && kv_lens_out && status,
+               "step_begin_rows: every array is required");
+  CGYM_REQUIRE(rows >= 0 && rows <= POOL_THREADS, "step_begin_rows: at most 1024 rows per step");
+  CGYM_REQUIRE(n_state_slots >= 0 && n_state_slots <= pool->n_slots, "step_begin_rows: n_state_slots out of range");
+  if (rows == 0) return 0;
+  const CompactRows compact{input_tokens, row_tokens_out, row_positions_out, slot_active_out, n_state_slots};
+  pages_reserve_kernel<<<1, POOL_THREADS, 0, as_stream(stream)>>>(*pool, slots, nullptr, seq_lens, nullptr, pending,
+                                                                  row_active_out, kv_lens_out, rows, status, compact);
+  return check_launch("step_begin_rows");
 }
 
 extern "C" int cgym_pages_reserve(const cgym_page_pool* pool, const int32_t* slot_ids, const int32_t* need_tokens,

@@ -154,6 +154,25 @@ class _DecodeGraph:
     filtered: bool = False  # the step derives top-k / top-p thresholds before it samples
 
 
+@dataclass
+class _CompactGraph:
+    """A captured step over ``slots.numel()`` rows that stand for an arbitrary subset of a session's slots
+    (the reference's CompactDecodeGraph, src/climbing_gym/inference/lfm25_batching.py:73-120). The rows
+    reach the shared paged cache, conv taps and request state through ``slots``; nothing is copied."""
+
+    graph: object
+    slots: torch.Tensor          # int32 [rows], -1 = padding row
+    buffers: tuple               # row-indexed inputs the graph reads (kept alive with it)
+    mapped_slots: tuple = ()
+
+    def set_slots(self, slots) -> None:
+        mapping = tuple(slots)
+        if mapping != self.mapped_slots:
+            values = mapping + (-1,) * (self.slots.numel() - len(mapping))
+            self.slots.copy_(torch.tensor(values, dtype=torch.int32), non_blocking=False)
+            self.mapped_slots = mapping
+
+
 class B200Decoder:
     supported_conv_kernel_sizes = (3,)
 
@@ -288,10 +307,7 @@ class B200Decoder:
         if penalised:
             state.allocate_penalty()
         logits = torch.zeros((batch_size, engine.config.vocab_size), device=engine.device, dtype=engine.dtype)
-        splits = 1
-        if batch_size * engine.config.num_key_value_heads < 148:
-            splits = min(16, max(1, -(-148 // (batch_size * engine.config.num_key_value_heads))))
-        bufs = ForwardBuffers(engine.weights, batch_size, fp8=self.fp8_mlp or self.fp8_lm_head, attn_splits=splits)
+        bufs = self._forward_buffers(batch_size)
         entry = _DecodeGraph(cache, state.input_tokens, logits, None, state.active, state, bufs, filtered=filtered)
         # All rows are dead (alive = pending = 0) while warming up and capturing, so neither run
         # touches KV pages, conv taps, logits or bookkeeping.
@@ -320,8 +336,74 @@ class B200Decoder:
         self.graphs[key] = entry
         return entry
 
+    def _forward_buffers(self, rows: int) -> ForwardBuffers:
+        """Activation scratch of a step over ``rows`` rows; decode attention is split along the context
+        when rows x kv_heads alone would leave SMs idle."""
+        heads = self.engine.config.num_key_value_heads
+        splits = min(16, max(1, -(-148 // (rows * heads)))) if rows * heads < 148 else 1
+        return ForwardBuffers(self.engine.weights, rows, fp8=self.fp8_mlp or self.fp8_lm_head, attn_splits=splits)
+
     def _select_graph(self, entry, live_slots):
-        return entry.graph, entry.input_tokens.numel()
+        """The graph to replay for the live rows and its compute batch. With adaptive batching, the
+        smallest bucket 16 * 2^k that holds them (the reference's rule,
+        src/climbing_gym/inference/lfm25_cuda.py:194-209); every variant works on the same physical cache."""
+        maximum = entry.input_tokens.numel()
+        if not self.adaptive_batching or maximum <= 16:
+            return entry.graph, maximum
+        size = 16
+        while size < len(live_slots):
+            size *= 2
+        if size >= maximum:
+            return entry.graph, maximum
+        if size not in entry.compact_graphs:
+            entry.compact_graphs[size] = self._capture_compact(entry, size)
+        compact = entry.compact_graphs[size]
+        compact.set_slots(live_slots)
+        return compact.graph, size
+
+    def _compact_step(self, entry: _DecodeGraph, rows: int, slots, tokens, positions, active, kv_lens, bufs,
+                      *, sample: bool) -> None:
+        cache, state = entry.cache, entry.state
+        stream = nv.stream_ptr(self.engine.device)
+        nv.call("cgym_step_begin_rows", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(state.pending),
+                nv.ptr(state.input_tokens), nv.ptr(slots), nv.ptr(active), nv.ptr(state.active), nv.ptr(tokens),
+                nv.ptr(positions), nv.ptr(kv_lens), rows, cache.n_slots, nv.ptr(cache.status), stream)
+        self.runner.decode_step(bufs, cache, tokens, active, entry.logits, slots=slots, rows=rows, kv_lens=kv_lens,
+                                positions=positions, logits_rows=slots)
+        if sample:
+            self._sample(entry, nv.ptr(state.active), stream)
+
+    @torch.inference_mode()
+    def _capture_compact(self, entry: _DecodeGraph, rows: int) -> _CompactGraph:
+        """Capture a step over ``rows`` compacted rows without disturbing resident requests: while
+        warming up and capturing every row is a padding row (slot -1), so no KV page, conv tap or logits
+        row is written, and the warm-up leaves the sampler out (its bookkeeping would advance live rows)."""
+        engine, dev = self.engine, self.engine.device
+        slots = torch.full((rows,), -1, device=dev, dtype=torch.int32)
+        tokens = torch.zeros(rows, device=dev, dtype=torch.int64)
+        positions = torch.zeros(rows, device=dev, dtype=torch.int32)
+        active = torch.zeros(rows, device=dev, dtype=torch.uint8)
+        kv_lens = torch.zeros(rows, device=dev, dtype=torch.int32)
+        bufs = self._forward_buffers(rows)
+        stream, current = self._capture_stream, torch.cuda.current_stream(dev)
+        stream.wait_stream(current)
+        lib = nv.load()
+        previous_pdl = lib.cgym_set_pdl(1 if self.use_pdl else 0)
+        try:
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    self._compact_step(entry, rows, slots, tokens, positions, active, kv_lens, bufs, sample=False)
+            current.wait_stream(stream)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            before = lib.cgym_launch_count()
+            with torch.cuda.graph(graph, stream=stream):
+                self._compact_step(entry, rows, slots, tokens, positions, active, kv_lens, bufs, sample=True)
+            current.wait_stream(stream)
+            step = _StepGraph(graph, int(lib.cgym_launch_count() - before))
+        finally:
+            lib.cgym_set_pdl(previous_pdl)
+        return _CompactGraph(step, slots, (tokens, positions, active, kv_lens, bufs))
 
     # ---- batch generate -------------------------------------------------------------------------------
     @torch.inference_mode()
@@ -385,10 +467,19 @@ class B200Decoder:
             start_event, end_event = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start_event.record()
         replays = 0
+        graph = entry.graph
         for step in range(1, sampling.max_new_tokens):
-            if not fixed_length and step % interval == 0 and not bool(state.alive.any().item()):
-                break
-            entry.graph.replay()
+            if not fixed_length and step % interval == 0:
+                if self.adaptive_batching:
+                    # rows that finished leave the compute batch: the live ones are compacted into the
+                    # smallest graph bucket that holds them (src/climbing_gym/inference/lfm25_cuda.py:350-357)
+                    live = torch.nonzero(state.alive).flatten().cpu().tolist()
+                    if not live:
+                        break
+                    graph, _ = self._select_graph(entry, live)
+                elif not bool(state.alive.any().item()):
+                    break
+            graph.replay()
             replays += 1
         if timing:
             end_event.record()

@@ -80,16 +80,17 @@ class LFM25Runner:
             packed.refresh()
 
     # ---- single kernels --------------------------------------------------------------------------
-    def _gemm(self, y, x, w, rows, bufs, status, row_mask=None):
+    def _gemm(self, y, x, w, rows, bufs, status, row_mask=None, row_map=None):
         n, k = w.shape
-        nv.call("cgym_gemm", nv.ptr(y), nv.ptr(x), nv.ptr(w), nv.ptr(row_mask), rows, n, k, self.dt, self.gemm_impl,
-                nv.ptr(bufs.gemm_ws), bufs.gemm_ws.numel(), nv.ptr(status), nv.stream_ptr(w.device))
+        nv.call("cgym_gemm_scatter", nv.ptr(y), nv.ptr(x), nv.ptr(w), nv.ptr(row_mask), nv.ptr(row_map), rows, n, k,
+                self.dt, self.gemm_impl, nv.ptr(bufs.gemm_ws), bufs.gemm_ws.numel(), nv.ptr(status),
+                nv.stream_ptr(w.device))
 
-    def _gemm_fp8(self, y, xq, xs, packed, rows, bufs, status, row_mask=None):
+    def _gemm_fp8(self, y, xq, xs, packed, rows, bufs, status, row_mask=None, row_map=None):
         n, k = packed.values.shape
-        nv.call("cgym_gemm_fp8", nv.ptr(y), nv.ptr(xq), nv.ptr(xs), nv.ptr(packed.values), nv.ptr(packed.scales),
-                nv.ptr(row_mask), rows, n, k, self.gemm_impl, nv.ptr(bufs.gemm_ws), bufs.gemm_ws.numel(),
-                nv.ptr(status), nv.stream_ptr(y.device))
+        nv.call("cgym_gemm_fp8_scatter", nv.ptr(y), nv.ptr(xq), nv.ptr(xs), nv.ptr(packed.values),
+                nv.ptr(packed.scales), nv.ptr(row_mask), nv.ptr(row_map), rows, n, k, self.gemm_impl,
+                nv.ptr(bufs.gemm_ws), bufs.gemm_ws.numel(), nv.ptr(status), nv.stream_ptr(y.device))
 
     def _rmsnorm(self, y, x, w, rows, residual=None, sum_out=None):
         nv.call("cgym_rmsnorm", nv.ptr(y), nv.ptr(sum_out), nv.ptr(x), nv.ptr(residual), nv.ptr(w), rows,
@@ -170,24 +171,28 @@ class LFM25Runner:
         nv.call("cgym_embedding", nv.ptr(bufs.embed), nv.ptr(self.weights.embed_tokens), nv.ptr(tokens), rows,
                 cfg.hidden_size, cfg.vocab_size, self.dt, nv.stream_ptr(self.weights.device))
 
-    def _head(self, bufs, logits, hidden_rows, rows, status, row_mask=None):
+    def _head(self, bufs, logits, hidden_rows, rows, status, row_mask=None, row_map=None):
         if self.fp8_lm_head:
             packed = self.fp8_weights[id(self.weights.lm_head_weight)]
-            self._gemm_fp8(logits, bufs.normed_q, bufs.normed_s, packed, rows, bufs, status, row_mask)
+            self._gemm_fp8(logits, bufs.normed_q, bufs.normed_s, packed, rows, bufs, status, row_mask, row_map)
         else:
-            self._gemm(logits, hidden_rows, self.weights.lm_head_weight, rows, bufs, status, row_mask)
+            self._gemm(logits, hidden_rows, self.weights.lm_head_weight, rows, bufs, status, row_mask, row_map)
 
     # ---- public sequences ------------------------------------------------------------------------------
     def decode_step(self, bufs: ForwardBuffers, cache: PagedHybridCache, tokens, active, logits, *, slots=None,
-                    rows: int | None = None, kv_lens=None) -> None:
+                    rows: int | None = None, kv_lens=None, positions=None, logits_rows=None) -> None:
         """One token per row. Rows with active == 0 leave KV, conv taps and their logits row untouched.
-        positions are the slots' current seq_lens; the caller advances seq_lens afterwards.
+        positions are the slots' current seq_lens (pass them when the caller already holds them per row, e.g.
+        a contiguous range of slots); the caller advances seq_lens afterwards.
         kv_lens: the per-row attention lengths cgym_step_begin wrote (seq_lens + 1); computed here with
-        a torch op when the caller did not ask step_begin for them."""
+        a torch op when the caller did not ask step_begin for them.
+        logits_rows (int32 per row, optional): row r's logits go to logits[logits_rows[r]] (negative: nowhere);
+        a step over a compacted set of rows writes each row's logits into its slot's row this way."""
         rows = tokens.numel() if rows is None else rows
         self._embed(bufs, tokens, rows)
         # a decode row at cache length L writes position L and then attends to L + 1 tokens
-        positions = cache.seq_lens if slots is None else bufs_positions(cache, slots)
+        if positions is None:
+            positions = cache.seq_lens if slots is None else bufs_positions(cache, slots)
         if kv_lens is None:
             kv_lens = self._kv_lens_plus_one(cache, positions)
         x, residual = self._layers(bufs, cache, rows, decode=True, positions=positions, slots=slots, active=active,
@@ -196,7 +201,7 @@ class LFM25Runner:
             self._rmsnorm_quant(bufs.normed_q, bufs.normed_s, x, self.weights.embedding_norm_weight, rows, residual, bufs.residual)
         else:
             self._rmsnorm(bufs.final, x, self.weights.embedding_norm_weight, rows, residual, bufs.residual)
-        self._head(bufs, logits, bufs.final, rows, cache.status, row_mask=active)
+        self._head(bufs, logits, bufs.final, rows, cache.status, row_mask=active, row_map=logits_rows)
 
     @staticmethod
     def kv_lens_buffer(cache) -> torch.Tensor:

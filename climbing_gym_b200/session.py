@@ -416,6 +416,12 @@ class LFM25GenerationSession:
             self.stats["appended_tokens"] += len(prompt) - len(handle.prefix_token_ids) + 1
             self.stats["resumed_requests"] += 1
 
+    def _select_graph(self, live):
+        captures = len(self.entry.compact_graphs)
+        graph, size = self.decoder._select_graph(self.entry, live)
+        self.stats["adaptive_graph_captures"] += len(self.entry.compact_graphs) - captures
+        return graph, size
+
     @torch.inference_mode()
     def poll(self, *, steps: int | None = None) -> list[LFM25SessionResult]:
         self._check_open()
@@ -425,7 +431,7 @@ class LFM25GenerationSession:
         live = [i for i, r in enumerate(self.requests) if r is not None and not r.delivered]
         if not live:
             return []
-        graph, batch = self.decoder._select_graph(self.entry, live)
+        graph, batch = self._select_graph(live)
         with self._timed("decode"):
             for _ in range(steps):
                 graph.replay()

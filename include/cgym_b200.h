@@ -174,11 +174,26 @@ int cgym_gemm(void* y, const void* x, const void* w, const uint8_t* row_mask, in
               int dtype, int impl, void* workspace, int64_t workspace_bytes, int32_t* status,
               cgym_stream_t stream);
 
+/* cgym_gemm whose output rows are scattered: token row m is written to y row row_map[m] (int32[M]; negative =
+ * not written; NULL = cgym_gemm). Replaces the compact decode graphs' _scatter_logits copy
+ * (lfm25_batching.py:25-33, 96-101): the LM head of a step over a compacted set of rows writes each row's
+ * logits straight into its slot's row of the session-wide logits buffer. */
+int cgym_gemm_scatter(void* y, const void* x, const void* w, const uint8_t* row_mask, const int32_t* row_map,
+                      int M, int N, int K, int dtype, int impl, void* workspace, int64_t workspace_bytes,
+                      int32_t* status, cgym_stream_t stream);
+
 /* _matmul (+_reduce_split) / PackedFP8Weight.linear_quantized (lfm25_fp8.py:76-168):
  * y = bf16((xq . wq^T) * x_scales[m] * w_scales[n]). */
 int cgym_gemm_fp8(void* y, const uint8_t* xq, const float* x_scales, const uint8_t* wq,
                   const float* w_scales, const uint8_t* row_mask, int M, int N, int K, int impl,
                   void* workspace, int64_t workspace_bytes, int32_t* status, cgym_stream_t stream);
+
+/* cgym_gemm_fp8 with scattered output rows, for an FP8 LM head in a compact decode graph (see
+ * cgym_gemm_scatter; lfm25_batching.py:25-33, lfm25_cuda.py:190-191). */
+int cgym_gemm_fp8_scatter(void* y, const uint8_t* xq, const float* x_scales, const uint8_t* wq,
+                          const float* w_scales, const uint8_t* row_mask, const int32_t* row_map, int M, int N,
+                          int K, int impl, void* workspace, int64_t workspace_bytes, int32_t* status,
+                          cgym_stream_t stream);
 
 /* Per-slot request state of the slot scheduler (LFM25GenerationSession's row tensors,
  * lfm25_session.py:147-167). All arrays are indexed by slot. */
@@ -309,6 +324,18 @@ typedef struct {
 int cgym_step_begin(const cgym_page_pool* pool, const int32_t* seq_lens, const uint8_t* pending,
                     uint8_t* active_out, const uint8_t* active, const int32_t* slots,
                     int32_t* kv_lens_out, int rows, int32_t* status, cgym_stream_t stream);
+
+/* Start of a decode step over a COMPACT set of rows (adaptive batching: _gather_inputs and the slot
+ * indirection of capture_compact, lfm25_batching.py:11-23, 88-101). Row e stands for slot slots[e] (-1 =
+ * padding row). Per row: row_active_out[e] = pending[slot] (pending is indexed by SLOT here),
+ * row_tokens_out[e] = input_tokens[slot], row_positions_out[e] = seq_lens[slot], kv_lens_out[e] =
+ * seq_lens[slot] + 1; padding rows get 0. slot_active_out (uint8[n_state_slots]) is cleared and then set for
+ * the slots whose input is consumed this step: it is the `advance` mask cgym_sample_record wants, which stays
+ * indexed by slot. Pages are allocated for active rows as in cgym_step_begin. At most 1024 rows. */
+int cgym_step_begin_rows(const cgym_page_pool* pool, const int32_t* seq_lens, const uint8_t* pending,
+                         const int64_t* input_tokens, const int32_t* slots, uint8_t* row_active_out,
+                         uint8_t* slot_active_out, int64_t* row_tokens_out, int32_t* row_positions_out,
+                         int32_t* kv_lens_out, int rows, int n_state_slots, int32_t* status, cgym_stream_t stream);
 
 /* Reserve pages so slot s can hold need_tokens[s] tokens (admission / prefill chunk).
  * No reference counterpart (the reference allocates slots x capacity up front). */
