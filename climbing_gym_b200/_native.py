@@ -47,7 +47,17 @@ class SlotState(C.Structure):
                 ("stop_offsets", C.c_void_p), ("stop_table", C.c_void_p), ("ignore_eos", C.c_void_p),
                 ("rng_positions", C.c_void_p), ("seeds", C.c_void_p), ("temperatures", C.c_void_p),
                 ("rng_offsets", C.c_void_p), ("force_eos_at", C.c_void_p), ("seq_lens", C.c_void_p),
-                ("min_logits", C.c_void_p), ("capacity", C.c_int32), ("eos_token_id", C.c_int32)]
+                ("min_logits", C.c_void_p), ("out_rows", C.c_void_p), ("capacity", C.c_int32),
+                ("eos_token_id", C.c_int32)]
+
+
+class AdmitQueue(C.Structure):
+    _fields_ = [("rows", C.c_void_p), ("requests", C.c_void_p), ("limits", C.c_void_p), ("seeds", C.c_void_p),
+                ("temperatures", C.c_void_p), ("ignore_eos", C.c_void_p), ("stop_offsets", C.c_void_p),
+                ("logits", C.c_void_p), ("head", C.c_void_p), ("tail", C.c_void_p), ("capacity", C.c_int32),
+                ("result_capacity", C.c_int32), ("result_lengths", C.c_void_p), ("result_reasons", C.c_void_p),
+                ("slot_requests", C.c_void_p), ("out_rows", C.c_void_p), ("adopt_rows", C.c_void_p),
+                ("adopt_entries", C.c_void_p), ("release_mask", C.c_void_p)]
 
 
 _P, _I, _F, _L = C.c_void_p, C.c_int, C.c_float, C.c_int64
@@ -71,6 +81,8 @@ SIGNATURES = {
     "cgym_gemm_fp8": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_scatter": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_fp8_scatter": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
+    "cgym_slot_turnover": [C.POINTER(PagePool), _I, C.POINTER(SlotState), C.POINTER(AdmitQueue), _P, _P, _P, _I, _I, _I,
+                           _I, _P],
     "cgym_step_begin_rows": [C.POINTER(PagePool), _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P],
     "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_sample": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P],

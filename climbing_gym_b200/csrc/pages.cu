@@ -257,6 +257,99 @@ __global__ void scatter_kv_dense_kernel(const float* __restrict__ k, const float
   }
 }
 
+// ---- slot turnover: eviction of finished requests and admission from a device-resident queue -------------
+// Runs at the start of a decode step, inside the captured graph. Three kernels:
+//   1. slot_turnover_kernel (one CTA): publishes the length / finish reason of every finished request under
+//      its request id, marks its slot for eviction, and deals the queue's pending entries to the free slots
+//      (free now or just finished) in ascending slot order, entry order first-in first-out. An adopted
+//      slot's request state is re-armed from the entry. Everything is a pure function of the state it
+//      reads, so the schedule is reproducible.
+//   2. pages_release_kernel: the evicted slots' pages go back to the pool.
+//   3. slot_adopt_kernel: an adopting slot takes over the parked row's block table (a move: no reference
+//      count changes, no KV copy), its length, conv taps and next-token logits; the parked row is left empty.
+__global__ void __launch_bounds__(POOL_THREADS)
+slot_turnover_kernel(cgym_slot_state st, cgym_admit_queue q, int n_slots) {
+  __shared__ int scratch[33];
+  const int s = threadIdx.x;
+  int is_free = 0, finished = 0;
+  if (s < n_slots) {
+    const int rid = q.slot_requests[s];
+    finished = rid >= 0 && st.reasons[s] != 0;
+    if (finished) {
+      const int slot_of_result = rid % q.result_capacity;
+      q.result_lengths[slot_of_result] = st.lengths[s];
+      q.result_reasons[slot_of_result] = st.reasons[s];
+    }
+    is_free = rid < 0 || finished;
+  }
+  int total_free = 0;
+  const int rank = block_exclusive_scan(is_free, &total_free, scratch);
+  const int head = *q.head, available = *q.tail - head;
+  if (s < n_slots) {
+    int adopt_row = -1, adopt_entry = -1;
+    if (is_free && rank < available) {
+      adopt_entry = (head + rank) % q.capacity;
+      adopt_row = q.rows[adopt_entry];
+      const int rid = q.requests[adopt_entry];
+      q.slot_requests[s] = rid;
+      q.out_rows[s] = rid % q.result_capacity;
+      st.lengths[s] = 0;
+      st.reasons[s] = 0;
+      st.alive[s] = 1;
+      st.pending[s] = 0;
+      st.stop_states[s] = 0;
+      st.rng_positions[s] = 0;
+      st.limits[s] = q.limits[adopt_entry];
+      st.ignore_eos[s] = q.ignore_eos[adopt_entry];
+      st.stop_offsets[s] = q.stop_offsets[adopt_entry];
+      // armed by the scheduler, read-only for the sampler: the same device arrays, written here
+      const_cast<int64_t*>(st.seeds)[s] = q.seeds[adopt_entry];
+      const_cast<float*>(st.temperatures)[s] = q.temperatures[adopt_entry];
+      const_cast<int64_t*>(st.rng_offsets)[s] = 0;
+    } else if (finished) {
+      q.slot_requests[s] = -1;
+      st.reasons[s] = 0;  // published above; the slot is free and must not be published again
+      st.alive[s] = 0;
+      st.pending[s] = 0;
+    }
+    q.adopt_rows[s] = adopt_row;
+    q.adopt_entries[s] = adopt_entry;
+    q.release_mask[s] = finished ? 1 : 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *q.head = head + min(total_free, max(available, 0));
+}
+
+template <typename T>
+__global__ void slot_adopt_kernel(cgym_page_pool pool, cgym_admit_queue q, int32_t* __restrict__ row_lens,
+                                  T* __restrict__ logits, T* __restrict__ conv_state, int n_conv_layers, int n_rows,
+                                  int hidden, int vocab) {
+  const int s = blockIdx.x;
+  const int row = q.adopt_rows[s];
+  if (row < 0) return;
+  const int entry = q.adopt_entries[s];
+  for (int b = threadIdx.x; b < pool.max_blocks; b += blockDim.x) {
+    int32_t* from = pool.block_table + static_cast<int64_t>(row) * pool.max_blocks + b;
+    pool.block_table[static_cast<int64_t>(s) * pool.max_blocks + b] = *from;
+    *from = -1;
+  }
+  const T* src_logits = static_cast<const T*>(q.logits) + static_cast<int64_t>(entry) * vocab;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) logits[static_cast<int64_t>(s) * vocab + i] = src_logits[i];
+  const int taps = 3 * hidden;
+  for (int layer = 0; layer < n_conv_layers; ++layer) {
+    const T* from = conv_state + (static_cast<int64_t>(layer) * n_rows + row) * taps;
+    T* to = conv_state + (static_cast<int64_t>(layer) * n_rows + s) * taps;
+    for (int i = threadIdx.x; i < taps; i += blockDim.x) to[i] = from[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    pool.n_blocks[s] = pool.n_blocks[row];
+    pool.n_blocks[row] = 0;
+    row_lens[s] = row_lens[row];
+    row_lens[row] = 0;
+  }
+}
+
 static int check_pool(const cgym_page_pool* pool) {
   CGYM_REQUIRE(pool != nullptr && pool->free_bitmap && pool->refcount && pool->block_table && pool->n_blocks,
                "page pool is incomplete");
@@ -320,6 +413,36 @@ extern "C" int cgym_pages_release(const cgym_page_pool* pool, const uint8_t* rel
   CGYM_REQUIRE(release_mask != nullptr, "pages_release: mask is required");
   pages_release_kernel<<<pool->n_slots, 128, 0, as_stream(stream)>>>(*pool, release_mask, seq_lens);
   return check_launch("pages_release");
+}
+
+extern "C" int cgym_slot_turnover(const cgym_page_pool* pool_rows, int n_slots, const cgym_slot_state* state,
+                                  const cgym_admit_queue* queue, void* logits, void* conv_state, int32_t* row_lens,
+                                  int n_conv_layers, int hidden, int vocab, int dtype, cgym_stream_t stream) {
+  if (int rc = check_pool(pool_rows)) return rc;
+  CGYM_REQUIRE(state && queue && logits && conv_state && row_lens, "slot_turnover: missing argument");
+  CGYM_REQUIRE(n_slots > 0 && n_slots <= POOL_THREADS && n_slots <= pool_rows->n_slots,
+               "slot_turnover: n_slots must be in [1, 1024] and within the pool's rows");
+  CGYM_REQUIRE(queue->capacity > 0 && queue->result_capacity > 0 && queue->rows && queue->requests && queue->head &&
+                   queue->tail && queue->slot_requests && queue->out_rows && queue->adopt_rows &&
+                   queue->adopt_entries && queue->release_mask && queue->result_lengths && queue->result_reasons,
+               "slot_turnover: the admission queue is incomplete");
+  const cudaStream_t cs = as_stream(stream);
+  slot_turnover_kernel<<<1, POOL_THREADS, 0, cs>>>(*state, *queue, n_slots);
+  cgym_page_pool slots_view = *pool_rows;  // eviction walks the decode slots only
+  slots_view.n_slots = n_slots;
+  pages_release_kernel<<<n_slots, 128, 0, cs>>>(slots_view, queue->release_mask, row_lens);
+  const int n_rows = pool_rows->n_slots;
+  if (dtype == CGYM_F32)
+    slot_adopt_kernel<float><<<n_slots, 256, 0, cs>>>(*pool_rows, *queue, row_lens, static_cast<float*>(logits),
+                                                      static_cast<float*>(conv_state), n_conv_layers, n_rows, hidden,
+                                                      vocab);
+  else if (dtype == CGYM_BF16)
+    slot_adopt_kernel<__nv_bfloat16><<<n_slots, 256, 0, cs>>>(
+        *pool_rows, *queue, row_lens, static_cast<__nv_bfloat16*>(logits), static_cast<__nv_bfloat16*>(conv_state),
+        n_conv_layers, n_rows, hidden, vocab);
+  else
+    return fail("slot_turnover: unsupported dtype %d", dtype);
+  return check_launch("slot_turnover", 3);
 }
 
 extern "C" int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout* kv, int n_layers,

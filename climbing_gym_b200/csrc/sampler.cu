@@ -208,8 +208,10 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
 
   // bookkeeping of the slot scheduler: EOS beats the stop table beats the length limit
   if (length < st.capacity) {
-    st.tokens[static_cast<int64_t>(row) * st.capacity + length] = token;
-    st.logprobs[static_cast<int64_t>(row) * st.capacity + length] = logp;
+    // a slot's tokens go to its own arena row, or to the row its request was given (device-side slot turnover)
+    const int64_t out_row = st.out_rows != nullptr ? st.out_rows[row] : row;
+    st.tokens[out_row * st.capacity + length] = token;
+    st.logprobs[out_row * st.capacity + length] = logp;
   }
   int32_t value = 0;
   if (st.stop_table != nullptr) {

@@ -59,18 +59,59 @@ class SlotState:
         self.top_k, self.top_p = rows(torch.int32), rows(torch.float32, 1.0)
         self.min_logits = rows(torch.float32, float("-inf"))
 
+        self.eos = eos
+        self.queue = None  # device-resident admission queue (allocate_queue)
+        self._build_structs()
+        self.head_k, self.head_ids, self.head_logprobs = 0, None, None
+        self.penalties, self.seen, self.penalised = None, None, None
+
+    def _build_structs(self) -> None:
+        out_rows = self.queue["out_rows"] if self.queue is not None else None
+
         def struct(min_logits):
             return nv.SlotState(
                 nv.ptr(self.tokens), nv.ptr(self.logprobs), nv.ptr(self.lengths), nv.ptr(self.limits),
                 nv.ptr(self.reasons), nv.ptr(self.alive), nv.ptr(self.pending), nv.ptr(self.input_tokens),
                 nv.ptr(self.stop_states), nv.ptr(self.stop_offsets), nv.ptr(self.stop_table), nv.ptr(self.ignore_eos),
                 nv.ptr(self.rng_positions), nv.ptr(self.seeds), nv.ptr(self.temperatures), nv.ptr(self.rng_offsets),
-                nv.ptr(self.force_eos_at), nv.ptr(seq_lens), nv.ptr(min_logits), capacity, eos)
+                nv.ptr(self.force_eos_at), nv.ptr(self.seq_lens), nv.ptr(min_logits), nv.ptr(out_rows), self.capacity,
+                self.eos)
 
         self.struct = struct(None)                      # full-support sampling
         self.struct_filtered = struct(self.min_logits)  # draws restricted to logits >= min_logits[slot]
-        self.head_k, self.head_ids, self.head_logprobs = 0, None, None
-        self.penalties, self.seen, self.penalised = None, None, None
+
+    def allocate_queue(self, queue_capacity: int, result_capacity: int, n_rows: int, logits_dtype) -> None:
+        """Device-resident admission queue and per-request result rows (cgym_admit_queue): parked prompts wait
+        in ``queue_capacity`` entries, and a request's tokens / log-probs live in row ``request id %
+        result_capacity`` of the arenas from its admission until the host has read them, whichever slot ran it."""
+        dev, n = self.lengths.device, self.n_slots
+        self.tokens = torch.zeros((result_capacity, self.capacity), device=dev, dtype=torch.int64)
+        self.logprobs = torch.zeros((result_capacity, self.capacity), device=dev, dtype=torch.float32)
+
+        def entries(dtype, value=0):
+            return torch.full((queue_capacity,), value, device=dev, dtype=dtype)
+
+        q = dict(rows=entries(torch.int32, -1), requests=entries(torch.int32, -1), limits=entries(torch.int32),
+                 seeds=entries(torch.int64), temperatures=entries(torch.float32), ignore_eos=entries(torch.uint8),
+                 stop_offsets=entries(torch.int64),
+                 logits=torch.zeros((queue_capacity, self.vocab), device=dev, dtype=logits_dtype),
+                 head=torch.zeros(1, device=dev, dtype=torch.int32), tail=torch.zeros(1, device=dev, dtype=torch.int32),
+                 result_lengths=torch.zeros(result_capacity, device=dev, dtype=torch.int32),
+                 result_reasons=torch.zeros(result_capacity, device=dev, dtype=torch.int8),
+                 slot_requests=torch.full((n,), -1, device=dev, dtype=torch.int32),
+                 out_rows=torch.zeros(n, device=dev, dtype=torch.int32),
+                 adopt_rows=torch.full((n,), -1, device=dev, dtype=torch.int32),
+                 adopt_entries=torch.full((n,), -1, device=dev, dtype=torch.int32),
+                 release_mask=torch.zeros(n_rows, device=dev, dtype=torch.uint8))
+        q["capacity"], q["result_capacity"] = queue_capacity, result_capacity
+        self.queue = q
+        self.queue_struct = nv.AdmitQueue(
+            nv.ptr(q["rows"]), nv.ptr(q["requests"]), nv.ptr(q["limits"]), nv.ptr(q["seeds"]), nv.ptr(q["temperatures"]),
+            nv.ptr(q["ignore_eos"]), nv.ptr(q["stop_offsets"]), nv.ptr(q["logits"]), nv.ptr(q["head"]), nv.ptr(q["tail"]),
+            queue_capacity, result_capacity, nv.ptr(q["result_lengths"]), nv.ptr(q["result_reasons"]),
+            nv.ptr(q["slot_requests"]), nv.ptr(q["out_rows"]), nv.ptr(q["adopt_rows"]), nv.ptr(q["adopt_entries"]),
+            nv.ptr(q["release_mask"]))
+        self._build_structs()
 
     def allocate_penalty(self) -> None:
         """Repetition-penalty buffers: per-slot factor, one seen byte per (slot, token) and the penalised
@@ -95,6 +136,11 @@ class SlotState:
             t.zero_()
         self.force_eos_at.fill_(-1)
         self.stop_table_used = self.vocab
+        if self.queue is not None:
+            for name in ("head", "tail", "result_lengths", "result_reasons", "out_rows", "release_mask"):
+                self.queue[name].zero_()
+            for name in ("rows", "requests", "slot_requests", "adopt_rows", "adopt_entries"):
+                self.queue[name].fill_(-1)
         if self.head_k:
             self.head_ids.zero_()
             self.head_logprobs.zero_()
@@ -247,10 +293,19 @@ class B200Decoder:
         n = cache.n_slots
         stream = nv.stream_ptr(self.engine.device)
         kv_lens = self.runner.kv_lens_buffer(cache)
+        if state.queue is not None:
+            self._turnover(entry)
         nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(state.pending), nv.ptr(state.active),
                 None, None, nv.ptr(kv_lens), n, nv.ptr(cache.status), stream)
         self.runner.decode_step(entry.bufs, cache, state.input_tokens, state.active, entry.logits, kv_lens=kv_lens)
         self._sample(entry, nv.ptr(state.active), stream)
+
+    def _turnover(self, entry: _DecodeGraph) -> None:
+        """Evict finished requests and admit parked ones, on the device (cgym_slot_turnover)."""
+        cache, state, cfg = entry.cache, entry.state, self.engine.config
+        nv.call("cgym_slot_turnover", cache.pool_rows, cache.n_slots, C.byref(state.struct), C.byref(state.queue_struct),
+                nv.ptr(entry.logits), nv.ptr(cache.conv_state), nv.ptr(cache.row_lens), cache.n_conv_layers,
+                cfg.hidden_size, cfg.vocab_size, nv.dtype_code(entry.logits.dtype), nv.stream_ptr(self.engine.device))
 
     def _sample(self, entry: _DecodeGraph, advance, stream) -> None:
         """Sampler + bookkeeping of one step; filtered entries first turn each row's top-k / top-p into
@@ -279,7 +334,8 @@ class B200Decoder:
 
     @torch.inference_mode()
     def _get_graph(self, batch_size: int, cache_len: int, *, masked: bool = False, filtered: bool = False,
-                   head_k: int = 0, head_positions: int = 0, penalised: bool = False) -> _DecodeGraph:
+                   head_k: int = 0, head_positions: int = 0, penalised: bool = False,
+                   queue_capacity: int = 0) -> _DecodeGraph:
         engine = self.engine
         alignment = 32 if batch_size >= 64 else 128
         alignment = max(alignment, self.page_size)
@@ -288,6 +344,7 @@ class B200Decoder:
         key = (batch_size, capacity, masked) + (("filtered",) if filtered else ())
         key += (f"head{head_k}x{head_positions}",) if head_k else ()
         key += ("penalised",) if penalised else ()
+        key += (f"queue{queue_capacity}",) if queue_capacity else ()
         if key in self.graphs:
             self.graphs.move_to_end(key)
             return self.graphs[key]
@@ -295,10 +352,12 @@ class B200Decoder:
             self.graphs.popitem(last=False)
         self.runner.prepare_fp8()
         spare, n_pages = (self.snapshot_rows if masked else 0), None
+        spare += queue_capacity  # one parked row per queue entry
         if spare:
             blocks = -(-capacity // self.page_size)
             reserve = self.snapshot_pages if self.snapshot_pages is not None else 8 * blocks + spare
-            n_pages = batch_size * blocks + reserve
+            # parked prompts hold pages of their own until a slot adopts them
+            n_pages = batch_size * blocks + reserve + queue_capacity * blocks
         cache = engine._empty_cache(max_slots=batch_size, max_seq_len=capacity, fp8_kv=self.fp8_kv,
                                     page_size=self.page_size, n_pages=n_pages, spare_rows=spare)
         state = SlotState(batch_size, capacity, engine.config.vocab_size, int(engine.config.eos_token_id), cache.seq_lens)
@@ -306,6 +365,10 @@ class B200Decoder:
             state.allocate_heads(head_k, head_positions)
         if penalised:
             state.allocate_penalty()
+        if queue_capacity:
+            # results stay addressable until the host has read them: room for every request that can be
+            # parked or running at once, twice over (finished requests wait for the next poll)
+            state.allocate_queue(queue_capacity, 2 * (batch_size + queue_capacity), cache.n_rows, engine.dtype)
         logits = torch.zeros((batch_size, engine.config.vocab_size), device=engine.device, dtype=engine.dtype)
         bufs = self._forward_buffers(batch_size)
         entry = _DecodeGraph(cache, state.input_tokens, logits, None, state.active, state, bufs, filtered=filtered)

@@ -168,13 +168,17 @@ class LFM25Engine:
         return self._cuda_decoder
 
     def generation_session(self, *, max_batch_size: int, max_new_tokens: int, cache_len: int | None = None,
-                           behavior_topk: int = 0, profile_timings: bool = False):
+                           behavior_topk: int = 0, profile_timings: bool = False, queue_capacity: int = 0):
+        """``queue_capacity`` > 0 opens the session with a device-side admission queue of that many parked
+        prompts (``session.enqueue``): finished requests are then evicted and queued ones admitted inside the
+        decode graph, without a host round-trip between polls."""
         if self._cuda_decoder is None:
             raise RuntimeError("generation_session requires enable_cuda_graphs()")
         from .session import LFM25GenerationSession
 
         return LFM25GenerationSession(self._cuda_decoder, max_batch_size=max_batch_size, max_new_tokens=max_new_tokens,
-                                      cache_len=cache_len, behavior_topk=behavior_topk, profile_timings=profile_timings)
+                                      cache_len=cache_len, behavior_topk=behavior_topk, profile_timings=profile_timings,
+                                      queue_capacity=queue_capacity)
 
     # ---- cache ------------------------------------------------------------------------------------------
     def _empty_cache(self, *, max_slots: int, max_seq_len: int, fp8_kv: bool = False, page_size: int = 64,

@@ -39,12 +39,13 @@ class LFM25ContinuationHandle:
 
 @dataclass(frozen=True, slots=True)
 class LFM25SessionResult:
-    handle: LFM25ContinuationHandle
+    handle: LFM25ContinuationHandle | None  # None: the request ran through the device-side queue (no continuation)
     prompt_token_ids: tuple
     token_ids: tuple
     logprobs: tuple | None
     finish_reason: int
     behavior_topk: BehaviorTopK | None = None
+    request_id: int | None = None  # set for requests submitted with ``enqueue``
 
 
 @dataclass(frozen=True, slots=True)
@@ -80,7 +81,7 @@ class _Request:
 class LFM25GenerationSession:
     @torch.inference_mode()
     def __init__(self, decoder, *, max_batch_size: int, max_new_tokens: int, cache_len: int | None = None,
-                 behavior_topk: int = 0, profile_timings: bool = False):
+                 behavior_topk: int = 0, profile_timings: bool = False, queue_capacity: int = 0):
         if decoder._active_session is not None:
             raise RuntimeError("A native generation session is already open")
         if type(max_batch_size) is not int or max_batch_size <= 0:
@@ -92,8 +93,14 @@ class LFM25GenerationSession:
         if type(behavior_topk) is not int or not 0 <= behavior_topk <= min(128, self.engine.config.vocab_size):
             raise ValueError("behavior_topk must be an integer between 0 and min(vocab, 128)")
         self.behavior_topk = behavior_topk
+        if type(queue_capacity) is not int or queue_capacity < 0:
+            raise ValueError("queue_capacity must be a non-negative integer")
+        if queue_capacity and behavior_topk:
+            raise ValueError("Behavior heads are not recorded for requests of the device-side queue")
+        self.queue_capacity = queue_capacity
         self.entry = decoder._get_graph(max_batch_size, cache_len or self.engine.max_model_len, masked=True,
-                                        head_k=behavior_topk, head_positions=max_new_tokens)
+                                        head_k=behavior_topk, head_positions=max_new_tokens,
+                                        queue_capacity=queue_capacity)
         self.state, self.cache = self.entry.state, self.entry.cache
         self.cache.release_rows(torch.ones(self.cache.n_rows, device=self.engine.device, dtype=torch.uint8))
         self.cache.conv_state.zero_()
@@ -101,6 +108,10 @@ class LFM25GenerationSession:
         self._snapshots: dict[int, _SnapshotState] = {}
         self._next_snapshot = 0
         self._free_rows = list(range(self.cache.n_slots, self.cache.n_rows))
+        # device-side queue mode (enqueue / poll): request id -> (prompt, sampling, parked row), ids in order
+        self._queued: dict[int, tuple] = {}
+        self._next_request_id = 0
+        self._queue_tail = self._queue_consumed = 0
         self.requests: list[_Request | None] = [None] * max_batch_size
         self.versions = [0] * max_batch_size
         self.closed = False
@@ -211,6 +222,7 @@ class LFM25GenerationSession:
         generation. ``device_prompts`` (optional, one int64 tensor per prompt, already on the engine's
         device and holding the same ids) skips the host-to-device copy of the token ids."""
         self._check_open()
+        self._not_in_queue_mode("admit")
         if len(prompts) != len(samplings):
             raise ValueError("One sampling configuration is required per prompt")
         if device_prompts is not None and len(device_prompts) != len(prompts):
@@ -337,6 +349,7 @@ class LFM25GenerationSession:
     def fork(self, snapshot: LFM25PrefixSnapshot, samplings: Sequence[LFM25SamplingConfig], *,
              slots: Sequence[int] | None = None) -> list[int]:
         """Admit independent children of a snapshot into free slots, without prefill."""
+        self._not_in_queue_mode("fork")
         state = self._snapshot_for(snapshot)
         free = [i for i, request in enumerate(self.requests) if request is None]
         slots = list(free[:len(samplings)] if slots is None else slots)
@@ -416,6 +429,122 @@ class LFM25GenerationSession:
             self.stats["appended_tokens"] += len(prompt) - len(handle.prefix_token_ids) + 1
             self.stats["resumed_requests"] += 1
 
+    def _not_in_queue_mode(self, what: str) -> None:
+        if self.queue_capacity:
+            raise RuntimeError(f"{what} is not available on a session with a device-side queue: its slots are "
+                               "assigned on the device (use enqueue)")
+
+    # ---- device-side queue: eviction and admission inside the decode graph ---------------------------------
+    @torch.inference_mode()
+    def enqueue(self, prompts: Sequence[Sequence[int]], samplings: Sequence[LFM25SamplingConfig], *,
+                device_prompts: Sequence[torch.Tensor] | None = None) -> list[int]:
+        """Park ``prompts`` for admission on the device and return their request ids.
+
+        Each prompt is prefilled now into a spare row of the paged cache; the decode graph itself moves it
+        into the first slot that is free or whose request has just finished (lowest slot first, requests in
+        the order they were enqueued), so between two ``poll`` calls finished rows are evicted and replaced
+        without the host. Needs ``generation_session(queue_capacity=...)``; at most ``queue_capacity`` prompts
+        wait at a time (``queue_space()``)."""
+        self._check_open()
+        if not self.queue_capacity:
+            raise RuntimeError("enqueue needs a session opened with queue_capacity > 0")
+        if len(prompts) != len(samplings):
+            raise ValueError("One sampling configuration is required per prompt")
+        n = len(prompts)
+        if n == 0:
+            return []
+        if n > self.queue_space():
+            raise ValueError("Admission queue is full: poll first, or open the session with a larger queue_capacity")
+        for prompt, sampling in zip(prompts, samplings):
+            self._validate(prompt, sampling)
+        queue, dev = self.state.queue, self.engine.device
+        rows = [self._free_rows.pop(0) for _ in range(n)]
+        entries = [(self._queue_tail + i) % self.queue_capacity for i in range(n)]
+        ids = list(range(self._next_request_id, self._next_request_id + n))
+        with self._timed("prefill"):
+            if device_prompts is None:
+                self.engine._prefill_packed(self.cache, rows, [list(p) for p in prompts], [0] * n, queue["logits"],
+                                            self.decoder.max_prefill_tokens, logits_rows=entries)
+            else:
+                self.engine._prefill_packed(self.cache, rows, [len(p) for p in prompts], [0] * n, queue["logits"],
+                                            self.decoder.max_prefill_tokens, logits_rows=entries,
+                                            flat_tokens=torch.cat(list(device_prompts)).to(torch.int64))
+        index = torch.tensor(entries, device=dev, dtype=torch.int64)
+
+        def put(name, values, dtype):
+            queue[name].index_copy_(0, index, torch.tensor(values, device=dev, dtype=dtype))
+
+        put("rows", rows, torch.int32)
+        put("requests", ids, torch.int32)
+        put("limits", [s.max_new_tokens for s in samplings], torch.int32)
+        put("seeds", [s.seed & 0x7FFFFFFFFFFFFFFF for s in samplings], torch.int64)
+        put("temperatures", [float(s.temperature) for s in samplings], torch.float32)
+        put("ignore_eos", [int(s.ignore_eos) for s in samplings], torch.uint8)
+        put("stop_offsets", [self._stop_offset(s) for s in samplings], torch.int64)
+        queue["tail"].add_(n)  # publishes the entries: stream-ordered after everything above
+        self._queue_tail += n
+        self._next_request_id += n
+        for rid, prompt, sampling, row in zip(ids, prompts, samplings, rows):
+            self._queued[rid] = (tuple(prompt), sampling, row)
+            self.stats["prefilled_tokens"] += len(prompt)
+            self.stats["admitted_requests"] += 1
+        return ids
+
+    def queue_space(self) -> int:
+        """Prompts that can be enqueued now: free queue entries, parked rows and result rows."""
+        if not self.queue_capacity:
+            return 0
+        waiting = self._queue_tail - self._queue_consumed
+        results_free = self.state.queue["result_capacity"] - len(self._queued)
+        return max(0, min(self.queue_capacity - waiting, len(self._free_rows), results_free))
+
+    def _poll_queue(self, steps: int) -> list[LFM25SessionResult]:
+        """``steps`` replays (slot turnover runs inside each), one more turnover so that the last step's
+        finishers are published and replaced, then one read of the result index."""
+        if not self._queued:
+            return []
+        queue, dev = self.state.queue, self.engine.device
+        with self._timed("decode"):
+            for _ in range(steps):
+                self.entry.graph.replay()
+            self.decoder._turnover(self.entry)
+        self.stats["decode_steps"] += steps
+        self.stats["decode_row_steps"] += self.batch_size * steps
+        self.stats["reserved_row_steps"] += self.batch_size * steps
+        batches = self.stats["decode_batches"]
+        batches[str(self.batch_size)] = batches.get(str(self.batch_size), 0) + steps
+        head = int(queue["head"].item())
+        reasons = queue["result_reasons"].cpu().tolist()  # with the head above: the reads of this poll
+        self.cache.check_status()
+        ring = queue["result_capacity"]
+        # parked rows whose prompt a slot has adopted are free again
+        # (request ids are handed out in queue order, so the ids below `head` are the entries consumed so far)
+        adopted = sorted(rid for rid, (_, _, row) in self._queued.items() if row is not None and rid < head)
+        for rid in adopted:
+            prompt, sampling, row = self._queued[rid]
+            self._free_rows.append(row)
+            self._queued[rid] = (prompt, sampling, None)
+        self._free_rows.sort()
+        self.stats["slot_refills"] += max(0, head - max(self._queue_consumed, self.batch_size))
+        self._queue_consumed = head
+        self.stats["peak_live_slots"] = max(self.stats["peak_live_slots"], min(self.batch_size, head))
+        done = [rid for rid in sorted(self._queued) if self._queued[rid][2] is None and reasons[rid % ring]]
+        if not done:
+            return []
+        index = torch.tensor([rid % ring for rid in done], device=dev)
+        lengths = queue["result_lengths"][index].cpu().tolist()
+        longest = max(lengths)
+        tokens = self.state.tokens[:, :longest].index_select(0, index).cpu().tolist()
+        logprobs = self.state.logprobs[:, :longest].index_select(0, index).cpu().tolist()
+        queue["result_reasons"].index_fill_(0, index, 0)  # delivered: the result rows may be reused
+        results = []
+        for rid, length, ids, probs in zip(done, lengths, tokens, logprobs):
+            prompt, sampling, _ = self._queued.pop(rid)
+            results.append(LFM25SessionResult(None, prompt, tuple(ids[:length]),
+                                              tuple(probs[:length]) if sampling.return_logprobs else None,
+                                              reasons[rid % ring], None, rid))
+        return results
+
     def _select_graph(self, live):
         captures = len(self.entry.compact_graphs)
         graph, size = self.decoder._select_graph(self.entry, live)
@@ -428,6 +557,8 @@ class LFM25GenerationSession:
         steps = self.decoder.finish_check_interval if steps is None else steps
         if type(steps) is not int or steps <= 0:
             raise ValueError("steps must be a positive integer")
+        if self.queue_capacity:
+            return self._poll_queue(steps)
         live = [i for i, r in enumerate(self.requests) if r is not None and not r.delivered]
         if not live:
             return []

@@ -218,6 +218,9 @@ typedef struct {
   int32_t* seq_lens;      /* cache length per slot; advanced here for rows in `advance` */
   const float* min_logits; /* optional: per slot, logits below this value cannot be drawn (top-k / top-p
                               support from cgym_filter_thresholds); they still count in the log-prob */
+  const int32_t* out_rows; /* optional: slot s writes its tokens / log-probs to row out_rows[s] of `tokens` /
+                              `logprobs` (which then hold more rows than slots) instead of row s: with
+                              device-side slot turnover a request keeps its row after its slot is reused */
   int32_t capacity;
   int32_t eos_token_id;
 } cgym_slot_state;
@@ -347,6 +350,49 @@ int cgym_pages_reserve(const cgym_page_pool* pool, const int32_t* slot_ids,
  * lfm25_session.py:511-518). */
 int cgym_pages_release(const cgym_page_pool* pool, const uint8_t* release_mask,
                        int32_t* seq_lens, cgym_stream_t stream);
+
+/* Device-resident admission queue and result index of the slot scheduler. No reference counterpart: the
+ * reference scans its slots on the host at every poll, releases finished requests from Python and admits
+ * with a host-driven prefill (lfm25_session.py:259-292, 456-518). Here the host only parks prefilled prompts
+ * (a spare row of the paged cache + the prompt's next-token logits) in this queue and later drains results;
+ * finished requests leave their slots and parked ones enter them inside the decode graph.
+ * Entry i lives at index i % capacity; entries [head, tail) are pending (the host publishes by advancing
+ * tail, stream-ordered; the device consumes by advancing head). Results are indexed by request id %
+ * result_capacity: the host must keep fewer than result_capacity requests between enqueue and delivery. */
+typedef struct {
+  const int32_t* rows;         /* [capacity] parked cache row that holds the entry's prefilled prompt */
+  const int32_t* requests;     /* [capacity] request id (>= 0) */
+  const int32_t* limits;       /* [capacity] max_new_tokens */
+  const int64_t* seeds;        /* [capacity] */
+  const float* temperatures;   /* [capacity] */
+  const uint8_t* ignore_eos;   /* [capacity] */
+  const int64_t* stop_offsets; /* [capacity] offset of the request's stop table in cgym_slot_state.stop_table */
+  const void* logits;          /* [capacity][vocab] next-token logits after the prompt (model dtype) */
+  int32_t* head;               /* [1] */
+  const int32_t* tail;         /* [1] */
+  int32_t capacity;
+  int32_t result_capacity;
+  int32_t* result_lengths;     /* [result_capacity] tokens generated, written when the request finishes */
+  int8_t* result_reasons;      /* [result_capacity] finish reason (1 EOS, 2 stop, 3 length), 0 = not finished */
+  int32_t* slot_requests;      /* [n_slots] request id in each slot, -1 = free */
+  int32_t* out_rows;           /* [n_slots] = request id % result_capacity: pass as cgym_slot_state.out_rows */
+  int32_t* adopt_rows;         /* [n_slots] scratch */
+  int32_t* adopt_entries;      /* [n_slots] scratch */
+  uint8_t* release_mask;       /* [n_rows] scratch; bytes beyond n_slots must stay 0 */
+} cgym_admit_queue;
+
+/* Slot turnover at the start of a decode step, on the device (capturable): every finished request's length
+ * and reason are published under its request id and its pages returned to the pool; the queue's pending
+ * entries are dealt first-in first-out to the free slots in ascending slot order; an adopting slot takes
+ * over the parked row's block table (a move: no KV is copied, no reference count changes), length, conv taps
+ * and logits row, and its request state is re-armed from the entry (length 0, alive, not pending), so the
+ * step's sampler draws its first token from the prompt's logits. pool_rows spans all n_rows cache rows
+ * (slots first); row_lens is [n_rows] (its first n_slots entries are the slots' seq_lens); conv_state is
+ * [n_conv_layers][n_rows][3][hidden]; logits is [n_slots][vocab]. At most 1024 slots.
+ * No reference counterpart (see cgym_admit_queue; host-side equivalent: lfm25_session.py:456-518). */
+int cgym_slot_turnover(const cgym_page_pool* pool_rows, int n_slots, const cgym_slot_state* state,
+                       const cgym_admit_queue* queue, void* logits, void* conv_state, int32_t* row_lens,
+                       int n_conv_layers, int hidden, int vocab, int dtype, cgym_stream_t stream);
 
 /* Share a prefix: dst slots get src's full pages by reference (refcount++) and a private copy of
  * the partially filled last page (replaces copy_prefix_from, lfm25_engine.py:400-423). */
