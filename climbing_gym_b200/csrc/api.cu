@@ -19,7 +19,7 @@ int fail(const char* fmt, ...) {
 }
 
 std::atomic<long long> g_kernel_launches{0};
-int g_pdl_enabled = 0;
+thread_local int g_pdl_enabled = 0;
 
 int check_launch(const char* what, int kernels) {
   const cudaError_t rc = cudaGetLastError();

@@ -637,13 +637,6 @@ bool attention_mma_supported(const cgym_kv_layout* kv, int n_q_heads, int dtype)
   return G >= 1 && G <= 16 && n_q_heads % kv->n_kv_heads == 0;
 }
 
-template <typename K>
-static int set_smem(K kernel, int bytes) {
-  const cudaError_t rc = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  CGYM_REQUIRE(rc == cudaSuccess, "attention: cannot reserve %d bytes of shared memory: %s", bytes, cudaGetErrorString(rc));
-  return 0;
-}
-
 template <int EB, int D, int NST, bool HI>
 static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const int32_t* slots, const uint8_t* active,
                          const cgym_kv_layout* kv, int layer, int rows, int n_q_heads, float scale, int n_splits,
@@ -653,8 +646,8 @@ static int launch_decode(void* out, const void* q, const int32_t* kv_lens, const
   constexpr int ring = 4 * NST * Geo::STAGE_BYTES, merge = (4 * 16 * D + 2 * 4 * 16) * 4;
   constexpr int smem = ring > merge ? ring : merge;
   auto kernel = decode_attention_mma_kernel<T, EB, D, 64, NST, HI>;
-  static bool configured = false;
-  if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
+  static SmemReservation reservation;
+  if (int rc = reserve_dynamic_smem(kernel, smem, reservation, "paged_attention")) return rc;
   const cudaError_t rc = launch_dependent(kernel, dim3(rows, kv->n_kv_heads, n_splits), dim3(128), smem, stream,
                                           static_cast<T*>(out), static_cast<const T*>(q), kv_lens, slots, active, *kv,
                                           layer, n_q_heads, scale, n_splits, workspace, status);
@@ -667,11 +660,7 @@ int launch_decode_attention_mma(void* out, const void* q, const int32_t* kv_lens
                                 float scale, int n_splits, float* workspace, int32_t* status, cudaStream_t stream) {
   const bool fp8 = kv->kv_dtype == CGYM_E4M3;
   // More CTAs than one per SM: short rings, several CTAs per SM. Fewer: one deep ring per SM.
-  static const int forced = [] {  // tuning aid: CGYM_ATTN_STAGES=1|2|3 (2: e4m3 caches only)
-    const char* v = std::getenv("CGYM_ATTN_STAGES");
-    return v != nullptr ? std::atoi(v) : 0;
-  }();
-  const bool shallow = forced ? forced == 1 : static_cast<int64_t>(rows) * kv->n_kv_heads * n_splits > 148;
+  const bool shallow = static_cast<int64_t>(rows) * kv->n_kv_heads * n_splits > 148;
   // rows 8..15 of the 16-row MMA tile carry query heads only when more than 8 heads share a KV head
   const bool hi = n_q_heads / kv->n_kv_heads > 8;
 #define CGYM_DECODE(EB, NST)                                                                                          \
@@ -679,10 +668,7 @@ int launch_decode_attention_mma(void* out, const void* q, const int32_t* kv_lens
                                          workspace, status, stream)                                                   \
       : launch_decode<EB, 64, NST, false>(out, q, kv_lens, slots, active, kv, layer, rows, n_q_heads, scale, n_splits, \
                                           workspace, status, stream))
-  if (fp8) {
-    if (forced == 1) return CGYM_DECODE(1, 1);
-    return (shallow || forced == 2) ? CGYM_DECODE(1, 2) : CGYM_DECODE(1, 3);
-  }
+  if (fp8) return shallow ? CGYM_DECODE(1, 2) : CGYM_DECODE(1, 3);
   return shallow ? CGYM_DECODE(2, 1) : CGYM_DECODE(2, 3);
 #undef CGYM_DECODE
 }
@@ -693,23 +679,12 @@ static int launch_prefill(void* out, const void* q, const PrefillTiles& tiles, c
   using T = __nv_bfloat16;
   using Geo = BlockGeom<EB, D, 64>;
   constexpr int smem = 4 * Geo::STAGE_BYTES;
-  static const int mt = [] {  // tuning aid: CGYM_PREFILL_MT=1|2 m-tiles per consumer warp
-    const char* v = std::getenv("CGYM_PREFILL_MT");
-    return v != nullptr && std::atoi(v) == 2 ? 2 : 1;
-  }();
-  if (mt == 2) {
-    auto kernel = prefill_attention_mma_kernel<T, EB, D, 64, 2>;
-    static bool configured = false;
-    if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
-    kernel<<<dim3(n_tiles, kv->n_kv_heads), 160, smem, stream>>>(static_cast<T*>(out), static_cast<const T*>(q), tiles,
-                                                                 *kv, layer, n_q_heads, scale, status);
-  } else {
-    auto kernel = prefill_attention_mma_kernel<T, EB, D, 64, 1>;
-    static bool configured = false;
-    if (!configured) { if (int rc = set_smem(kernel, smem)) return rc; configured = true; }
-    kernel<<<dim3(n_tiles, kv->n_kv_heads), 288, smem, stream>>>(static_cast<T*>(out), static_cast<const T*>(q), tiles,
-                                                                 *kv, layer, n_q_heads, scale, status);
-  }
+  // eight consumer warps of one 16-row m-tile each (four warps of two m-tiles measured slower on long prompts)
+  auto kernel = prefill_attention_mma_kernel<T, EB, D, 64, 1>;
+  static SmemReservation reservation;
+  if (int rc = reserve_dynamic_smem(kernel, smem, reservation, "prefill_attention")) return rc;
+  kernel<<<dim3(n_tiles, kv->n_kv_heads), 288, smem, stream>>>(static_cast<T*>(out), static_cast<const T*>(q), tiles, *kv,
+                                                               layer, n_q_heads, scale, status);
   return 0;
 }
 

@@ -8,6 +8,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 
 #include "../../include/cgym_b200.h"
 
@@ -38,7 +39,7 @@ inline cudaStream_t as_stream(cgym_stream_t s) { return reinterpret_cast<cudaStr
 // kernels trigger BEFORE they wait, which lets the kernels several positions ahead become
 // resident - the GEMMs among them stream their first weight tiles - while the chain catches up.
 // Both are no-ops for ordinary launches.
-extern int g_pdl_enabled;  // toggled by cgym_set_pdl(); read at launch time on the host
+extern thread_local int g_pdl_enabled;  // per host thread: set by cgym_set_pdl(), read at launch time
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // A kernel that does work BEFORE pdl_wait() must reach its predecessor's output only through pointers
@@ -66,6 +67,33 @@ inline cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 b
   config.attrs = attr;
   config.numAttrs = g_pdl_enabled ? 1 : 0;
   return cudaLaunchKernelEx(&config, kernel, static_cast<Params>(args)...);
+}
+
+// ---- opt-in dynamic shared memory ------------------------------------------------------------
+// cudaFuncAttributeMaxDynamicSharedMemorySize belongs to a (kernel, device) pair: a process that drives
+// several GPUs must set it once on each. SmemReservation remembers, per device ordinal, the largest size set
+// so far for one kernel (declare one `static SmemReservation` beside each kernel's launch); calls from
+// several host threads are serialised. Ordinals beyond the table set the attribute on every call.
+struct SmemReservation {
+  static constexpr int MAX_DEVICES = 64;
+  std::mutex mutex;
+  int reserved[MAX_DEVICES] = {};
+};
+
+template <typename K>
+inline int reserve_dynamic_smem(K kernel, int bytes, SmemReservation& seen, const char* what) {
+  int device = -1;
+  cudaError_t rc = cudaGetDevice(&device);
+  if (rc != cudaSuccess) return fail("%s: cudaGetDevice failed: %s", what, cudaGetErrorString(rc));
+  std::lock_guard<std::mutex> lock(seen.mutex);
+  const bool tracked = device >= 0 && device < SmemReservation::MAX_DEVICES;
+  if (tracked && seen.reserved[device] >= bytes) return 0;
+  rc = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (rc != cudaSuccess)
+    return fail("%s: cannot reserve %d bytes of shared memory on device %d: %s", what, bytes, device,
+                cudaGetErrorString(rc));
+  if (tracked) seen.reserved[device] = bytes;
+  return 0;
 }
 
 // ---- element types ---------------------------------------------------------------------

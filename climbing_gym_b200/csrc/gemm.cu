@@ -1,8 +1,5 @@
 // Entry points of the projection GEMMs: pick the tcgen05/TMEM kernel when the operands allow it and
 // the CUDA-core tile kernel otherwise (fp32 models, unaligned K).
-#include <cstdlib>
-#include <cstring>
-
 #include "common.cuh"
 
 namespace cgym {
@@ -14,16 +11,6 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
                         void* workspace, int64_t workspace_bytes, int32_t* status, int force_splits,
                         cudaStream_t stream);
 bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const void* w);
-
-// CGYM_GEMM_IMPL=simt|tcgen05 overrides impl == 0 (auto); read once.
-static int env_impl() {
-  static int cached = -1;
-  if (cached < 0) {
-    const char* v = std::getenv("CGYM_GEMM_IMPL");
-    cached = (v == nullptr) ? 0 : (std::strcmp(v, "simt") == 0 ? 1 : (std::strcmp(v, "tcgen05") == 0 ? 2 : 0));
-  }
-  return cached;
-}
 }  // namespace cgym
 
 using namespace cgym;
@@ -35,7 +22,6 @@ extern "C" int cgym_gemm_scatter(void* y, const void* x, const void* w, const ui
   CGYM_REQUIRE(y && x && w, "gemm: null operand");
   CGYM_REQUIRE(impl >= 0 && impl <= 3, "gemm: impl must be 0 (auto), 1 (simt), 2 (tcgen05) or 3 (tcgen05, forced split-K)");
   if (M == 0) return 0;
-  if (impl == 0) impl = env_impl();
   if (impl == 0) impl = (dtype == CGYM_BF16 && gemm_tcgen05_supports(M, N, K, false, x, w)) ? 2 : 1;
   if (impl >= 2) {
     CGYM_REQUIRE(dtype == CGYM_BF16, "gemm(tcgen05): bf16 operands only");
@@ -60,7 +46,6 @@ extern "C" int cgym_gemm_fp8_scatter(void* y, const uint8_t* xq, const float* x_
   CGYM_REQUIRE(y && xq && wq && x_scales && w_scales, "gemm_fp8: null operand");
   CGYM_REQUIRE(impl >= 0 && impl <= 3, "gemm_fp8: impl must be 0..3");
   if (M == 0) return 0;
-  if (impl == 0) impl = env_impl();
   if (impl == 0) impl = gemm_tcgen05_supports(M, N, K, true, xq, wq) ? 2 : 1;
   if (impl >= 2)
     return launch_gemm_tcgen05(y, xq, wq, x_scales, w_scales, row_mask, row_map, M, N, K, true, workspace,

@@ -18,7 +18,6 @@
 // copies with the same bound, frees its TMEM and returns.
 #include <cuda.h>
 
-#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -129,24 +128,8 @@ struct GemmEpilogue {
   int M, N, K;
   int partial;             // 1: split-K over a cluster of gridDim.z CTAs
   float* split_ws;         // split-K partial tiles [tile][split][UN][128] fp32; NULL = exchange through DSMEM
-#ifdef CGYM_TRACE
-  unsigned long long* trace;  // [ctas <= 512][8] globaltimer stamps of this launch (debug builds only)
-#endif
 };
 
-#ifdef CGYM_TRACE
-__device__ __forceinline__ void trace_stamp(const GemmEpilogue& ep, int which) {
-  if (ep.trace == nullptr) return;
-  const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-  if (cta >= 512u) return;
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  ep.trace[cta * 16 + which] = t;
-}
-#define CGYM_STAMP(which) trace_stamp(ep, which)
-#else
-#define CGYM_STAMP(which)
-#endif
 
 // Cluster split-K reduction of the parked [UN][128] fp32 tiles. CTA `rank` owns the token rows
 // ml = rank, rank + SPLITS, ...; epilogue warp `quarter` takes every fourth of them, and one 16-byte
@@ -194,19 +177,6 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
                      : "r"(peer[sp] + ml * (UM * 4u)));
     }
   }
-#ifdef CGYM_TRACE
-  if (ep.trace != nullptr && quarter == 2 && lane == 0 && first == 0) {  // stamp 8: all remote loads have landed
-    float sink = 0.0f;
-#pragma unroll
-    for (int b = 0; b < BATCH; ++b)
-#pragma unroll
-      for (int sp = 0; sp < SPLITS; ++sp) sink += value[b][sp].w;
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "f"(sink));
-    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    if (cta < 512u) ep.trace[cta * 16 + 8] = t;
-  }
-#endif
 #pragma unroll
   for (int b = 0; b < BATCH; ++b) {
     const int i = first + b;
@@ -268,7 +238,6 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   __shared__ int abort_flag;
 
   pdl_trigger();  // the next kernel may be scheduled now; it waits for this grid before touching y
-  if (threadIdx.x == 0) CGYM_STAMP(0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t tiles = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int n0 = blockIdx.x * (UM * FM), m0 = blockIdx.y * UN;
@@ -313,7 +282,6 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
                     n0 + f * UM);
     }
     pdl_wait();
-    CGYM_STAMP(1);
     for (int i = 0; i < prefetch; ++i) {
       tma_load_2d(tiles + i * STAGE_BYTES + W_BYTES, &tmap_x, smem_u32(&bar_full[i]),
                   (kb_begin + i) * ELEMS_PER_SLICE, m0);
@@ -367,7 +335,6 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     pdl_wait();  // scales / row mask come from earlier kernels of the step
     if (n_kb > 0) mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
     asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps agree on abort_flag
-    if (warp == 2 && lane == 0) CGYM_STAMP(2);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (abort_flag == 0 || ep.partial) {
 #pragma unroll 1
@@ -414,9 +381,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
     // split order, the token rows m with m % splits == r straight out of its peers' shared memory
     // (distributed shared memory), applies scales / mask and writes y. Deterministic, no HBM round trip.
     __syncwarp();  // the producer / MMA lanes rejoin their warps before the aligned cluster barrier
-    if (warp == 2 && lane == 0) CGYM_STAMP(4);
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-    if (warp == 2 && lane == 0) CGYM_STAMP(5);
     if (warp >= 2) {
       const int quarter = warp & 3;
       const uint32_t splits = gridDim.z, rank = blockIdx.z;
@@ -432,19 +397,16 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
         else cluster_reduce_rows<8, UN, false>(ep, tiles, nullptr, rank, quarter, lane, m0, n0);
       }
     }
-    if (warp == 2 && lane == 0) CGYM_STAMP(6);
     if (ep.split_ws == nullptr) {
       // nobody leaves (and frees its shared memory) while a peer may still be reading it
       __syncwarp();
       asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     }
-    if (warp == 2 && lane == 0) CGYM_STAMP(7);
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (threadIdx.x == 0 && abort_flag) atomicOr(ep.status, CGYM_STATUS_WAIT_TIMEOUT);
-  if (threadIdx.x == 0) CGYM_STAMP(3);
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_acc), "r"(TMEM_COLS) : "memory");
@@ -491,13 +453,8 @@ static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
   constexpr int STAGES = (RING_KB * 1024 / STAGE_BYTES) > 8 ? 8 : (RING_KB * 1024 / STAGE_BYTES);
   constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
   static_assert(UN * UM * 4 <= STAGES * STAGE_BYTES, "the split-K partial tile must fit in the idle ring");
-  static bool configured = false;  // per instantiation; the attribute is per function, set once
-  if (!configured) {
-    const cudaError_t rc = cudaFuncSetAttribute(gemm_tcgen05_kernel<UN, FP8, RING_KB, FM>,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    CGYM_REQUIRE(rc == cudaSuccess, "gemm: cannot reserve %d bytes of shared memory: %s", SMEM, cudaGetErrorString(rc));
-    configured = true;
-  }
+  static SmemReservation reservation;  // per instantiation
+  if (int rc = reserve_dynamic_smem(gemm_tcgen05_kernel<UN, FP8, RING_KB, FM>, SMEM, reservation, "gemm(tcgen05)")) return rc;
   cudaLaunchConfig_t config = {};
   config.gridDim = grid;
   config.blockDim = dim3(GEMM_THREADS);
@@ -524,15 +481,6 @@ static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
   return 0;
 }
 
-#ifdef CGYM_TRACE
-static unsigned long long* g_trace_buffer = nullptr;
-static int g_trace_launch = 0;
-extern "C" int cgym_debug_trace(void* buffer) {  // 512 launches x 512 CTAs x 4 stamps of u64
-  g_trace_buffer = static_cast<unsigned long long*>(buffer);
-  g_trace_launch = 0;
-  return 0;
-}
-#endif
 
 bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const void* w) {
   const int elem = fp8 ? 1 : 2;
@@ -552,25 +500,15 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   // Token tile: the smallest that covers M up to 128; up to 256 rows (a full decode batch) two tiles of
   // 128 keep the weight-streaming layout (half-SM rings, split-K) - the second tile's weight loads hit
   // L2 - and only larger M (prefill) takes the 256-token tile that halves L2 -> SM traffic per FLOP.
-  static const int wide_from = [] {  // tuning aid: smallest M that uses the 256-token tile
-    const char* v = std::getenv("CGYM_GEMM_WIDE_FROM");
-    return v != nullptr && std::atoi(v) > 0 ? std::atoi(v) : 257;
-  }();
-  int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M < wide_from ? 128 : 256));
+  int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 256 ? 128 : 256));
   // Two feature sub-tiles per CTA (one fetch of the token tile serves 256 features) for unsplit GEMMs
   // over more than 128 tokens. With 256-token tiles (prefill) it pays unless halving the CTA count costs
   // more in the last, partly filled wave than the saved traffic gains; for a decode batch of 129..256
   // rows only the LM head is large enough, and it then takes the 256-token tile as well.
-  static const int fm_mode = [] {  // tuning aid: CGYM_GEMM_FM=1 never, 2 wherever the shape allows
-    const char* v = std::getenv("CGYM_GEMM_FM");
-    return v != nullptr ? std::atoi(v) : 0;
-  }();
   bool dual = false;
-  if (M > 128 && N % (2 * UM) == 0 && force_splits <= 1 && fm_mode != 1) {
+  if (M > 128 && N % (2 * UM) == 0 && force_splits <= 1) {
     auto wave_fill = [](int ctas) { return static_cast<double>(ctas) / (148.0 * ((ctas + 147) / 148)); };
-    if (fm_mode == 2) {
-      dual = true;
-    } else if (un == 256) {
+    if (un == 256) {
       const int single = (N / UM) * ((M + 255) / 256);
       dual = wave_fill(single / 2) >= wave_fill(single) - 0.1;
     } else if (N / (2 * UM) >= 148) {
@@ -581,15 +519,11 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   const int n_tiles = (N + UM - 1) / UM, m_tiles = (M + un - 1) / un;
   const int total_kb = (K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
   // decode-sized token tiles take the half-SM ring (two CTAs per SM), larger ones the full ring
-  bool half_ring = un <= 128;
-  if (const char* forced = std::getenv("CGYM_GEMM_RING_KB")) half_ring = un <= 128 && std::atoi(forced) <= 96;  // tuning aid
+  const bool half_ring = un <= 128;
   // Split-K until the CTAs fill the GPU's resident slots (at most 8: the portable cluster size). A
   // weight stream is bound by the bytes in flight, i.e. by how many rings are filling at once, so a
   // decode GEMM wants about two CTAs on every SM, each owning as little as one ring of K slices.
-  static const int min_kb = [] {  // tuning aid: fewest K slices per split
-    const char* v = std::getenv("CGYM_GEMM_MIN_KB");
-    return v != nullptr && std::atoi(v) > 0 ? std::atoi(v) : 4;
-  }();
+  constexpr int min_kb = 4;  // fewest K slices per split: one fill of the half-SM ring
   int splits = 1;
   if (force_splits > 0) {
     splits = force_splits;
@@ -598,10 +532,6 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
     splits = slots / (n_tiles * m_tiles);
     if (splits > total_kb / min_kb) splits = total_kb / min_kb;
   }
-  if (const char* forced = std::getenv("CGYM_GEMM_SPLITS")) {  // tuning aid: force a split count (1 = off)
-    const int v = std::atoi(forced);
-    if (v >= 1) splits = v;
-  }
   if (dual) splits = 1;
   if (splits > 8) splits = 8;
   if (splits > total_kb) splits = total_kb;
@@ -609,13 +539,9 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   // every split must own at least one K slice
   while (splits > 1 && (splits - 1) * ((total_kb + splits - 1) / splits) >= total_kb) splits /= 2;
   // partial tiles go through the caller's workspace (L2) when it is large enough, else through DSMEM
-  static const bool use_workspace = [] {  // tuning aid: CGYM_GEMM_SPLIT_WS=0 forces the DSMEM exchange
-    const char* v = std::getenv("CGYM_GEMM_SPLIT_WS");
-    return v == nullptr || std::atoi(v) != 0;
-  }();
   const int64_t split_bytes = static_cast<int64_t>(n_tiles) * m_tiles * splits * un * UM * 4;
   float* split_ws = nullptr;
-  if (splits > 1 && use_workspace && workspace != nullptr && workspace_bytes >= split_bytes &&
+  if (splits > 1 && workspace != nullptr && workspace_bytes >= split_bytes &&
       (reinterpret_cast<uintptr_t>(workspace) & 15u) == 0)
     split_ws = static_cast<float*>(workspace);
 
@@ -625,9 +551,6 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, row_map, status, M, N, K,
                   splits > 1 ? 1 : 0, split_ws};
   dim3 grid(dual ? n_tiles / 2 : n_tiles, m_tiles, splits);
-#ifdef CGYM_TRACE
-  ep.trace = g_trace_buffer != nullptr && g_trace_launch < 512 ? g_trace_buffer + (g_trace_launch++) * 8192ull : nullptr;
-#endif
   int rc = 0;
 #define LAUNCH_UN(U, R)                                                                 \
   rc = fp8 ? launch_tile<U, true, R>(mw, mx, ep, grid, stream) : launch_tile<U, false, R>(mw, mx, ep, grid, stream)

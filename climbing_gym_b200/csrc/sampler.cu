@@ -530,18 +530,9 @@ extern "C" int cgym_filter_thresholds(float* min_logits, const void* logits, con
   if (rows == 0) return 0;
   if (dtype == CGYM_BF16) {
     const int smem = vocab * static_cast<int>(sizeof(uint16_t));
-    static std::mutex mutex;
-    static int reserved = 0;
-    {
-      std::lock_guard<std::mutex> lock(mutex);
-      if (smem > reserved) {
-        const cudaError_t rc = cudaFuncSetAttribute(filter_threshold_kernel<__nv_bfloat16>,
-                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        CGYM_REQUIRE(rc == cudaSuccess, "filter_thresholds: cannot reserve %d bytes of shared memory: %s", smem,
-                     cudaGetErrorString(rc));
-        reserved = smem;
-      }
-    }
+    static SmemReservation reservation;
+    if (int rc = reserve_dynamic_smem(filter_threshold_kernel<__nv_bfloat16>, smem, reservation, "filter_thresholds"))
+      return rc;
     launch_dependent(filter_threshold_kernel<__nv_bfloat16>, dim3(rows), dim3(FILTER_THREADS), smem, as_stream(stream),
                      min_logits, static_cast<const __nv_bfloat16*>(logits), temperatures, top_k, top_p, alive, vocab);
   } else if (dtype == CGYM_F32) {
@@ -562,18 +553,8 @@ extern "C" int cgym_topk_head(int32_t* out_ids, float* out_logprobs, const void*
   if (n_slots == 0) return 0;
   if (dtype == CGYM_BF16) {
     const int smem = vocab * static_cast<int>(sizeof(uint16_t));
-    static std::mutex mutex;
-    static int reserved = 0;
-    {
-      std::lock_guard<std::mutex> lock(mutex);
-      if (smem > reserved) {
-        const cudaError_t rc = cudaFuncSetAttribute(topk_head_kernel<__nv_bfloat16>,
-                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        CGYM_REQUIRE(rc == cudaSuccess, "topk_head: cannot reserve %d bytes of shared memory: %s", smem,
-                     cudaGetErrorString(rc));
-        reserved = smem;
-      }
-    }
+    static SmemReservation reservation;
+    if (int rc = reserve_dynamic_smem(topk_head_kernel<__nv_bfloat16>, smem, reservation, "topk_head")) return rc;
     launch_dependent(topk_head_kernel<__nv_bfloat16>, dim3(n_slots), dim3(FILTER_THREADS), smem, as_stream(stream), out_ids,
                      out_logprobs, static_cast<const __nv_bfloat16*>(logits), alive, lengths, vocab, capacity, k);
   } else if (dtype == CGYM_F32) {

@@ -11,7 +11,6 @@ rows are masked inside the kernels instead of being compacted on the host.
 from __future__ import annotations
 
 import ctypes as C
-import os
 from collections import OrderedDict
 from dataclasses import dataclass, field
 
@@ -153,7 +152,9 @@ class SlotState:
         flat = table.reshape(-1).to(device=self.stop_table.device, dtype=torch.int32)
         offset = self.stop_table_used
         if offset + flat.numel() > self.stop_table.numel():
-            raise ValueError("stop tables exceed the session's reserved stop-state arena")
+            states = self.stop_table.numel() // self.vocab
+            raise ValueError(f"stop tables exceed the reserved stop-state arena ({states} states, one per proper prefix "
+                             "of every stop string): raise enable_cuda_graphs(stop_states=...)")
         self.stop_table[offset:offset + flat.numel()].copy_(flat)
         self.stop_table_used = offset + flat.numel()
         return offset
@@ -226,7 +227,7 @@ class B200Decoder:
                  max_prefill_tokens: int = 4096, finish_check_interval: int = 32,
                  skip_finished_attention: bool = True, fp8_mlp: bool = False, fp8_kv: bool = False,
                  adaptive_batching: bool = False, fp8_lm_head: bool = False, page_size: int = 64,
-                 use_cuda_graphs: bool = True, snapshot_rows: int = 32, snapshot_pages: int | None = None):
+                 snapshot_rows: int = 32, snapshot_pages: int | None = None, stop_states: int = 256):
         if engine.device.type != "cuda" or engine.dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("LFM2.5 CUDA graphs require CUDA and bfloat16 (or float32) weights")
         cfg = engine.config
@@ -254,13 +255,21 @@ class B200Decoder:
         self.fp8_mlp, self.fp8_kv = bool(fp8_mlp), bool(fp8_kv)
         self.adaptive_batching, self.fp8_lm_head = bool(adaptive_batching), bool(fp8_lm_head)
         self.page_size = page_size
-        self.use_cuda_graphs = use_cuda_graphs
         if snapshot_rows < 0 or (snapshot_pages is not None and snapshot_pages < 0):
             raise ValueError("snapshot_rows and snapshot_pages must be >= 0")
         # session caches park prefix snapshots in spare rows of the paged cache; the page reserve defaults to
         # eight full-length prefixes plus one private tail page per snapshot
         self.snapshot_rows, self.snapshot_pages = int(snapshot_rows), snapshot_pages
-        self.use_pdl = os.environ.get("CGYM_PDL", "1") != "0"
+        # Stop tables live in one device arena of `stop_states` x vocab int32 entries per graph entry (state 0
+        # is the shared "no stops" table): one state per proper prefix of every stop string in use. 256 states
+        # cost 64 MB at a 65,536-token vocabulary. The reference concatenates tables without a limit
+        # (src/climbing_gym/inference/lfm25_session.py:228-241); here the arena is fixed because the captured
+        # graph holds its address, so its size is an option and tables no slot refers to are recycled.
+        if type(stop_states) is not int or stop_states < 2:
+            raise ValueError("stop_states must be an integer >= 2")
+        self.stop_states = stop_states
+        # the step's kernels are chained with programmatic dependent launches while a graph is captured
+        self.use_pdl = True
         self.runner = LFM25Runner(engine.weights, engine._rope_cos, engine._rope_sin, fp8_mlp=self.fp8_mlp,
                                   fp8_lm_head=self.fp8_lm_head)
         self.graphs: OrderedDict = OrderedDict()
@@ -360,7 +369,8 @@ class B200Decoder:
             n_pages = batch_size * blocks + reserve + queue_capacity * blocks
         cache = engine._empty_cache(max_slots=batch_size, max_seq_len=capacity, fp8_kv=self.fp8_kv,
                                     page_size=self.page_size, n_pages=n_pages, spare_rows=spare)
-        state = SlotState(batch_size, capacity, engine.config.vocab_size, int(engine.config.eos_token_id), cache.seq_lens)
+        state = SlotState(batch_size, capacity, engine.config.vocab_size, int(engine.config.eos_token_id), cache.seq_lens,
+                          stop_states=self.stop_states)
         if head_k:
             state.allocate_heads(head_k, head_positions)
         if penalised:
@@ -385,15 +395,12 @@ class B200Decoder:
                     self._step(entry)
             current.wait_stream(stream)
             torch.cuda.synchronize(engine.device)
-            if self.use_cuda_graphs:
-                graph = torch.cuda.CUDAGraph()
-                before = lib.cgym_launch_count()
-                with torch.cuda.graph(graph, stream=stream):
-                    self._step(entry)
-                current.wait_stream(stream)
-                entry.graph = _StepGraph(graph, int(lib.cgym_launch_count() - before))
-            else:
-                entry.graph = _EagerStep(self, entry)
+            graph = torch.cuda.CUDAGraph()
+            before = lib.cgym_launch_count()
+            with torch.cuda.graph(graph, stream=stream):
+                self._step(entry)
+            current.wait_stream(stream)
+            entry.graph = _StepGraph(graph, int(lib.cgym_launch_count() - before))
         finally:
             lib.cgym_set_pdl(previous_pdl)
         self.graphs[key] = entry
@@ -570,16 +577,6 @@ class _StepGraph:
     def replay(self) -> None:
         self.graph.replay()
         nv.note_graph_replay(self.kernels)
-
-
-class _EagerStep:
-    """Graph stand-in that launches the step kernels directly (debugging / profiling aid)."""
-
-    def __init__(self, decoder: B200Decoder, entry: _DecodeGraph):
-        self.decoder, self.entry = decoder, entry
-
-    def replay(self) -> None:
-        self.decoder._step(self.entry)
 
 
 def build_token_stop_table(sampling: LFM25SamplingConfig, vocab: int, device) -> torch.Tensor:

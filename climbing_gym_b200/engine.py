@@ -492,33 +492,65 @@ class LFM25Engine:
     @torch.inference_mode()
     def decode_step(self, state: LFM25DecodeBatch, input_tokens: torch.Tensor,
                     sampling: LFM25SamplingConfig | None = None) -> LFM25StepOutput:
-        """Append one token per slot of ``state`` and sample the next one (greedy or full-support)."""
+        """Append one token to every slot in ``state.active_slot_ids`` (one input token each, in that order)
+        and sample the next one; other slots of the cache are not touched. Outputs are indexed like
+        ``active_slot_ids`` (reference: src/climbing_gym/inference/lfm25_engine.py:715-738). Top-k / top-p are
+        applied through the device threshold kernel; a repetition penalty needs the generate loop's seen-token
+        mask and is refused here."""
         sampling = sampling or LFM25SamplingConfig()
         cache, dev = state.cache, self.device
-        tokens = input_tokens.to(device=dev, dtype=torch.long).reshape(-1)
-        if tokens.numel() != cache.max_slots:
+        slots = state.active_slot_ids.to(device=dev, dtype=torch.int32).reshape(-1)
+        tokens = input_tokens.to(device=dev, dtype=torch.long).reshape(-1).contiguous()
+        n = int(slots.numel())
+        if tokens.numel() != n:
             raise ValueError("input_tokens must have one token per active slot")
-        if bool((cache.seq_lens >= cache.max_seq_len).any()):
+        if float(sampling.repetition_penalty) != 1.0:
+            raise ValueError("decode_step does not apply a repetition penalty: use generate, which tracks the seen tokens")
+        if n == 0:
+            raise ValueError("decode_step needs at least one active slot")
+        rows = slots.long()
+        if bool((slots < 0).any()) or bool((slots >= cache.max_slots).any()) or rows.unique().numel() != n:
+            raise ValueError("active_slot_ids must be distinct slots of the cache")
+        if bool((cache.seq_lens.index_select(0, rows) >= cache.max_seq_len).any()):
             raise RuntimeError("cache capacity exceeded")
         runner = self._runner()
-        bufs = ForwardBuffers(self.weights, cache.max_slots, fp8=runner.fp8_mlp or runner.fp8_lm_head)
-        active = torch.ones(cache.max_slots, device=dev, dtype=torch.uint8)
-        logits = torch.empty((cache.max_slots, self.config.vocab_size), device=dev, dtype=self.dtype)
-        kv_lens = runner.kv_lens_buffer(cache)
-        nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), None, None, nv.ptr(active), None,
-                nv.ptr(kv_lens), cache.max_slots, nv.ptr(cache.status), nv.stream_ptr(dev))
-        runner.decode_step(bufs, cache, tokens, active, logits, kv_lens=kv_lens)
-        cache.seq_lens.add_(1)
-        n = cache.max_slots
+        vocab = self.config.vocab_size
+        bufs = ForwardBuffers(self.weights, n, fp8=runner.fp8_mlp or runner.fp8_lm_head)
+        active = torch.ones(n, device=dev, dtype=torch.uint8)
+        logits = torch.empty((n, vocab), device=dev, dtype=self.dtype)
+        kv_lens = torch.empty(n, device=dev, dtype=torch.int32)
+        stream = nv.stream_ptr(dev)
+        nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), None, None, nv.ptr(active), nv.ptr(slots),
+                nv.ptr(kv_lens), n, nv.ptr(cache.status), stream)
+        runner.decode_step(bufs, cache, tokens, active, logits, slots=slots, rows=n, kv_lens=kv_lens)
+        cache.seq_lens.index_add_(0, rows, torch.ones(n, device=dev, dtype=torch.int32))
         out_tokens = torch.empty(n, device=dev, dtype=torch.int64)
         out_logp = torch.empty(n, device=dev, dtype=torch.float32)
         seeds = torch.full((n,), int(sampling.seed) & 0x7FFFFFFFFFFFFFFF, device=dev, dtype=torch.int64)
         steps = torch.zeros(n, device=dev, dtype=torch.int64)
         temps = torch.full((n,), float(sampling.temperature), device=dev, dtype=torch.float32)
-        offsets = torch.arange(n, device=dev, dtype=torch.int64) * self.config.vocab_size
-        nv.call("cgym_sample", nv.ptr(out_tokens), nv.ptr(out_logp), nv.ptr(logits), nv.ptr(seeds), nv.ptr(steps),
-                nv.ptr(temps), nv.ptr(offsets), n, self.config.vocab_size, nv.dtype_code(self.dtype), None,
-                nv.stream_ptr(dev))
+        offsets = torch.arange(n, device=dev, dtype=torch.int64) * vocab
+        filtered = sampling.temperature > 0.0 and (0 < sampling.top_k < vocab or sampling.top_p < 1.0)
+        if filtered:
+            # same kernels as the generate loop: a per-row value threshold, then the sampler restricted to it
+            from .decoder import SlotState
+
+            scratch = SlotState(n, 1, vocab, int(self.config.eos_token_id), torch.zeros(n, device=dev, dtype=torch.int32))
+            scratch.configure(list(range(n)), limits=2, seeds=int(sampling.seed) & 0x7FFFFFFFFFFFFFFF,
+                              temperatures=float(sampling.temperature), ignore_eos=1, stop_offsets=0,
+                              rng_offsets=[row * vocab for row in range(n)])
+            scratch.top_k.fill_(int(sampling.top_k))
+            scratch.top_p.fill_(float(sampling.top_p))
+            dt = nv.dtype_code(self.dtype)
+            nv.call("cgym_filter_thresholds", nv.ptr(scratch.min_logits), nv.ptr(logits), nv.ptr(scratch.temperatures),
+                    nv.ptr(scratch.top_k), nv.ptr(scratch.top_p), nv.ptr(scratch.alive), n, vocab, dt, stream)
+            import ctypes as C
+
+            nv.call("cgym_sample_record", nv.ptr(logits), C.byref(scratch.struct_filtered), None, nv.ptr(out_tokens),
+                    nv.ptr(out_logp), n, vocab, dt, nv.ptr(scratch.sample_ws), stream)
+        else:
+            nv.call("cgym_sample", nv.ptr(out_tokens), nv.ptr(out_logp), nv.ptr(logits), nv.ptr(seeds), nv.ptr(steps),
+                    nv.ptr(temps), nv.ptr(offsets), n, vocab, nv.dtype_code(self.dtype), None, stream)
         reasons = torch.zeros(n, device=dev, dtype=torch.int8)
         if not sampling.ignore_eos:
             reasons[out_tokens == int(self.config.eos_token_id)] = 1

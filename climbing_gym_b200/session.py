@@ -194,15 +194,47 @@ class LFM25GenerationSession:
         if table is not None and (table.ndim != 2 or table.size(1) != vocab or table.dtype != torch.int32):
             raise ValueError("stop_table must be an int32 state-by-vocabulary table")
 
+    @staticmethod
+    def _stop_key(sampling):
+        return (id(sampling.stop_table), sampling.stop_token_ids)
+
     def _stop_offset(self, sampling) -> int:
         if sampling.stop_table is None and not sampling.stop_token_ids:
             return 0
-        key = (id(sampling.stop_table), sampling.stop_token_ids)
+        key = self._stop_key(sampling)
         if key not in self._stop_tables:
             table = build_token_stop_table(sampling, self.engine.config.vocab_size, self.engine.device)
+            try:
+                offset = self.state.add_stop_table(table)
+            except ValueError:
+                self._recycle_stop_tables()
+                offset = self.state.add_stop_table(table)
             # keep the source table alive so a later table cannot reuse its id()
-            self._stop_tables[key] = (self.state.add_stop_table(table), sampling.stop_table)
+            self._stop_tables[key] = (offset, sampling.stop_table, table)
         return self._stop_tables[key][0]
+
+    def _recycle_stop_tables(self) -> None:
+        """The arena is full: keep only the tables a resident request still refers to, packed from the
+        start, and point those requests' slots at the new offsets (chains of requests with ever new stop
+        rules would otherwise fill the arena for good)."""
+        resident = {slot: self._stop_key(r.sampling) for slot, r in enumerate(self.requests)
+                    if r is not None and (r.sampling.stop_table is not None or r.sampling.stop_token_ids)}
+        parked = {self._stop_key(s) for _, s, _ in self._queued.values() if s.stop_table is not None or s.stop_token_ids}
+        if parked:
+            raise ValueError("stop tables exceed the reserved stop-state arena while requests with stop rules are parked "
+                             "in the device-side queue: raise enable_cuda_graphs(stop_states=...)")
+        # (a request that is being armed right now is resident already, but its table is the one being added)
+        resident = {slot: key for slot, key in resident.items() if key in self._stop_tables}
+        keep = {key: entry for key, entry in self._stop_tables.items() if key in set(resident.values())}
+        self.state.stop_table_used = self.engine.config.vocab_size
+        self._stop_tables = {}
+        for key, (_, source, table) in keep.items():
+            self._stop_tables[key] = (self.state.add_stop_table(table), source, table)
+        if resident:
+            slots = torch.tensor(sorted(resident), device=self.engine.device, dtype=torch.int64)
+            offsets = torch.tensor([self._stop_tables[resident[s]][0] for s in sorted(resident)],
+                                   device=self.engine.device, dtype=torch.int64)
+            self.state.stop_offsets.index_copy_(0, slots, offsets)
 
     def _configure(self, slots, prompts, samplings, *, rng_positions=None, stop_states=None):
         for slot, prompt, sampling in zip(slots, prompts, samplings):

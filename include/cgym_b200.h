@@ -43,11 +43,23 @@ enum {
 };
 
 /* Geometry of the paged hybrid cache (replaces the dense LFM25HybridCache,
- * lfm25_engine.py:370-431,1165-1221). One page holds `page_size` tokens of every KV head of
- * one attention layer: pool[layer][page][k|v][kv_head][token][dim]. */
+ * lfm25_engine.py:370-431,1165-1221). One page holds `page_size` tokens of every KV head of one attention
+ * layer. kv_pool is [layer][n_pages][kv_head][2 * page_size * head_dim] elements; one (page, head) block is
+ *     K   as [token][dim]   (page_size rows of head_dim elements), followed by
+ *     V^T as [dim][token]   (head_dim rows of page_size elements),
+ * i.e. both are stored contraction-contiguous for the tensor-core attention kernels, and a block moves to
+ * shared memory with one linear bulk copy. Inside every row the 16-byte chunks are permuted, in global
+ * memory: chunk c of row r (c = byte offset / 16 within the row, n = chunks per row) is stored at chunk
+ *     c ^ (r & 7)                      when n >= 8,
+ *     c ^ ((r / (8 / n)) & (n - 1))    when n < 8 (8 / n consecutive rows share a 128-byte line),
+ * so that 8 consecutive rows read at one logical column hit 8 different 16-byte bank groups. For K the row is
+ * the token and the column the dim; for V^T the row is the dim and the column the token. Element (token t,
+ * dim d) of K therefore lives at block + t * head_dim + swz(t, d / e, head_dim / e) * e + d % e with e = 16 /
+ * element size, and of V at block + page_size * head_dim + d * page_size + swz(d, t / e, page_size / e) * e +
+ * t % e. cgym_scatter_kv_dense / cgym_gather_kv_dense write and read the cache through this mapping. */
 typedef struct {
   void* kv_pool;          /* element type kv_dtype */
-  float* kv_scales;       /* [layer][page][k|v][kv_head][token], only for CGYM_E4M3, else NULL */
+  float* kv_scales;       /* [layer][n_pages][kv_head][k|v][token] fp32, only for CGYM_E4M3, else NULL */
   const int32_t* block_table; /* [n_slots][max_blocks] page ids, -1 = none */
   int32_t n_pages;
   int32_t page_size;      /* tokens per page, power of two */
@@ -72,7 +84,8 @@ long long cgym_launch_count(void);
  * write (in the decode step these come from cgym_step_begin - launched without the attribute, so it
  * completes before the chain starts - or from earlier steps). A caller that chains entry points
  * itself while this is enabled must keep to the same rule. Off by default; returns the previous setting.
- * Process-wide host flag read at launch time (set it around a graph capture). No reference
+ * The flag belongs to the calling host thread and is read at launch time by launches from that thread (set
+ * it around a graph capture; other threads' launches, e.g. a second engine's, are unaffected). No reference
  * counterpart (the reference relies on CUDA graphs alone, lfm25_cuda.py:246-262). */
 int cgym_set_pdl(int enabled);
 /* 1 when the device of the current context is compute capability 10.x */
@@ -214,7 +227,9 @@ typedef struct {
   const int64_t* seeds;
   const float* temperatures;
   const int64_t* rng_offsets; /* Philox counter base per slot: row*vocab (batch keying) or 0 */
-  const int32_t* force_eos_at; /* optional: generated position whose token becomes EOS, -1 none */
+  const int32_t* force_eos_at; /* TEST HOOK, NULL in production: generated position whose token is replaced by
+                                  EOS (-1 none); stands in for the sampler wrap the reference's tests use to
+                                  force an EOS (tests/test_text_stops.py:122-126) */
   int32_t* seq_lens;      /* cache length per slot; advanced here for rows in `advance` */
   const float* min_logits; /* optional: per slot, logits below this value cannot be drawn (top-k / top-p
                               support from cgym_filter_thresholds); they still count in the log-prob */
@@ -268,6 +283,8 @@ int cgym_filter_thresholds(float* min_logits, const void* logits, const float* t
  *  - The first call on each device, made with that device current, resolves the address of the
  *    device's copy of the array (this may load the library's device code). Make that call before
  *    any stream capture begins on the device; rows = 0 does only this set-up and launches nothing.
+ *  - EVERY call picks the array of the CURRENT device: make each call with the device that owns
+ *    `stream` (and the tensors) current, or the kernel is handed another device's copy of the array.
  *  - Each call clears the row counters it needs with a memset on `stream` ahead of the kernel; it
  *    calls no allocating or freeing routine of the CUDA runtime.
  *  - Calls on one device share the one array: two calls whose execution can overlap (different
@@ -399,6 +416,11 @@ int cgym_slot_turnover(const cgym_page_pool* pool_rows, int n_slots, const cgym_
 int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout* kv, int n_layers,
                     const int32_t* src_slots, const int32_t* dst_slots, const int32_t* prefix_lens,
                     int n, int32_t* status, cgym_stream_t stream);
+
+/* ---- TEST HOOKS ----------------------------------------------------------------------------------------
+ * The two entry points below exist for tests: they read and write the paged cache through dense fp32 arrays,
+ * standing in for the dense k_cache / v_cache views the reference's tests index directly. Nothing on the
+ * generate path calls them. (cgym_slot_state.force_eos_at above is the third test hook of this ABI.) */
 
 /* Test/debug helper: gather one slot's K or V history into a dense [len][Hkv][D] fp32 array
  * (dequantised), standing in for the dense k_cache/v_cache views the reference tests read

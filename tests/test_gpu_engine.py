@@ -356,3 +356,75 @@ def test_stop_token_sequences_end_generation_at_the_matched_suffix(dev):
                 break
         assert both_lengths[row] == want_len, (row, both_lengths[row], want_len)
     assert both_lengths[6] == 4 and both.finish_reasons.cpu().numpy()[6, 0] == 2
+
+
+def test_decode_step_advances_only_the_active_slots_and_applies_filters(dev):
+    """The step-level API with a strict subset of the cache's slots (reference:
+    src/climbing_gym/inference/lfm25_engine.py:715-738): the other slots keep their length and cache, outputs
+    are indexed like active_slot_ids, and a top-k of 1 under temperature 1 must pick the arg-max."""
+    from climbing_gym_b200.types import LFM25DecodeBatch
+
+    engine = make_engine(dev, dtype=torch.float32)
+    greedy = LFM25SamplingConfig(temperature=0.0, max_new_tokens=4, ignore_eos=True)
+    ids, cu, longest = flat(PROMPTS[:4], dev)
+    want = engine.generate(ids, cu, longest, repeats=1, sampling=greedy).token_ids.cpu().numpy()[:, 0]
+    cache = engine._empty_cache(max_slots=4, max_seq_len=longest + 4)
+    prefix = engine.prefill(ids, cu, longest, max_cache_len=longest + 4, cache=cache)
+    state = engine.fork(prefix, 1)
+    first = prefix.next_token_logits.argmax(-1)
+    before = state.cache.seq_lens.clone()
+    subset = torch.tensor([3, 1], device=dev)
+    part = LFM25DecodeBatch(cache=state.cache, active_slot_ids=subset, prompt_indices=subset, repeat_indices=subset * 0,
+                            alive=torch.ones(2, device=dev, dtype=torch.bool))
+    out = engine.decode_step(part, first[subset], greedy)
+    assert out.token_ids.cpu().tolist() == [int(want[3, 1]), int(want[1, 1])]
+    after = state.cache.seq_lens
+    assert after[[1, 3]].tolist() == (before[[1, 3]] + 1).tolist() and after[[0, 2]].tolist() == before[[0, 2]].tolist()
+    # the untouched slots still decode their own greedy path afterwards
+    rest = LFM25DecodeBatch(cache=state.cache, active_slot_ids=torch.tensor([0, 2], device=dev),
+                            prompt_indices=torch.tensor([0, 2], device=dev), repeat_indices=torch.zeros(2, device=dev),
+                            alive=torch.ones(2, device=dev, dtype=torch.bool))
+    out = engine.decode_step(rest, first[[0, 2]], LFM25SamplingConfig(temperature=1.0, top_k=1, max_new_tokens=4, seed=3))
+    assert out.token_ids.cpu().tolist() == [int(want[0, 1]), int(want[2, 1])], "top-k 1 leaves only the arg-max"
+    with pytest.raises(ValueError, match="one token per active slot"):
+        engine.decode_step(rest, first, greedy)
+    with pytest.raises(ValueError, match="repetition penalty"):
+        engine.decode_step(rest, first[[0, 2]], LFM25SamplingConfig(repetition_penalty=1.2, max_new_tokens=4))
+
+
+def test_stop_table_arena_is_sized_by_an_option_and_recycled(dev):
+    """A stop set with more prefix states than the old fixed arena (31) runs under the default size; a small
+    arena names the option to raise; a session that meets ever new stop rules recycles tables nobody uses."""
+    vocab = 4096
+    plain_engine = make_engine(dev, dtype=torch.float32)
+    free = plain_engine.generate(*flat(PROMPTS[:2], dev), repeats=1,
+                                 sampling=LFM25SamplingConfig(temperature=0.0, max_new_tokens=12)).token_ids.cpu().numpy()[:, 0]
+
+    def chain_table(tokens, states):
+        """`states`-state automaton that matches the token sequence `tokens` (padded with unreachable states)."""
+        table = torch.zeros((states, vocab), dtype=torch.int32)
+        for state, token in enumerate(tokens[:-1]):
+            table[state, int(token)] = state + 1
+        table[len(tokens) - 1, int(tokens[-1])] = 65536
+        return table
+
+    big = chain_table(free[0, :4], 40)  # 40 states > 31
+    out = plain_engine.generate(*flat(PROMPTS[:2], dev), repeats=1,
+                                sampling=LFM25SamplingConfig(temperature=0.0, max_new_tokens=12, stop_table=big))
+    assert out.lengths.cpu().tolist()[0] == [4] and out.finish_reasons.cpu().tolist()[0] == [2]
+    small = make_engine(dev, dtype=torch.float32, stop_states=8)
+    with pytest.raises(ValueError, match="stop_states"):
+        small.generate(*flat(PROMPTS[:2], dev), repeats=1,
+                       sampling=LFM25SamplingConfig(temperature=0.0, max_new_tokens=12, stop_table=big))
+    # 6 requests, each with its own 3-state table, through a 2-slot session whose arena holds 8 states
+    # (1 shared + room for two tables): only recycling lets all of them run
+    with small.generation_session(max_batch_size=2, max_new_tokens=12, cache_len=128) as session:
+        finished = 0
+        for index in range(6):
+            table = chain_table(free[index % 2, :3], 3)
+            session.admit([PROMPTS[index % 2]], [LFM25SamplingConfig(temperature=0.0, max_new_tokens=12, stop_table=table)])
+            for result in session.poll(steps=12):
+                assert result.finish_reason == 2 and len(result.token_ids) == 3
+                session.release(result.handle)
+                finished += 1
+        assert finished == 6
