@@ -498,6 +498,61 @@ class QueueDriver:
         return self.delivered_tokens + self.live_generated()
 
 
+class DeviceQueueDriver(QueueDriver):
+    """The same schedule with the slot turnover on the device: the host parks the next prompts of the queue
+    (``session.enqueue``: prefill into a spare cache row) and reads results; finished requests leave their
+    slots and parked ones enter them inside the decode graph, without a host release / admit between polls."""
+
+    def _occupied(self):
+        return self.session.state.queue["slot_requests"] >= 0
+
+    def _park(self, host: bool):
+        count = self.session.queue_space()
+        if not count:
+            return
+        n = len(self.prompts)
+        ids = [(self.next_request + i) % n for i in range(count)]
+        self.next_request += count
+        if host:
+            device_prompts = [self.pinned[i].to(self.device, non_blocking=True) for i in ids]
+            self.h2d_bytes += sum(self.pinned[i].numel() * 8 for i in ids)
+        else:
+            device_prompts = [self.staged[i] for i in ids]
+        self.session.enqueue([self.prompts[i] for i in ids], [self.samplings[i] for i in ids],
+                             device_prompts=device_prompts)
+
+    def fill(self):
+        self._park(host=False)
+        self.session.poll(steps=1)  # the first turnover deals the parked prompts to the empty slots
+        self._park(host=False)
+
+    def live_generated(self) -> int:
+        return int((self.session.lengths * self._occupied()).sum())
+
+    def _context_tokens(self) -> float:
+        occupied = self._occupied()
+        return float((self.session.entry.cache.seq_lens * occupied).sum()), float(occupied.sum())
+
+    def window(self, host: bool, *, account_kv: bool = False):
+        if account_kv:
+            context, rows = self._context_tokens()
+            before = context + rows
+        results = self.session.poll(steps=self.poll_steps)
+        if account_kv:
+            context, rows = self._context_tokens()
+            self.kv_token_steps += self.poll_steps * (before + context + rows) / 2.0
+        for result in results:
+            n = len(result.token_ids)
+            if result.logprobs is None or not all(math.isfinite(v) for v in result.logprobs):
+                raise RuntimeError("session returned no or non-finite log-probs")
+            self.delivered_tokens += n
+            self.delivered_requests += 1
+            self.d2h_bytes += n * 12 + 4
+        self.d2h_bytes += 4 + self.session.state.queue["result_capacity"]  # queue head + the result index
+        self._park(host)
+        self.windows += 1
+
+
 def run_queue(args) -> dict:
     from climbing_gym_b200 import _native as nv
 
@@ -511,8 +566,14 @@ def run_queue(args) -> dict:
     engine, cfg = impl.build(w["model"], device, options, max_model_len=w["max_model_len"])
     broadcast = broadcast_timed(ranks, engine) if ours else None
     prompts, limits = queue_requests(args.workload, cfg.vocab_size, seed=2000 + rank)
-    session = engine.generation_session(max_batch_size=slots, max_new_tokens=w["cap"], profile_timings=True)
-    driver = QueueDriver(impl, session, prompts, limits, device, poll_steps, ours=ours)
+    on_device = ours and args.scheduler == "device"
+    if on_device:
+        session = engine.generation_session(max_batch_size=slots, max_new_tokens=w["cap"], profile_timings=True,
+                                            queue_capacity=slots)
+        driver = DeviceQueueDriver(impl, session, prompts, limits, device, poll_steps, ours=True)
+    else:
+        session = engine.generation_session(max_batch_size=slots, max_new_tokens=w["cap"], profile_timings=True)
+        driver = QueueDriver(impl, session, prompts, limits, device, poll_steps, ours=ours)
     driver.fill()
     for _ in range(preroll):
         driver.window(host=False)
@@ -573,6 +634,9 @@ def run_queue(args) -> dict:
                    "step": f"{windows_per_step} scheduling windows of a continuously running session: poll({poll_steps}) -> "
                            "deliver finished requests -> release -> admit the next queued requests into the freed slots "
                            f"({windows_per_step * poll_steps} decode steps + the admitted prompts' prefill)",
+                   "scheduler": ("device: finished requests are evicted and parked prompts admitted inside the decode "
+                                 "graph; the host parks the next prompts and reads results once per window"
+                                 if on_device else "host: release and admit from Python at every window"),
                    "preroll": f"{preroll} untimed windows before the warm-up (age mix of a session in mid-queue)",
                    "options": options, "sampling": "temperature 1, full support", "replicas": world,
                    "tokens_per_step": round(sum(generated) / args.steps, 1),
@@ -805,6 +869,8 @@ def main():
                              "on the full workload on the GPU")
     parser.add_argument("--workload", default=DEFAULT_WORKLOAD,
                         choices=sorted([*WORKLOADS, *QUEUE_WORKLOADS, *GROUP_WORKLOADS]))
+    parser.add_argument("--scheduler", default="device", choices=["device", "host"],
+                        help="queue workloads: slot turnover inside the decode graph (default) or from the host")
     parser.add_argument("--batch", type=int, default=0, help="override prompts per GPU (generate workloads)")
     parser.add_argument("--new-tokens", type=int, default=0, help="override sampled tokens per prompt (generate workloads)")
     parser.add_argument("--no-cpu-baseline", action="store_true")

@@ -47,7 +47,8 @@ class SlotState(C.Structure):
                 ("stop_offsets", C.c_void_p), ("stop_table", C.c_void_p), ("ignore_eos", C.c_void_p),
                 ("rng_positions", C.c_void_p), ("seeds", C.c_void_p), ("temperatures", C.c_void_p),
                 ("rng_offsets", C.c_void_p), ("force_eos_at", C.c_void_p), ("seq_lens", C.c_void_p),
-                ("min_logits", C.c_void_p), ("out_rows", C.c_void_p), ("capacity", C.c_int32),
+                ("min_logits", C.c_void_p), ("gumbel_noise", C.c_void_p), ("out_rows", C.c_void_p),
+                ("capacity", C.c_int32),
                 ("eos_token_id", C.c_int32)]
 
 
@@ -81,11 +82,15 @@ SIGNATURES = {
     "cgym_gemm_fp8": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_scatter": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_fp8_scatter": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
+    "cgym_bf16_stream_pack": [_P, _P, _P, _L, _I, _P],
+    "cgym_bf16_stream_unpack": [_P, _P, _P, _P, _L, _I, _P],
+    "cgym_bf16_stream_gemv": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "cgym_slot_turnover": [C.POINTER(PagePool), _I, C.POINTER(SlotState), C.POINTER(AdmitQueue), _P, _P, _P, _I, _I, _I,
                            _I, _P],
     "cgym_step_begin_rows": [C.POINTER(PagePool), _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P],
     "cgym_sample_record": [_P, C.POINTER(SlotState), _P, _P, _P, _I, _I, _I, _P, _P],
     "cgym_sample": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P],
+    "cgym_gumbel_noise": [_P, C.POINTER(SlotState), _I, _I, _P],
     "cgym_sample_static": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "cgym_filter_thresholds": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
     "cgym_topk_head": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],

@@ -688,9 +688,20 @@ static int launch_prefill(void* out, const void* q, const PrefillTiles& tiles, c
   return 0;
 }
 
+bool prefill_attention_tcgen05_supported(const cgym_kv_layout* kv, int n_q_heads);
+int launch_prefill_attention_tcgen05(void* out, const void* q, const int32_t* tile_row0, const int32_t* tile_ntok,
+                                     const int32_t* tile_slot, const int32_t* tile_pos0, const cgym_kv_layout* kv,
+                                     int layer, int n_tiles, int n_q_heads, float scale, int32_t* status,
+                                     cudaStream_t stream);
+
+// bf16 caches take the tcgen05 / TMEM kernel (attention_tcgen05.cu); e4m3 caches, whose operands are widened to
+// fp16 in registers, stay on the mma.sync kernel above.
 int launch_prefill_attention_mma(void* out, const void* q, const int32_t* tile_row0, const int32_t* tile_ntok,
                                  const int32_t* tile_slot, const int32_t* tile_pos0, const cgym_kv_layout* kv, int layer,
                                  int n_tiles, int n_q_heads, float scale, int32_t* status, cudaStream_t stream) {
+  if (prefill_attention_tcgen05_supported(kv, n_q_heads))
+    return launch_prefill_attention_tcgen05(out, q, tile_row0, tile_ntok, tile_slot, tile_pos0, kv, layer, n_tiles,
+                                            n_q_heads, scale, status, stream);
   const PrefillTiles tiles{tile_row0, tile_ntok, tile_slot, tile_pos0};
   const bool fp8 = kv->kv_dtype == CGYM_E4M3;
   return fp8 ? launch_prefill<1, 64>(out, q, tiles, kv, layer, n_tiles, n_q_heads, scale, status, stream)

@@ -112,12 +112,22 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
   // support of the draw: logits below the row's threshold (top-k / top-p) are never candidates
   const float floor = (has_state && st.min_logits != nullptr) ? st.min_logits[row] : -INFINITY;
   // Gumbel-max score of element i (x / 1 is exact, so the division is skipped at temperature 1)
+  // log(-log(u)) of this row, drawn ahead of the logits by gumbel_noise_kernel (same Philox stream, same
+  // float operations, so the draw is bit-identical), or evaluated here
+  const float* noise = (has_state && st.gumbel_noise != nullptr) ? st.gumbel_noise + static_cast<int64_t>(row) * vocab
+                                                                 : nullptr;
   auto consider = [&](int i, float v) {
     if (v < floor) return;
     float score = v;
     if (temperature > 0.0f) {
-      const float u = fmaxf(uniform_from_word(philox_first_word(base + static_cast<uint32_t>(i), k0, k1)), 1.0e-30f);
-      score = (temperature == 1.0f ? v : __fdiv_rn(v, t_div)) - logf(-logf(u));
+      float g;
+      if (noise != nullptr) {
+        g = noise[i];
+      } else {
+        const float u = fmaxf(uniform_from_word(philox_first_word(base + static_cast<uint32_t>(i), k0, k1)), 1.0e-30f);
+        g = logf(-logf(u));
+      }
+      score = (temperature == 1.0f ? v : __fdiv_rn(v, t_div)) - g;
     }
     if (score > mine.score || (score == mine.score && i < mine.index)) { mine.score = score; mine.index = i; }
   };
@@ -228,6 +238,41 @@ sample_kernel(const T* __restrict__ logits, cgym_slot_state st, bool has_state,
   st.alive[row] = reason == 0;
   st.pending[row] = reason == 0;
   st.input_tokens[row] = token;
+}
+
+// The Gumbel noise of a step does not depend on the step's logits: key and counter come from the row's
+// seed, its position and the column. This kernel evaluates log(-log(u)) for every alive, tempered row while
+// the layers of the step are still running (it is launched on a side stream at the start of the step: the
+// ten Philox rounds per logit are ALU work that fits beside the latency-bound GEMM chain), and the sampler
+// then only subtracts it. Grid (rows, parts); eight columns per thread and iteration, 16-byte stores.
+__global__ void __launch_bounds__(SAMPLE_THREADS)
+gumbel_noise_kernel(float* __restrict__ noise, cgym_slot_state st, int vocab) {
+  const int row = blockIdx.x, part = blockIdx.y, parts = gridDim.y;
+  if (!st.alive[row] || !(st.temperatures[row] > 0.0f)) return;
+  const uint64_t key = (static_cast<uint64_t>(st.seeds[row]) +
+                        static_cast<uint64_t>(st.rng_positions[row]) * 0x9E3779B97F4A7C15ull) & 0x7FFFFFFFFFFFFFFFull;
+  const uint32_t k0 = static_cast<uint32_t>(key), k1 = static_cast<uint32_t>(key >> 32);
+  const uint32_t base = st.rng_offsets != nullptr ? static_cast<uint32_t>(st.rng_offsets[row]) : 0u;
+  float* out = noise + static_cast<int64_t>(row) * vocab;
+  auto draw = [&](int i) {
+    const float u = fmaxf(uniform_from_word(philox_first_word(base + static_cast<uint32_t>(i), k0, k1)), 1.0e-30f);
+    return logf(-logf(u));
+  };
+  if (vocab % 8 == 0 && (reinterpret_cast<uintptr_t>(noise) & 15u) == 0) {
+    const int groups = vocab / 8, per_part = (groups + parts - 1) / parts;
+    const int g_end = min(groups, (part + 1) * per_part);
+    for (int g = part * per_part + threadIdx.x; g < g_end; g += SAMPLE_THREADS) {
+      float4 a, b;
+      a.x = draw(g * 8), a.y = draw(g * 8 + 1), a.z = draw(g * 8 + 2), a.w = draw(g * 8 + 3);
+      b.x = draw(g * 8 + 4), b.y = draw(g * 8 + 5), b.z = draw(g * 8 + 6), b.w = draw(g * 8 + 7);
+      reinterpret_cast<float4*>(out + g * 8)[0] = a;
+      reinterpret_cast<float4*>(out + g * 8)[1] = b;
+    }
+  } else {
+    const int chunk = (vocab + parts - 1) / parts;
+    const int begin = part * chunk, end = min(vocab, begin + chunk);
+    for (int i = begin + threadIdx.x; i < end; i += SAMPLE_THREADS) out[i] = draw(i);
+  }
 }
 
 static int pick_parts(int rows, int vocab, const float* workspace) {
@@ -590,6 +635,18 @@ extern "C" int cgym_sample_record(const void* logits, const cgym_slot_state* sta
   else
     return fail("sample_record: unsupported logits dtype %d", dtype);
   return check_launch("sample_record");
+}
+
+extern "C" int cgym_gumbel_noise(float* noise, const cgym_slot_state* state, int n_slots, int vocab,
+                                 cgym_stream_t stream) {
+  CGYM_REQUIRE(noise != nullptr && state != nullptr && n_slots >= 0 && vocab > 0, "gumbel_noise: bad arguments");
+  CGYM_REQUIRE(state->seeds && state->temperatures && state->rng_positions && state->alive,
+               "gumbel_noise: slot state is incomplete");
+  if (n_slots == 0) return 0;
+  int parts = vocab / 4096;
+  parts = parts < 1 ? 1 : (parts > SAMPLE_MAX_PARTS ? SAMPLE_MAX_PARTS : parts);
+  gumbel_noise_kernel<<<dim3(n_slots, parts), SAMPLE_THREADS, 0, as_stream(stream)>>>(noise, *state, vocab);
+  return check_launch("gumbel_noise");
 }
 
 extern "C" int cgym_sample(int64_t* tokens, float* logprobs, const void* logits, const int64_t* seeds,

@@ -60,6 +60,7 @@ class SlotState:
 
         self.eos = eos
         self.queue = None  # device-resident admission queue (allocate_queue)
+        self.noise = None  # [n_slots][vocab] fp32 Gumbel noise of the current step (allocate_noise)
         self._build_structs()
         self.head_k, self.head_ids, self.head_logprobs = 0, None, None
         self.penalties, self.seen, self.penalised = None, None, None
@@ -73,11 +74,16 @@ class SlotState:
                 nv.ptr(self.reasons), nv.ptr(self.alive), nv.ptr(self.pending), nv.ptr(self.input_tokens),
                 nv.ptr(self.stop_states), nv.ptr(self.stop_offsets), nv.ptr(self.stop_table), nv.ptr(self.ignore_eos),
                 nv.ptr(self.rng_positions), nv.ptr(self.seeds), nv.ptr(self.temperatures), nv.ptr(self.rng_offsets),
-                nv.ptr(self.force_eos_at), nv.ptr(self.seq_lens), nv.ptr(min_logits), nv.ptr(out_rows), self.capacity,
-                self.eos)
+                nv.ptr(self.force_eos_at), nv.ptr(self.seq_lens), nv.ptr(min_logits), nv.ptr(self.noise),
+                nv.ptr(out_rows), self.capacity, self.eos)
 
         self.struct = struct(None)                      # full-support sampling
         self.struct_filtered = struct(self.min_logits)  # draws restricted to logits >= min_logits[slot]
+
+    def allocate_noise(self) -> None:
+        """Buffer for the step's Gumbel noise, drawn beside the layers (cgym_gumbel_noise)."""
+        self.noise = torch.zeros((self.n_slots, self.vocab), device=self.lengths.device, dtype=torch.float32)
+        self._build_structs()
 
     def allocate_queue(self, queue_capacity: int, result_capacity: int, n_rows: int, logits_dtype) -> None:
         """Device-resident admission queue and per-request result rows (cgym_admit_queue): parked prompts wait
@@ -249,9 +255,11 @@ class B200Decoder:
         self.max_graphs = max_graphs
         self.max_prefill_tokens = max_prefill_tokens
         self.finish_check_interval = finish_check_interval
+        # Accepted for the reference's constructor contract and always in force here: a finished row is inactive
+        # in every kernel of the step (no KV append, no attention over its history), which is what the
+        # reference's flag switches on by zeroing the row's length (src/climbing_gym/inference/lfm25_cuda.py:361-365).
         self.skip_finished_attention = bool(skip_finished_attention)
         self.bf16_weight_packing = bool(bf16_weight_packing) and engine.dtype == torch.bfloat16
-        self.packed_weights: dict = {}  # the lossless batch-1 bf16 stream of the reference has no B200 analogue
         self.fp8_mlp, self.fp8_kv = bool(fp8_mlp), bool(fp8_kv)
         self.adaptive_batching, self.fp8_lm_head = bool(adaptive_batching), bool(fp8_lm_head)
         self.page_size = page_size
@@ -274,7 +282,9 @@ class B200Decoder:
                                   fp8_lm_head=self.fp8_lm_head)
         self.graphs: OrderedDict = OrderedDict()
         self._active_session = None
-        self._capture_stream = torch.cuda.Stream(device=engine.device)
+        # the step's own kernels go first wherever both streams have work ready
+        self._capture_stream = torch.cuda.Stream(device=engine.device, priority=-1)
+        self._noise_stream = torch.cuda.Stream(device=engine.device)
         self.debug_force_eos_at = None  # test hook: per-row generated position forced to EOS
         # when set, generate() brackets its decode-graph replays with CUDA events on the launching
         # stream and appends (start, end, replays) here; resolved by the caller after a synchronize
@@ -285,14 +295,36 @@ class B200Decoder:
     def fp8_weights(self) -> dict:
         return self.runner.fp8_weights
 
+    @property
+    def packed_weights(self) -> dict:
+        """Lossless 12-bit bf16 streams of the matrices a single-request step reads (PackedBF16Weight)."""
+        return self.runner.packed_weights
+
+    def _prepare_weights(self) -> None:
+        """Encoded copies of the vocabulary head and the MLP matrices for batch-1 graphs (reference:
+        src/climbing_gym/inference/lfm25_cuda.py:108-122): they dominate single-request decode traffic."""
+        if not self.bf16_weight_packing or self.runner.packed_weights:
+            return
+        from .weights import PackedBF16Weight
+
+        weights = self.engine.weights
+        matrices = [] if self.fp8_lm_head else [weights.lm_head_weight]
+        if not self.fp8_mlp:
+            for layer in weights.layers:
+                matrices.extend((layer.w13_weight, layer.w2_weight))
+        self.runner.packed_weights = {id(w): PackedBF16Weight.from_weight(w) for w in matrices
+                                      if w.size(1) % 2 == 0 and w.size(1) <= 16384}
+
     def clear(self) -> None:
         if self._active_session is not None:
             self._active_session.close()
         self.graphs.clear()
-        self.packed_weights.clear()
+        self.runner.packed_weights.clear()
         self.runner.fp8_weights.clear()
 
     def refresh_weights(self) -> None:
+        for packed in self.runner.packed_weights.values():
+            packed.refresh()
         self.runner.refresh_fp8()
 
     # ---- graph entries ------------------------------------------------------------------------------
@@ -306,8 +338,27 @@ class B200Decoder:
             self._turnover(entry)
         nv.call("cgym_step_begin", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(state.pending), nv.ptr(state.active),
                 None, None, nv.ptr(kv_lens), n, nv.ptr(cache.status), stream)
+        self._launch_noise(entry)
         self.runner.decode_step(entry.bufs, cache, state.input_tokens, state.active, entry.logits, kv_lens=kv_lens)
+        self._join_noise(entry)
         self._sample(entry, nv.ptr(state.active), stream)
+
+    def _launch_noise(self, entry: _DecodeGraph) -> None:
+        """The step's Gumbel noise depends on the slot state alone (seed, position, temperature), not on the
+        logits: draw it now on a side stream, beside the layers, and let the sampler subtract it. The ten
+        Philox rounds per logit otherwise sit on the critical path after the LM head (0.1 ms at 256 rows)."""
+        state = entry.state
+        if state.noise is None:
+            return
+        main = torch.cuda.current_stream(self.engine.device)
+        self._noise_stream.wait_stream(main)
+        with torch.cuda.stream(self._noise_stream):
+            nv.call("cgym_gumbel_noise", nv.ptr(state.noise), C.byref(state.struct), state.n_slots, state.vocab,
+                    nv.stream_ptr(self.engine.device))
+
+    def _join_noise(self, entry: _DecodeGraph) -> None:
+        if entry.state.noise is not None:
+            torch.cuda.current_stream(self.engine.device).wait_stream(self._noise_stream)
 
     def _turnover(self, entry: _DecodeGraph) -> None:
         """Evict finished requests and admit parked ones, on the device (cgym_slot_turnover)."""
@@ -339,6 +390,8 @@ class B200Decoder:
 
     def _sample_only(self, entry: _DecodeGraph) -> None:
         """First token of freshly prefetched rows: sample from the prefill logits, no forward."""
+        self._launch_noise(entry)
+        self._join_noise(entry)
         self._sample(entry, None, nv.stream_ptr(self.engine.device))
 
     @torch.inference_mode()
@@ -360,6 +413,10 @@ class B200Decoder:
         if len(self.graphs) >= self.max_graphs:
             self.graphs.popitem(last=False)
         self.runner.prepare_fp8()
+        if batch_size == 1:
+            self._prepare_weights()
+        elif not any(existing[0] == 1 for existing in self.graphs):
+            self.runner.packed_weights.clear()  # no surviving graph uses the single-request copies
         spare, n_pages = (self.snapshot_rows if masked else 0), None
         spare += queue_capacity  # one parked row per queue entry
         if spare:
@@ -375,6 +432,8 @@ class B200Decoder:
             state.allocate_heads(head_k, head_positions)
         if penalised:
             state.allocate_penalty()
+        if engine.config.vocab_size >= 4096:  # smaller vocabularies: the sampler draws the noise itself
+            state.allocate_noise()
         if queue_capacity:
             # results stay addressable until the host has read them: room for every request that can be
             # parked or running at once, twice over (finished requests wait for the next poll)
@@ -438,9 +497,12 @@ class B200Decoder:
         nv.call("cgym_step_begin_rows", cache.pool, nv.ptr(cache.seq_lens), nv.ptr(state.pending),
                 nv.ptr(state.input_tokens), nv.ptr(slots), nv.ptr(active), nv.ptr(state.active), nv.ptr(tokens),
                 nv.ptr(positions), nv.ptr(kv_lens), rows, cache.n_slots, nv.ptr(cache.status), stream)
+        if sample:
+            self._launch_noise(entry)
         self.runner.decode_step(bufs, cache, tokens, active, entry.logits, slots=slots, rows=rows, kv_lens=kv_lens,
                                 positions=positions, logits_rows=slots)
         if sample:
+            self._join_noise(entry)
             self._sample(entry, nv.ptr(state.active), stream)
 
     @torch.inference_mode()

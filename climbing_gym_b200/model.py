@@ -61,6 +61,7 @@ class LFM25Runner:
         self.gemm_impl = gemm_impl
         self.attn_impl = 0  # 0 auto, 1 CUDA-core kernel, 2 tensor-core kernel (see cgym_paged_attention)
         self.fp8_weights: dict[int, PackedFP8Weight] = {}
+        self.packed_weights: dict = {}  # id(weight) -> PackedBF16Weight, used by single-row steps only
         self.scale = float(self.cfg.head_dim ** -0.5)
         if (fp8_mlp or fp8_lm_head) and weights.dtype != torch.bfloat16:
             raise ValueError("FP8 projections require bfloat16 weights")
@@ -82,6 +83,10 @@ class LFM25Runner:
     # ---- single kernels --------------------------------------------------------------------------
     def _gemm(self, y, x, w, rows, bufs, status, row_mask=None, row_map=None):
         n, k = w.shape
+        packed = self.packed_weights.get(id(w)) if rows == 1 and row_map is None else None
+        if packed is not None:  # single-request decode: the 12-bit weight stream (lfm25_cuda.py:124-126)
+            packed.linear(x[:1], out=y[:1], row_mask=row_mask)
+            return
         nv.call("cgym_gemm_scatter", nv.ptr(y), nv.ptr(x), nv.ptr(w), nv.ptr(row_mask), nv.ptr(row_map), rows, n, k,
                 self.dt, self.gemm_impl, nv.ptr(bufs.gemm_ws), bufs.gemm_ws.numel(), nv.ptr(status),
                 nv.stream_ptr(w.device))

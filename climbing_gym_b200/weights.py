@@ -283,6 +283,46 @@ class PackedFP8Weight:
                 nv.BF16, nv.stream_ptr(self.original.device))
 
 
+class PackedBF16Weight:
+    """Lossless 12-bit stream of a bf16 matrix for single-request decode (reference:
+    src/climbing_gym/inference/lfm25_bf16.py:61-102). ``original`` stays the matrix every other path uses;
+    ``mantissa`` / ``exponent`` are refreshed in place after a policy sync, so captured graphs keep their
+    addresses."""
+
+    def __init__(self, original: torch.Tensor, base: int = 110):
+        if original.dtype != torch.bfloat16 or not original.is_cuda or not original.is_contiguous():
+            raise ValueError("lossless BF16 packing requires contiguous CUDA BF16 weights")
+        if original.ndim != 2 or original.size(1) % 2:
+            raise ValueError("lossless BF16 packing requires a matrix with even input width")
+        self.original, self.base = original, base
+        self.mantissa = torch.empty(original.shape, device=original.device, dtype=torch.uint8)
+        self.exponent = torch.empty((original.size(0), original.size(1) // 2), device=original.device, dtype=torch.uint8)
+        self.refresh()
+
+    @classmethod
+    def from_weight(cls, weight: torch.Tensor) -> "PackedBF16Weight":
+        return cls(weight)
+
+    def refresh(self) -> None:
+        nv.call("cgym_bf16_stream_pack", nv.ptr(self.mantissa), nv.ptr(self.exponent), nv.ptr(self.original),
+                self.original.numel(), self.base, nv.stream_ptr(self.original.device))
+
+    def unpack(self) -> torch.Tensor:
+        out = torch.empty_like(self.original)
+        nv.call("cgym_bf16_stream_unpack", nv.ptr(out), nv.ptr(self.original), nv.ptr(self.mantissa),
+                nv.ptr(self.exponent), out.numel(), self.base, nv.stream_ptr(out.device))
+        return out
+
+    def linear(self, x: torch.Tensor, out: torch.Tensor | None = None, row_mask: torch.Tensor | None = None) -> torch.Tensor:
+        rows, width = self.original.shape
+        if tuple(x.shape) != (1, width) or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise ValueError("packed BF16 GEMV requires one contiguous BF16 input row")
+        out = torch.empty((1, rows), device=x.device, dtype=x.dtype) if out is None else out
+        nv.call("cgym_bf16_stream_gemv", nv.ptr(out), nv.ptr(x), nv.ptr(self.original), nv.ptr(self.mantissa),
+                nv.ptr(self.exponent), nv.ptr(row_mask), rows, width, self.base, nv.stream_ptr(x.device))
+        return out
+
+
 def describe_lfm25_checkpoint(model_dir) -> dict:
     config = LFM2Config.from_pretrained(model_dir)
     attention = [i for i, kind in enumerate(config.layer_types) if kind == "full_attention"]

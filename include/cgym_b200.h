@@ -208,6 +208,20 @@ int cgym_gemm_fp8_scatter(void* y, const uint8_t* xq, const float* x_scales, con
                           int K, int impl, void* workspace, int64_t workspace_bytes, int32_t* status,
                           cgym_stream_t stream);
 
+/* PackedBF16Weight (lfm25_bf16.py:17-102): a lossless 12-bit stream of a bf16 matrix for single-request
+ * decode. Per weight: one byte of sign + mantissa, and a 4-bit exponent code (two per byte): code c in 1..15
+ * stands for exponent base + c - 1, code 0 for "read the original value" (every bit pattern stays exact).
+ * pack fills mantissa [numel] and exponent [numel / 2] from w (bf16, numel even); unpack rebuilds the bf16
+ * matrix bit for bit; gemv computes y[N] = w[N, K] . x[K] from the stream (x, y bf16, fp32 accumulation, K
+ * even and <= 16384, the original w still needed for code 0; row_mask (uint8[1], optional): 0 leaves y
+ * untouched, like cgym_gemm's row mask). The reference's base is 110. */
+int cgym_bf16_stream_pack(uint8_t* mantissa, uint8_t* exponent, const void* w, int64_t numel, int base,
+                          cgym_stream_t stream);
+int cgym_bf16_stream_unpack(void* out, const void* w, const uint8_t* mantissa, const uint8_t* exponent,
+                            int64_t numel, int base, cgym_stream_t stream);
+int cgym_bf16_stream_gemv(void* y, const void* x, const void* w, const uint8_t* mantissa, const uint8_t* exponent,
+                          const uint8_t* row_mask, int N, int K, int base, cgym_stream_t stream);
+
 /* Per-slot request state of the slot scheduler (LFM25GenerationSession's row tensors,
  * lfm25_session.py:147-167). All arrays are indexed by slot. */
 typedef struct {
@@ -233,6 +247,9 @@ typedef struct {
   int32_t* seq_lens;      /* cache length per slot; advanced here for rows in `advance` */
   const float* min_logits; /* optional: per slot, logits below this value cannot be drawn (top-k / top-p
                               support from cgym_filter_thresholds); they still count in the log-prob */
+  const float* gumbel_noise; /* optional, [n_slots][vocab] fp32: log(-log(u)) of this step's draw for every alive,
+                                tempered slot, filled by cgym_gumbel_noise earlier in the step; NULL = the sampler
+                                evaluates the Philox stream itself (same values either way) */
   const int32_t* out_rows; /* optional: slot s writes its tokens / log-probs to row out_rows[s] of `tokens` /
                               `logprobs` (which then hold more rows than slots) instead of row s: with
                               device-side slot turnover a request keeps its row after its slot is reused */
@@ -251,6 +268,14 @@ typedef struct {
 int cgym_sample_record(const void* logits, const cgym_slot_state* state, const uint8_t* advance,
                        int64_t* sampled_out, float* logp_out, int n_slots, int vocab, int dtype,
                        float* workspace, cgym_stream_t stream);
+
+/* The noise half of the Gumbel-max draw, ahead of the logits: noise[slot][col] = log(-log(u)) with u the
+ * reference sampler's uniform for (seed, rng position, offset + col) (tl.rand in _partial_sample,
+ * lfm25_sampling.py:17-26), for every slot that is alive with temperature > 0 (other rows are left alone).
+ * It depends on the slot state only, so a decode step launches it on a side stream at the start of the step,
+ * beside the layers, and passes the buffer to cgym_sample_record through cgym_slot_state.gumbel_noise; the
+ * draw is bit-identical to the sampler evaluating the stream itself. */
+int cgym_gumbel_noise(float* noise, const cgym_slot_state* state, int n_slots, int vocab, cgym_stream_t stream);
 
 /* Stand-alone sampler (sample_logits / RowSampler.sample, lfm25_sampling.py:61-123). */
 int cgym_sample(int64_t* tokens, float* logprobs, const void* logits, const int64_t* seeds,

@@ -196,3 +196,42 @@ def test_graph_cache_rounds_capacities_and_evicts_least_recently_used(dev):
     assert decoder.graphs[(4, 128, False)] is entry and torch.equal(again.token_ids, repeat.token_ids)
     engine.release_inference_buffers()
     assert not decoder.graphs and not decoder.fp8_weights
+
+
+def test_single_request_graphs_stream_packed_weights_and_drop_them_with_the_graph(dev):
+    """Batch-1 decode reads the vocabulary head and the MLP matrices through the lossless 12-bit stream; the
+    copies follow a policy sync in place and are released when no batch-1 graph survives (reference:
+    tests/test_lfm25_cuda.py:256-275, 383-396)."""
+    engine = make_engine(dev, torch.bfloat16, max_graphs=1, max_prefill_tokens=128)
+    decoder = engine._cuda_decoder
+    sampling = LFM25SamplingConfig(temperature=0.0, max_new_tokens=6, ignore_eos=True)
+    one = flat([[1, 2, 3]], dev)
+    original = engine.generate(*one, repeats=1, sampling=sampling)
+    assert decoder.packed_weights, "a batch-1 graph prepares the packed copies"
+    n_layers = len(engine.weights.layers)
+    assert len(decoder.packed_weights) == 2 * n_layers + 1
+    plain = make_engine(dev, torch.bfloat16, max_graphs=1, bf16_weight_packing=False)
+    unpacked = plain.generate(*one, repeats=1, sampling=sampling)
+    assert not plain._cuda_decoder.packed_weights
+    # lossless weights: only the summation order differs from the tensor-core GEMM
+    assert float((original.logprobs - unpacked.logprobs).abs().max()) <= 2e-2
+    assert float((original.token_ids == unpacked.token_ids).float().mean()) >= 0.8
+    addresses = [p.mantissa.data_ptr() for p in decoder.packed_weights.values()]
+    cfg = synthetic.tiny_config()
+
+    class Model:
+        config = cfg
+
+        def state_dict(self):
+            return {k: torch.from_numpy(v) for k, v in synthetic.make_state_dict(cfg, seed=1, untied_head=True).items()}
+
+    engine.sync_from_model(Model())
+    assert addresses == [p.mantissa.data_ptr() for p in decoder.packed_weights.values()]
+    for packed in decoder.packed_weights.values():
+        assert torch.equal(packed.unpack().view(torch.int16), packed.original.view(torch.int16))
+    synced = engine.generate(*one, repeats=1, sampling=sampling)
+    assert not torch.equal(synced.token_ids, original.token_ids)
+    engine.generate(*flat([[1, 2, 3]] * 64, dev), repeats=1, sampling=sampling)
+    assert not decoder.packed_weights, "the 64-row graph evicted the only batch-1 graph"
+    repeated = engine.generate(*one, repeats=1, sampling=sampling)
+    assert decoder.packed_weights and torch.equal(repeated.token_ids, synced.token_ids)

@@ -629,3 +629,41 @@ def test_target_logprobs(dev):
     logits_dev, targets_dev = bf(logits_np, dev), torch.from_numpy(targets_np).to(dev)
     nv.call("cgym_target_logprobs", nv.ptr(out), nv.ptr(logits_dev), nv.ptr(targets_dev), 7, 5000, nv.BF16, stream())
     assert np.allclose(out.cpu().numpy(), OracleEngine.logprob_of(logits_np, targets_np), atol=3e-6)
+
+
+# ------------------------------------------------------------------------------------------ 12-bit bf16 weight stream
+def test_bf16_stream_preserves_every_bit_pattern_and_refreshes(dev):
+    """All 65,536 bf16 bit patterns (rare exponents, signed zeros, infinities, NaN payloads) survive the packed
+    stream; refresh re-encodes in place (reference: tests/test_lfm25_cuda.py:66-78)."""
+    from climbing_gym_b200.weights import PackedBF16Weight
+
+    bits = torch.arange(65536, device=dev, dtype=torch.int32).to(torch.int16).reshape(256, 256)
+    weights = bits.view(torch.bfloat16).clone()
+    packed = PackedBF16Weight.from_weight(weights)
+    assert torch.equal(packed.unpack().view(torch.int16), bits)
+    addresses = (packed.mantissa.data_ptr(), packed.exponent.data_ptr())
+    weights.copy_(weights.flip(0))
+    packed.refresh()
+    assert torch.equal(packed.unpack().view(torch.int16), weights.view(torch.int16))
+    assert addresses == (packed.mantissa.data_ptr(), packed.exponent.data_ptr())
+    # the stream really is 12 bits per weight
+    assert packed.mantissa.numel() + packed.exponent.numel() == weights.numel() * 3 // 2
+
+
+@pytest.mark.parametrize("width", (128, 130, 2048, 10752))
+def test_bf16_stream_gemv_matches_the_unpacked_product(dev, width):
+    from climbing_gym_b200.weights import PackedBF16Weight
+
+    rng = np.random.default_rng(319 + width)
+    w_np = round_bf16(rng.standard_normal((256, width)) * 0.025)
+    w_np[0, :4] = round_bf16(np.array([0.0, 1e-20, 1000.0, -1e-20]))  # values outside the coded exponent band
+    x_np = round_bf16(rng.standard_normal((1, width)))
+    weights, x = bf(w_np, dev), bf(x_np, dev)
+    packed = PackedBF16Weight.from_weight(weights)
+    assert torch.equal(packed.unpack().view(torch.int16), weights.view(torch.int16))
+    want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
+    got = f32(packed.linear(x))
+    assert_gemm_close(got, want, exact_fraction=0.97, what=f"stream gemv {width}")
+    kept = torch.full((1, 256), 5.0, device=dev, dtype=torch.bfloat16)
+    packed.linear(x, out=kept, row_mask=torch.zeros(1, device=dev, dtype=torch.uint8))
+    assert bool((kept == 5.0).all()), "a masked row is not written"
