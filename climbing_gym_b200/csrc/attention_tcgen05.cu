@@ -9,14 +9,18 @@
 //     P  = exp2(scale * S - running max), rounded to bf16  one thread per row (a TMEM lane is a row, so the
 //                                                          row max and row sum need no shuffles), written to
 //                                                          shared memory in the 128-byte-swizzled operand layout
-//     PV [128 x 64 dims]   = P [128 x 64 tokens] . V       tcgen05.mma, PV in TMEM
-//     O  = (O + PV of the previous page) * exp2(old max - new max)   in registers, one row per thread
+//     O  [128 x 64 dims]  += P [128 x 64 tokens] . V       tcgen05.mma, O accumulates in TMEM over the pages
 // The cache stores a (page, head) block as K [token][dim] followed by V^T [dim][token], rows of 128 bytes whose
 // 16-byte chunks are XOR-ed with the row index: exactly the shared-memory image of a K-major SWIZZLE_128B
 // operand, so a block is staged with ONE linear cp.async.bulk and used as the B operand of both products
-// without any rearrangement. S and PV are double-buffered in TMEM (4 x 64 = 256 columns), P in shared memory,
-// so the tensor pipe computes S of page i + 1 while the softmax threads work on page i and P.V of page i
-// runs while they read S of page i + 1.
+// without any rearrangement. S is double-buffered in TMEM and P in shared memory, so the tensor pipe computes
+// S of page i + 1 and P.V of page i while the softmax threads work on S of page i + 1.
+//
+// O stays in TMEM for the whole tile: P is taken relative to a reference maximum per row that is only moved
+// when the row's running maximum has outgrown it by more than 2^8 (P <= 256 is exact enough in bf16 and far
+// from overflow), so the usual per-page rescaling of O disappears. When a row does move its reference, its
+// thread waits for the P.V products in flight (they write every row), rescales ITS lane of O in place
+// (tcgen05.ld / tcgen05.st; the next P.V cannot start before this thread has delivered its P row) and goes on.
 //
 // Warp roles (192 threads): 0 = page producer, 1 = MMA issuer + TMEM owner, 2..5 = one row per thread.
 // Every mbarrier wait is bounded (two seconds of %globaltimer): on expiry the CTA raises
@@ -34,7 +38,8 @@ constexpr int PAGE_BYTES = 2 * P * D * 2;   // K + V^T of one (page, head), bf16
 constexpr int Q_BYTES = ROWS * D * 2;       // 16 KB
 constexpr int P_BYTES = ROWS * P * 2;       // 16 KB
 constexpr int SMEM_BYTES = 1024 + Q_BYTES + 2 * P_BYTES + KV_STAGES * PAGE_BYTES;
-constexpr int TMEM_COLS = 256;              // S0, S1, PV0, PV1: 64 fp32 columns each
+constexpr int TMEM_COLS = 256;              // S0, S1, O: 64 fp32 columns each (allocations are powers of two)
+constexpr float RESCALE_SLACK = 8.0f;       // log2 of the largest P a row may reach before its reference moves
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -118,6 +123,27 @@ __device__ __forceinline__ void tmem_load_row(uint32_t taddr, float (&v)[64]) {
 #pragma unroll
   for (int j = 0; j < 64; ++j) v[j] = __uint_as_float(r[j]);
 }
+__device__ __forceinline__ void tmem_store_row(uint32_t taddr, const float (&v)[64]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr + 32 * h), "r"(__float_as_uint(v[32 * h + 0])), "r"(__float_as_uint(v[32 * h + 1])),
+          "r"(__float_as_uint(v[32 * h + 2])), "r"(__float_as_uint(v[32 * h + 3])), "r"(__float_as_uint(v[32 * h + 4])),
+          "r"(__float_as_uint(v[32 * h + 5])), "r"(__float_as_uint(v[32 * h + 6])), "r"(__float_as_uint(v[32 * h + 7])),
+          "r"(__float_as_uint(v[32 * h + 8])), "r"(__float_as_uint(v[32 * h + 9])), "r"(__float_as_uint(v[32 * h + 10])),
+          "r"(__float_as_uint(v[32 * h + 11])), "r"(__float_as_uint(v[32 * h + 12])), "r"(__float_as_uint(v[32 * h + 13])),
+          "r"(__float_as_uint(v[32 * h + 14])), "r"(__float_as_uint(v[32 * h + 15])), "r"(__float_as_uint(v[32 * h + 16])),
+          "r"(__float_as_uint(v[32 * h + 17])), "r"(__float_as_uint(v[32 * h + 18])), "r"(__float_as_uint(v[32 * h + 19])),
+          "r"(__float_as_uint(v[32 * h + 20])), "r"(__float_as_uint(v[32 * h + 21])), "r"(__float_as_uint(v[32 * h + 22])),
+          "r"(__float_as_uint(v[32 * h + 23])), "r"(__float_as_uint(v[32 * h + 24])), "r"(__float_as_uint(v[32 * h + 25])),
+          "r"(__float_as_uint(v[32 * h + 26])), "r"(__float_as_uint(v[32 * h + 27])), "r"(__float_as_uint(v[32 * h + 28])),
+          "r"(__float_as_uint(v[32 * h + 29])), "r"(__float_as_uint(v[32 * h + 30])), "r"(__float_as_uint(v[32 * h + 31]))
+        : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -140,7 +166,7 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
                                  int32_t* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_q, bar_kv_full[KV_STAGES], bar_kv_empty[KV_STAGES];
-  __shared__ __align__(8) uint64_t bar_s_full[2], bar_s_free[2], bar_p_full[2], bar_pv_full[2], bar_pv_free[2];
+  __shared__ __align__(8) uint64_t bar_s_full[2], bar_s_free[2], bar_p_full[2], bar_pv_done[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -161,8 +187,7 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
       bar_init(smem_u32(&bar_s_full[b]), 1);
       bar_init(smem_u32(&bar_s_free[b]), 128);
       bar_init(smem_u32(&bar_p_full[b]), 128);
-      bar_init(smem_u32(&bar_pv_full[b]), 1);
-      bar_init(smem_u32(&bar_pv_free[b]), 128);
+      bar_init(smem_u32(&bar_pv_done[b]), 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -175,7 +200,7 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_slot;
-  const uint32_t tmem_s[2] = {tmem, tmem + 64}, tmem_pv[2] = {tmem + 128, tmem + 192};
+  const uint32_t tmem_s[2] = {tmem, tmem + 64}, tmem_o = tmem + 128;
 
   if (warp == 0) {
     // ---- page producer: one linear bulk copy per (page, head) block ----
@@ -205,15 +230,14 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
                              (static_cast<uint32_t>(128 >> 4) << 24);
       const uint64_t dq = operand_desc(q_tile);
       bool ok = bar_wait(smem_u32(&bar_q), 0, &abort_flag);
-      auto issue_pv = [&](int i) {  // PV[i % 2] = P[i % 2] . V of page i
+      auto issue_pv = [&](int i) {  // O += P[i % 2] . V of page i
         const int b = i & 1, s = i % KV_STAGES;
         if (!bar_wait(smem_u32(&bar_p_full[b]), (i >> 1) & 1, &abort_flag)) return false;
-        if (i >= 2 && !bar_wait(smem_u32(&bar_pv_free[b]), ((i >> 1) & 1) ^ 1, &abort_flag)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t dp = operand_desc(p_tile + b * P_BYTES), dv = operand_desc(kv_ring + s * PAGE_BYTES + P * D * 2);
 #pragma unroll
-        for (int k = 0; k < P / 16; ++k) mma_bf16(tmem_pv[b], dp + 2 * k, dv + 2 * k, idesc, k > 0 ? 1u : 0u);
-        mma_commit(smem_u32(&bar_pv_full[b]));
+        for (int k = 0; k < P / 16; ++k) mma_bf16(tmem_o, dp + 2 * k, dv + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        mma_commit(smem_u32(&bar_pv_done[b]));
         mma_commit(smem_u32(&bar_kv_empty[s]));  // the page is free once both products have read it
         return true;
       };
@@ -250,10 +274,7 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       bar_arrive(smem_u32(&bar_q));
     }
-    float o[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) o[d] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
+    float ref = -INFINITY, l = 0.0f;  // reference maximum (log2 domain) the row's P values are taken against
     const float scale_log2 = scale * 1.4426950408889634f;
     bool ok = true;
     for (int i = 0; i < n_pages; ++i) {
@@ -264,7 +285,7 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
       tmem_load_row(tmem_s[b] + lane_addr, s);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       bar_arrive(smem_u32(&bar_s_free[b]));
-      // causal mask (only the pages that straddle the row's limit need it), running max of the raw scores
+      // causal mask (only the pages that straddle the row's limit need it), maximum of the raw scores
       const int first = i * P;
       if (first + P > limit) {
 #pragma unroll
@@ -274,10 +295,27 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
       float row_max = s[0];
 #pragma unroll
       for (int j = 1; j < P; ++j) row_max = fmaxf(row_max, s[j]);
-      const float m_new = fmaxf(m, row_max * scale_log2);  // scale > 0: scaling commutes with the maximum
-      const bool empty = m_new == -INFINITY;               // nothing to attend to yet (rows beyond the tile)
-      const float alpha = empty ? 1.0f : fast_exp2(m - m_new);  // exp2(-inf) = 0 on the first page
-      const float shift = empty ? 0.0f : -m_new;
+      row_max *= scale_log2;  // scale > 0: scaling commutes with the maximum
+      // P buffer b was last read by the P.V of page i - 2: it must have completed before the row is overwritten
+      if (i >= 2 && !bar_wait(smem_u32(&bar_pv_done[b]), ((i - 2) >> 1) & 1, &abort_flag)) { ok = false; break; }
+      if (row_max > ref + RESCALE_SLACK || (ref == -INFINITY && row_max > -INFINITY)) {
+        // move the reference; what the row has accumulated so far is rescaled in place
+        if (i >= 1 && ref > -INFINITY) {
+          if (!bar_wait(smem_u32(&bar_pv_done[(i - 1) & 1]), ((i - 1) >> 1) & 1, &abort_flag)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const float factor = fast_exp2(ref - row_max);
+          float acc[D];
+          tmem_load_row(tmem_o + lane_addr, acc);
+#pragma unroll
+          for (int d = 0; d < D; ++d) acc[d] *= factor;
+          tmem_store_row(tmem_o + lane_addr, acc);
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          l *= factor;
+        }
+        ref = row_max;
+      }
+      const bool empty = ref == -INFINITY;  // nothing to attend to (rows beyond the tile)
+      const float shift = empty ? 0.0f : -ref;
       float sum = 0.0f;
       uint32_t packed[P / 2];
 #pragma unroll
@@ -289,37 +327,19 @@ prefill_attention_tcgen05_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfl
         sum += p0 + p1;  // the row sum adds the fp32 values; only the tensor-core operand is rounded
         packed[j / 2] = *reinterpret_cast<const uint32_t*>(&pair);
       }
-      l = l * alpha + sum;
-      m = m_new;
-      // P row -> shared memory (operand layout); buffer b was last read by the P.V of page i - 2, whose
-      // completion this thread saw when it read PV of that page
+      l += sum;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(p_tile + b * P_BYTES + swizzled(r, c)),
                      "r"(packed[4 * c]), "r"(packed[4 * c + 1]), "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3]) : "memory");
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       bar_arrive(smem_u32(&bar_p_full[b]));
-      // add the previous page's P.V (it ran while this thread worked on S), then rescale to the new max
-      if (i >= 1) {
-        const int pb = (i - 1) & 1;
-        if (!bar_wait(smem_u32(&bar_pv_full[pb]), ((i - 1) >> 1) & 1, &abort_flag)) { ok = false; break; }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        float pv[D];
-        tmem_load_row(tmem_pv[pb] + lane_addr, pv);
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        bar_arrive(smem_u32(&bar_pv_free[pb]));
-#pragma unroll
-        for (int d = 0; d < D; ++d) o[d] = (o[d] + pv[d]) * alpha;
-      }
     }
+    float o[D];
     if (ok && n_pages > 0) {
-      const int pb = (n_pages - 1) & 1;
-      if (bar_wait(smem_u32(&bar_pv_full[pb]), ((n_pages - 1) >> 1) & 1, &abort_flag)) {
+      if (bar_wait(smem_u32(&bar_pv_done[(n_pages - 1) & 1]), ((n_pages - 1) >> 1) & 1, &abort_flag)) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        float pv[D];
-        tmem_load_row(tmem_pv[pb] + lane_addr, pv);
-#pragma unroll
-        for (int d = 0; d < D; ++d) o[d] += pv[d];
+        tmem_load_row(tmem_o + lane_addr, o);
       } else {
         ok = false;
       }

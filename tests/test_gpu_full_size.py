@@ -81,17 +81,22 @@ def test_sampled_requests_are_reproducible_and_schedule_independent(engine):
     # the same requests through a 3-slot session: row r of the batch used seed 77 with counter offset r * vocab;
     # a session keys every request by its own seed with offset 0, so give each request a distinct seed and compare
     # session runs at two polling intervals instead
-    def session_run(steps):
+    def session_run(steps, together):
         done = {}
         with engine.generation_session(max_batch_size=3, max_new_tokens=40) as session:
             pending, slot_of = list(range(6)), {}
 
             def admit(count, slots=None):
                 ids = [pending.pop(0) for _ in range(count)]
-                got = session.admit([prompts[i] for i in ids],
-                                    [LFM25SamplingConfig(temperature=1.0, max_new_tokens=limits[i], seed=1000 + i,
-                                                         ignore_eos=True) for i in ids], slots=slots)
-                slot_of.update(zip(got, ids))
+                # one admit call packs its prompts into one prefill; admitting one by one keeps every prompt's
+                # prefill the same whatever the schedule
+                groups = [list(range(count))] if together else [[i] for i in range(count)]
+                for group in groups:
+                    got = session.admit([prompts[ids[i]] for i in group],
+                                        [LFM25SamplingConfig(temperature=1.0, max_new_tokens=limits[ids[i]],
+                                                             seed=1000 + ids[i], ignore_eos=True) for i in group],
+                                        slots=None if slots is None else [slots[i] for i in group])
+                    slot_of.update(zip(got, [ids[i] for i in group]))
 
             admit(3)
             while slot_of:
@@ -106,11 +111,24 @@ def test_sampled_requests_are_reproducible_and_schedule_independent(engine):
             assert session.cache.free_pages() == session.cache.n_pages
         return done
 
-    a, b = session_run(4), session_run(16)
+    # prompts prefilled one by one: a request's stream depends on its own prompt and seed alone, so two polling
+    # intervals (other company in the decode rows, other slots, other pages) give the same bits
+    a, b = session_run(4, together=False), session_run(16, together=False)
     for i in range(6):
         assert a[i].token_ids == b[i].token_ids and len(a[i].token_ids) == limits[i]
-        # requests join in different company in the two runs, so their prompts are packed into prefill chunks of
-        # different sizes (other GEMM tiling, other bf16 roundings): same tokens, log-probs equal to bf16 accuracy
-        assert np.allclose(a[i].logprobs, b[i].logprobs, atol=0.15)
+        assert np.array_equal(np.asarray(a[i].logprobs), np.asarray(b[i].logprobs))
         assert all(0 <= t < vocab for t in a[i].token_ids) and a[i].finish_reason == 3
+    # prompts that finish in the same polling window are prefilled together: chunks of other sizes take other
+    # GEMM tiles and split-K depths, so activations differ by bf16 roundings (log-probs by up to ~0.06 here) and
+    # a draw that sits on a near tie may flip, after which the two continuations are different texts. Up to
+    # the first such flip the streams agree; most requests never meet one.
+    c, d = session_run(4, together=True), session_run(16, together=True)
+    identical = 0
+    for i in range(6):
+        assert len(c[i].token_ids) == len(d[i].token_ids) == limits[i]
+        same = [x == y for x, y in zip(c[i].token_ids, d[i].token_ids)]
+        common = same.index(False) if False in same else len(same)
+        identical += common == len(same)
+        assert np.allclose(c[i].logprobs[:common], d[i].logprobs[:common], atol=0.15)
+    assert identical >= 3
     assert np.isfinite(first_lp).all()
