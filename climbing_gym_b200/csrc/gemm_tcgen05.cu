@@ -105,7 +105,7 @@ __device__ __forceinline__ void umma_fp8(uint32_t tmem_d, uint64_t da, uint64_t 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&v)[32]) {
+__device__ __forceinline__ void tmem_issue32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -115,7 +115,17 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
         "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Completes every TMEM load of this thread. The registers of the load being waited for pass through the
+// statement, so no use of them can be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_wait32(uint32_t (&v)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+                 "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]),
+                 "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+               :
+               : "memory");
 }
 
 struct GemmEpilogue {
@@ -135,7 +145,9 @@ struct GemmEpilogue {
 // ml = rank, rank + SPLITS, ...; epilogue warp `quarter` takes every fourth of them, and one 16-byte
 // load per lane fetches a whole 128-feature row of one peer's tile over distributed shared memory
 // (lane l holds features 4l .. 4l+3). All loads of a thread are issued before the first add; the
-// sum runs in split order, so the result does not depend on timing.
+// sum runs in split order, so the result does not depend on timing. Where a token row goes (row mask, row
+// map, M edge) and its activation scale were staged in shared memory while the MMAs ran (row_out /
+// row_scale), so no load from global memory sits between the partial sums and the store.
 //
 // GLOBAL = true is the same reduction with the partial tiles parked in a global fp32 workspace
 // ([split][UN][128] per output tile, L2-resident) instead of shared memory: the SM-to-SM network
@@ -143,7 +155,9 @@ struct GemmEpilogue {
 // is faster through L2 and needs no barrier after it (nobody reads a peer's shared memory).
 template <int SPLITS, int UN, bool GLOBAL>
 __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint32_t tile, const float* ws_tile,
-                                                    uint32_t rank, int quarter, int lane, int m0, int n0) {
+                                                    uint32_t rank, int quarter, int lane, int n0,
+                                                    const int32_t* row_out, const float* row_scale,
+                                                    const float (&ws)[4]) {
   constexpr int ROWS = UN / SPLITS;  // rows this CTA reduces (a multiple of 4: UN >= 32, SPLITS <= 8)
   constexpr int MINE = ROWS / 4;     // rows per warp
   static_assert(ROWS % 4 == 0, "each epilogue warp reduces ROWS / 4 rows");
@@ -155,10 +169,6 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
       asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer[sp]) : "r"(column), "r"(sp));
   }
   const int n = n0 + 4 * lane;
-  float ws[4] = {1.0f, 1.0f, 1.0f, 1.0f};
-  if (ep.w_scales != nullptr)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) ws[j] = n + j < ep.N ? ep.w_scales[n + j] : 1.0f;
   constexpr int BATCH = MINE * SPLITS <= 16 ? MINE : 16 / SPLITS;  // at most 16 loads of 16 bytes in flight
 #pragma unroll 1
   for (int first = 0; first < MINE; first += BATCH) {
@@ -180,10 +190,8 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
 #pragma unroll
   for (int b = 0; b < BATCH; ++b) {
     const int i = first + b;
-    const int m = m0 + static_cast<int>(rank) + (quarter + 4 * i) * SPLITS;
-    if (m >= ep.M) continue;
-    if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
-    const int out_row = ep.row_map != nullptr ? ep.row_map[m] : m;
+    const int ml = static_cast<int>(rank) + (quarter + 4 * i) * SPLITS;
+    const int out_row = row_out[ml];  // negative: beyond M, masked or unmapped
     if (out_row < 0) continue;
     float total[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -194,7 +202,7 @@ __device__ __forceinline__ void cluster_reduce_rows(const GemmEpilogue& ep, uint
       total[3] = __fadd_rn(total[3], value[b][sp].w);
     }
     if (ep.x_scales != nullptr) {
-      const float xs = ep.x_scales[m];
+      const float xs = row_scale[ml];
 #pragma unroll
       for (int j = 0; j < 4; ++j) total[j] = __fmul_rn(__fmul_rn(total[j], xs), ws[j]);
     }
@@ -236,6 +244,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   __shared__ __align__(8) uint64_t bar_acc;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
+  __shared__ int32_t row_out[UN];   // output row of token row ml of this tile; negative = not written
+  __shared__ __align__(16) float row_scale[UN];  // its activation scale (1 without scales)
 
   pdl_trigger();  // the next kernel may be scheduled now; it waits for this grid before touching y
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -266,6 +276,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem_acc = tmem_slot;
+  float ws_reduce[4] = {1.0f, 1.0f, 1.0f, 1.0f};  // epilogue warps: weight scales of the features a lane reduces
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
@@ -332,45 +343,116 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   } else if (warp >= 2) {
     // ---- epilogue: TMEM lane = output feature, column = token ----
     const int quarter = warp & 3;  // a warp may only touch TMEM lanes [32 * (warp % 4), +32)
-    pdl_wait();  // scales / row mask come from earlier kernels of the step
+    // Weight scales are constants of the model: fetch them before the wait, in the layout the final store
+    // uses (split-K: lane l reduces features 4l .. 4l+3; else lane = feature of each sub-tile). A load issued
+    // after the main loop would queue behind the other CTAs' tile traffic.
+    float ws_direct[FM];
+#pragma unroll
+    for (int f = 0; f < FM; ++f) {
+      const int n = n0 + f * UM + quarter * 32 + lane;
+      ws_direct[f] = (!ep.partial && ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
+    }
+    if (ep.partial && ep.w_scales != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ws_reduce[j] = n0 + 4 * lane + j < ep.N ? ep.w_scales[n0 + 4 * lane + j] : 1.0f;
+    }
+    pdl_wait();  // activation scales / row mask come from earlier kernels of the step
+    // While the MMAs run: resolve where each token row of the tile goes and what scales it. The loops
+    // below then depend on shared memory alone (one load from global memory per row and lane, between the
+    // accumulator and the store, made the epilogue longer than the main loop).
+    for (int ml = static_cast<int>(threadIdx.x) - 64; ml < UN; ml += 128) {
+      const int m = m0 + ml;
+      int out = -1;
+      float xs = 1.0f;
+      if (m < ep.M && (ep.row_mask == nullptr || ep.row_mask[m])) {
+        out = ep.row_map != nullptr ? ep.row_map[m] : m;
+        if (ep.x_scales != nullptr) xs = ep.x_scales[m];
+      }
+      row_out[ml] = out;
+      row_scale[ml] = xs;
+    }
     if (n_kb > 0) mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps agree on abort_flag
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps agree on abort_flag and see the rows
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (abort_flag == 0 || ep.partial) {
-#pragma unroll 1
-      for (int f = 0; f < FM; ++f) {
-      const int n_local = quarter * 32 + lane, n = n0 + f * UM + n_local;
-      const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
+      // rows of 8 features are stored as one 16-byte word when the tile lies inside y and rows are aligned
+      const bool wide = !ep.partial && (ep.N & 7) == 0 && n0 + FM * UM <= ep.N;
+      const bool scaled = ep.x_scales != nullptr;
+      const bool live = n_kb > 0 && abort_flag == 0;  // else the accumulator was never written: the tile is zero
+      // per warp: a [32 tokens][32 features] bf16 block of the idle ring turns the accumulator (lane =
+      // feature) into token rows
+      __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem_raw + (tiles - smem_u32(smem_raw))) + quarter * 1024;
       // partial tile [UN][128]: in this CTA's shared memory (the ring is idle now) or in the workspace
       float* part = reinterpret_cast<float*>(smem_raw + (tiles - smem_u32(smem_raw)));
       if (ep.partial && ep.split_ws != nullptr)
         part = ep.split_ws + ((static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * gridDim.z + blockIdx.z) * (UN * UM);
-#pragma unroll 1
-      for (int c = 0; c < UN / 32; ++c) {
-        uint32_t v[32];
-        if (n_kb > 0 && abort_flag == 0) {
-          tmem_load32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + f * UN + c * 32, v);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0u;
-        }
+      const int n_local = quarter * 32 + lane;
+      constexpr int CHUNKS = UN / 32, TOTAL = FM * CHUNKS;  // blocks of 32 token columns, sub-tile major
+      auto chunk_addr = [&](int i) {
+        return tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>((i / CHUNKS) * UN + (i % CHUNKS) * 32);
+      };
+      auto emit = [&](int i, const uint32_t (&v)[32]) {
+        const int f = i / CHUNKS, c = i % CHUNKS, n = n0 + f * UM + n_local;
+        const float ws = (FM > 1 && f == 1) ? ws_direct[FM - 1] : ws_direct[0];
         if (ep.partial) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) part[(c * 32 + j) * UM + n_local] = __uint_as_float(v[j]);
+          for (int j = 0; j < 32; ++j) part[(c * 32 + j) * UM + n_local] = live ? __uint_as_float(v[j]) : 0.0f;
+        } else if (wide) {
+#pragma unroll
+          for (int j0 = 0; j0 < 32; j0 += 8) {
+            // the scales of eight rows are read before the first store of the group: the compiler cannot tell
+            // that the stores below leave row_scale alone, and would order every read behind the store before it
+            float xs[8];
+            *reinterpret_cast<float4*>(&xs[0]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0]);
+            *reinterpret_cast<float4*>(&xs[4]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0 + 4]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float val = live ? __uint_as_float(v[j0 + j]) : 0.0f;
+              if (scaled) val = __fmul_rn(__fmul_rn(val, xs[j]), ws);
+              stage[(j0 + j) * 32 + lane] = __float2bfloat16_rn(val);
+            }
+          }
+          __syncwarp();
+          // four lanes per token row (8 features = 16 bytes each), eight rows per pass
+#pragma unroll
+          for (int pass = 0; pass < 4; ++pass) {
+            const int row = pass * 8 + (lane >> 2);
+            const uint4 word = *reinterpret_cast<const uint4*>(stage + row * 32 + (lane & 3) * 8);
+            const int out_row = row_out[c * 32 + row];
+            if (out_row >= 0)
+              *reinterpret_cast<uint4*>(ep.y + static_cast<int64_t>(out_row) * ep.N + n0 + f * UM + quarter * 32 + (lane & 3) * 8) = word;
+          }
+          __syncwarp();
         } else if (n < ep.N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c * 32 + j;
-            if (m >= ep.M) break;
-            if (ep.row_mask != nullptr && !ep.row_mask[m]) continue;
-            const int out_row = ep.row_map != nullptr ? ep.row_map[m] : m;
+            const int out_row = row_out[c * 32 + j];
             if (out_row < 0) continue;
-            float val = __uint_as_float(v[j]);
-            if (ep.x_scales != nullptr) val = __fmul_rn(__fmul_rn(val, ep.x_scales[m]), ws);
+            float val = live ? __uint_as_float(v[j]) : 0.0f;
+            if (scaled) val = __fmul_rn(__fmul_rn(val, row_scale[c * 32 + j]), ws);
             ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
           }
         }
-      }
+      };
+      // A TMEM load and its wait cost about half a microsecond back to back, whatever the width. A CTA that
+      // owns its SM fetches 128 columns (four blocks) per wait. The half-SM kernels of the decode step fetch one
+      // block at a time: their registers decide how early the CTAs of the NEXT kernel of the chain become
+      // resident beside them, which is worth more there than a shorter epilogue.
+      constexpr int GROUP = RING_KB > 96 ? (TOTAL < 4 ? TOTAL : 4) : 1;
+      static_assert(TOTAL % GROUP == 0, "token tiles are 32, 64, 128 or 256 columns");
+#pragma unroll 1
+      for (int i = 0; i < TOTAL; i += GROUP) {
+        uint32_t v[GROUP][32];
+#pragma unroll
+        for (int g = 0; g < GROUP; ++g) {
+          if (live) tmem_issue32(chunk_addr(i + g), v[g]);
+        }
+        if (live) {
+#pragma unroll
+          for (int g = 0; g < GROUP; ++g) tmem_wait32(v[g]);  // the first completes all; the rest tie the registers
+        }
+#pragma unroll
+        for (int g = 0; g < GROUP; ++g) emit(i + g, v[g]);
       }
     }
   }
@@ -388,13 +470,13 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
       if (ep.split_ws != nullptr) {
         const float* ws_tile =
             ep.split_ws + (static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * gridDim.z * (UN * UM);
-        if (splits == 2) cluster_reduce_rows<2, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, m0, n0);
-        else if (splits == 4) cluster_reduce_rows<4, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, m0, n0);
-        else cluster_reduce_rows<8, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, m0, n0);
+        if (splits == 2) cluster_reduce_rows<2, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, n0, row_out, row_scale, ws_reduce);
+        else if (splits == 4) cluster_reduce_rows<4, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, n0, row_out, row_scale, ws_reduce);
+        else cluster_reduce_rows<8, UN, true>(ep, tiles, ws_tile, rank, quarter, lane, n0, row_out, row_scale, ws_reduce);
       } else {
-        if (splits == 2) cluster_reduce_rows<2, UN, false>(ep, tiles, nullptr, rank, quarter, lane, m0, n0);
-        else if (splits == 4) cluster_reduce_rows<4, UN, false>(ep, tiles, nullptr, rank, quarter, lane, m0, n0);
-        else cluster_reduce_rows<8, UN, false>(ep, tiles, nullptr, rank, quarter, lane, m0, n0);
+        if (splits == 2) cluster_reduce_rows<2, UN, false>(ep, tiles, nullptr, rank, quarter, lane, n0, row_out, row_scale, ws_reduce);
+        else if (splits == 4) cluster_reduce_rows<4, UN, false>(ep, tiles, nullptr, rank, quarter, lane, n0, row_out, row_scale, ws_reduce);
+        else cluster_reduce_rows<8, UN, false>(ep, tiles, nullptr, rank, quarter, lane, n0, row_out, row_scale, ws_reduce);
       }
     }
     if (ep.split_ws == nullptr) {
