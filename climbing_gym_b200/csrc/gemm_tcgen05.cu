@@ -579,10 +579,17 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
                "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
   CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
-  // Token tile: the smallest that covers M up to 128; up to 256 rows (a full decode batch) two tiles of
-  // 128 keep the weight-streaming layout (half-SM rings, split-K) - the second tile's weight loads hit
+  // Token tile: the smallest that covers M up to 128; up to 256 rows (a full decode batch) tiles of 128
+  // or 64 keep the weight-streaming layout (half-SM rings, split-K) - the other tiles' weight loads hit
   // L2 - and only larger M (prefill) takes the 256-token tile that halves L2 -> SM traffic per FLOP.
   int un = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 256 ? 128 : 256));
+  // A full decode batch (129..256 rows) takes 64-token tiles where all of them still fit the GPU's resident
+  // slots at once (every projection of the 1.2B model except w13 and the LM head): with four token tiles
+  // the K dimension needs half as many splits to fill the SMs, so half as many fp32 partial tiles are written
+  // and read back, the clusters are half as large (eight co-resident CTAs in one GPC often had to wait for
+  // the previous kernel to drain), and a CTA's epilogue covers 64 columns instead of 128. The weight tiles
+  // are fetched by four token tiles instead of two - out of L2, which has the bandwidth to spare here.
+  if (M > 128 && M <= 256 && ((N + UM - 1) / UM) * ((M + 63) / 64) <= 2 * 148) un = 64;
   // Two feature sub-tiles per CTA (one fetch of the token tile serves 256 features) for unsplit GEMMs
   // over more than 128 tokens. With 256-token tiles (prefill) it pays unless halving the CTA count costs
   // more in the last, partly filled wave than the saved traffic gains; for a decode batch of 129..256
