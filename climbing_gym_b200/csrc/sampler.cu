@@ -275,8 +275,17 @@ gumbel_noise_kernel(float* __restrict__ noise, cgym_slot_state st, int vocab) {
   }
 }
 
-static int pick_parts(int rows, int vocab, const float* workspace) {
+static int pick_parts(int rows, int vocab, const float* workspace, bool noise_ready = false) {
   if (workspace == nullptr || vocab < 8192) return 1;
+  // With the Gumbel noise drawn ahead (gumbel_noise_kernel) a slice is two loads, an exponential and a
+  // compare per logit: a CTA's fixed cost (launch, block reductions, the merge through the workspace) then
+  // outweighs its share of the row, so take as few slices as still give every resident slot a CTA.
+  if (noise_ready) {
+    int parts = (2 * 148) / (rows > 0 ? rows : 1);
+    if (parts > vocab / 4096) parts = vocab / 4096;
+    if (parts > SAMPLE_MAX_PARTS) parts = SAMPLE_MAX_PARTS;
+    return parts < 1 ? 1 : parts;
+  }
   // Two 512-thread CTAs fit an SM (62 registers per thread), i.e. 296 CTAs run at once. The kernel's time
   // is the number of such waves times a slice's share of the row, so pick the slice count that minimises
   // waves / parts (64 rows: 4 slices fill one wave where 5 would start a second; 256 rows: 8 slices leave
@@ -622,7 +631,7 @@ extern "C" int cgym_sample_record(const void* logits, const cgym_slot_state* sta
   CGYM_REQUIRE(state->seeds && state->temperatures && state->rng_positions && state->lengths && state->alive,
                "sample_record: slot state is incomplete");
   if (n_slots == 0) return 0;
-  const dim3 grid(n_slots, pick_parts(n_slots, vocab, workspace));
+  const dim3 grid(n_slots, pick_parts(n_slots, vocab, workspace, state->gumbel_noise != nullptr));
   if (dtype == CGYM_F32)
     launch_dependent(sample_kernel<float>, grid, dim3(SAMPLE_THREADS), 0, as_stream(stream),
                      static_cast<const float*>(logits), *state, true, advance, state->seeds, state->rng_positions,
