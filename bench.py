@@ -65,7 +65,7 @@ WORKLOADS = {
 # ncu capture on a small case of the same step) divided by the step's algorithmic bytes at the captured
 # sequence lengths. Both grow with the same two terms (weights once, KV history once), so `roofline.traffic`
 # scales the full-size algorithmic bytes by this ratio.
-DRAM_TRAFFIC_RATIO = {"bf16-b64x512": 1.0518, "fp8-queue2048x256": 1.143}
+DRAM_TRAFFIC_RATIO = {"bf16-b64x512": 1.058, "fp8-queue2048x256": 1.143}
 
 # Continuous batching through a generation session: a queue of requests served by a fixed number of live
 # slots; a finished request's slot is refilled from the queue at the next scheduling window.
