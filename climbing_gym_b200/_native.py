@@ -104,7 +104,7 @@ SIGNATURES = {
 }
 PLAIN = {"cgym_last_error": ([], C.c_char_p), "cgym_version": ([], _I), "cgym_device_supported": ([], _I),
          "cgym_launch_count": ([], C.c_longlong), "cgym_sample_workspace_bytes": ([_I], C.c_int64),
-         "cgym_set_pdl": ([_I], _I)}
+         "cgym_set_pdl": ([_I], _I), "cgym_test_gemm_wait": ([C.c_ulonglong, _I], _I)}
 
 _lib = None
 

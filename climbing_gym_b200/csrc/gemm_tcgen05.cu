@@ -29,6 +29,13 @@ constexpr int SLICE_BYTES = 128;  // K bytes per pipeline stage (one swizzle ato
 constexpr int GEMM_THREADS = 192;
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
+// TEST HOOK (cgym_test_gemm_wait): a shorter limit for the waits that decide to give up, and a switch that
+// makes the producer arm its barriers without issuing the copies, so that a wait nothing satisfies runs out
+// and the give-up path (status word, TMEM freed, kernel returns) can be exercised without a fault or a hang.
+// Both keep their defaults in production; waits that drain copies already in flight always use the full limit.
+__device__ unsigned long long g_wait_limit_ns = WAIT_LIMIT_NS;
+__device__ int g_drop_loads = 0;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
 __device__ __forceinline__ unsigned long long global_timer() {
@@ -55,14 +62,17 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 // bounded wait: false when the limit expired or another role already gave up
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          bool draining = false) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long start = global_timer();
+  unsigned long long limit = 2000000000ull;  // WAIT_LIMIT_NS
+  if (!draining) limit = *const_cast<volatile unsigned long long*>(&g_wait_limit_ns);
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try(bar, parity)) return true;
     if ((spin & 63u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_timer() - start > WAIT_LIMIT_NS) {
+      if (*abort_flag && !draining) return false;
+      if (global_timer() - start > limit) {
         *abort_flag = 1;
         return false;
       }
@@ -281,6 +291,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
     int issued = 0;
+    const bool drop = *const_cast<volatile int*>(&g_drop_loads) != 0;  // test hook: arm the barriers, copy nothing
     // Weights never depend on the previous kernel: fill the ring with weight tiles right away, and
     // only then wait for the kernel that produces the activations (programmatic dependent launch).
     const int prefetch = n_kb < STAGES ? n_kb : STAGES;
@@ -289,13 +300,15 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
       mbar_expect_tx(full, STAGE_BYTES);
 #pragma unroll
       for (int f = 0; f < FM; ++f)
-        tma_load_2d(tiles + i * STAGE_BYTES + f * UM * SLICE_BYTES, &tmap_w, full, (kb_begin + i) * ELEMS_PER_SLICE,
-                    n0 + f * UM);
+        if (!drop)
+          tma_load_2d(tiles + i * STAGE_BYTES + f * UM * SLICE_BYTES, &tmap_w, full, (kb_begin + i) * ELEMS_PER_SLICE,
+                      n0 + f * UM);
     }
     pdl_wait();
     for (int i = 0; i < prefetch; ++i) {
-      tma_load_2d(tiles + i * STAGE_BYTES + W_BYTES, &tmap_x, smem_u32(&bar_full[i]),
-                  (kb_begin + i) * ELEMS_PER_SLICE, m0);
+      if (!drop)
+        tma_load_2d(tiles + i * STAGE_BYTES + W_BYTES, &tmap_x, smem_u32(&bar_full[i]),
+                    (kb_begin + i) * ELEMS_PER_SLICE, m0);
       issued = i + 1;
     }
     for (int i = prefetch; i < n_kb; ++i) {
@@ -306,15 +319,17 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
       mbar_expect_tx(full, STAGE_BYTES);
       const uint32_t a_dst = tiles + s * STAGE_BYTES, b_dst = a_dst + W_BYTES;
       const int k_elem = (kb_begin + i) * ELEMS_PER_SLICE;
+      if (!drop) {
 #pragma unroll
-      for (int f = 0; f < FM; ++f) tma_load_2d(a_dst + f * UM * SLICE_BYTES, &tmap_w, full, k_elem, n0 + f * UM);
-      tma_load_2d(b_dst, &tmap_x, full, k_elem, m0);
+        for (int f = 0; f < FM; ++f) tma_load_2d(a_dst + f * UM * SLICE_BYTES, &tmap_w, full, k_elem, n0 + f * UM);
+        tma_load_2d(b_dst, &tmap_x, full, k_elem, m0);
+      }
       issued = i + 1;
     }
-    if (abort_flag) {
+    if (abort_flag && !drop) {
       // let copies already in flight land before the CTA's shared memory is released
       for (int i = max(0, issued - STAGES); i < issued; ++i)
-        mbar_wait(smem_u32(&bar_full[i % STAGES]), (i / STAGES) & 1, &abort_flag);
+        mbar_wait(smem_u32(&bar_full[i % STAGES]), (i / STAGES) & 1, &abort_flag, true);
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
@@ -657,3 +672,13 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
 }
 
 }  // namespace cgym
+
+extern "C" int cgym_test_gemm_wait(unsigned long long limit_ns, int drop_loads) {
+  using namespace cgym;
+  const unsigned long long limit = limit_ns == 0 ? WAIT_LIMIT_NS : limit_ns;
+  const int drop = drop_loads ? 1 : 0;
+  cudaError_t rc = cudaMemcpyToSymbol(g_wait_limit_ns, &limit, sizeof(limit));
+  if (rc == cudaSuccess) rc = cudaMemcpyToSymbol(g_drop_loads, &drop, sizeof(drop));
+  CGYM_REQUIRE(rc == cudaSuccess, "test_gemm_wait: %s", cudaGetErrorString(rc));
+  return 0;
+}

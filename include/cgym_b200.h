@@ -443,9 +443,10 @@ int cgym_pages_fork(const cgym_page_pool* pool, const cgym_kv_layout* kv, int n_
                     int n, int32_t* status, cgym_stream_t stream);
 
 /* ---- TEST HOOKS ----------------------------------------------------------------------------------------
- * The two entry points below exist for tests: they read and write the paged cache through dense fp32 arrays,
+ * The first two entry points below exist for tests: they read and write the paged cache through dense fp32 arrays,
  * standing in for the dense k_cache / v_cache views the reference's tests index directly. Nothing on the
- * generate path calls them. (cgym_slot_state.force_eos_at above is the third test hook of this ABI.) */
+ * generate path calls them. (cgym_slot_state.force_eos_at above and cgym_test_gemm_wait below are the other
+ * test hooks of this ABI.) */
 
 /* Test/debug helper: gather one slot's K or V history into a dense [len][Hkv][D] fp32 array
  * (dequantised), standing in for the dense k_cache/v_cache views the reference tests read
@@ -459,6 +460,14 @@ int cgym_gather_kv_dense(float* out, const cgym_kv_layout* kv, int layer, int wh
  * tests assign into k_cache / v_cache views, tests/test_lfm25_fp8_kv.py:24-90). */
 int cgym_scatter_kv_dense(const float* k, const float* v, const cgym_kv_layout* kv, int layer,
                           int slot, int start, int length, cgym_stream_t stream);
+
+/* Test hook for the bounded waits of the tcgen05 GEMM (no reference counterpart): limit_ns replaces the limit
+ * (about two seconds) after which a wait that decides to give up does so (0 = restore it), and drop_loads != 0
+ * makes the producer arm its barriers without issuing the tile copies, so the consumer's wait is one that
+ * nothing satisfies. A GEMM launched in that state returns normally with CGYM_STATUS_WAIT_TIMEOUT in its status
+ * word and an undefined y; nothing faults and nothing is left in flight. Call it with the device current and no
+ * GEMM running; call it again with (0, 0) before any real work. */
+int cgym_test_gemm_wait(unsigned long long limit_ns, int drop_loads);
 
 #ifdef __cplusplus
 }

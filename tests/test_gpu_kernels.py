@@ -490,11 +490,95 @@ def test_gemm_fp8_scaled_epilogue(dev, impl, shape):
     assert_gemm_close(f32(y), want, exact_fraction=0.97, what=f"fp8 gemm impl {impl}")
 
 
+DECODE_WS_BYTES = 2 * 148 * 128 * 128 * 4  # the engine's GEMM workspace: one fp32 partial tile per resident CTA
+
+
+def test_gemm_bounded_wait_gives_up_and_the_context_survives(dev):
+    """A wait that nothing satisfies (the producer arms its barriers but copies no tile: test hook) runs into the
+    shortened limit; the kernel raises CGYM_STATUS_WAIT_TIMEOUT in the status word, frees its TMEM and returns.
+    The next GEMM on the same context is correct. Nothing faults, traps or hangs."""
+    STATUS_WAIT_TIMEOUT = 4  # CGYM_STATUS_WAIT_TIMEOUT
+    lib = nv.load()
+    m, n, k = 64, 512, 1024
+    rng = np.random.default_rng(3)
+    x_np, w_np = round_bf16(rng.standard_normal((m, k))), round_bf16(rng.standard_normal((n, k)) * 0.1)
+    want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
+    x, w = bf(x_np, dev), bf(w_np, dev)
+    y = torch.zeros((m, n), device=dev, dtype=torch.bfloat16)
+    ws = torch.zeros(DECODE_WS_BYTES, device=dev, dtype=torch.uint8)
+    status = torch.zeros(1, device=dev, dtype=torch.int32)
+
+    def launch():
+        nv.call("cgym_gemm", nv.ptr(y), nv.ptr(x), nv.ptr(w), None, m, n, k, nv.dtype_code(torch.bfloat16), 0,
+                nv.ptr(ws), ws.numel(), nv.ptr(status), stream())
+        torch.cuda.synchronize()
+
+    torch.cuda.synchronize()
+    assert lib.cgym_test_gemm_wait(2_000_000, 1) == 0  # give up after 2 ms; copy nothing
+    try:
+        launch()
+        assert int(status.item()) & STATUS_WAIT_TIMEOUT, "the expired wait must be reported in the status word"
+    finally:
+        torch.cuda.synchronize()
+        assert lib.cgym_test_gemm_wait(0, 0) == 0
+    status.zero_()
+    launch()
+    assert int(status.item()) == 0
+    assert_gemm_close(f32(y), want, exact_fraction=0.97, what="gemm after a timed-out launch")
+
+
+@pytest.mark.parametrize("shape,ws", [((200, 512, 256), 0), ((200, 2048, 2048), 1), ((256, 16384, 512), 0),
+                                      ((48, 256, 4096), 1)])
+def test_gemm_scatter_writes_mapped_rows_only(dev, shape, ws):
+    """cgym_gemm_scatter / cgym_gemm_fp8_scatter: token row m lands in output row row_map[m]; rows mapped to a
+    negative index and masked rows leave y untouched (replaces _scatter_logits, lfm25_batching.py:25-33).
+    Shapes take the unsplit epilogue (16-byte row segments), split-K through the workspace, two feature
+    sub-tiles per CTA and 64-token tiles."""
+    m, n, k = shape
+    rng = np.random.default_rng(m + n)
+    out_rows = m + 24
+    row_map = rng.permutation(out_rows)[:m].astype(np.int32)
+    row_map[rng.random(m) < 0.15] = -1
+    mask = (rng.random(m) < 0.8).astype(np.uint8)
+    written = (row_map >= 0) & (mask == 1)
+    ws_bytes = DECODE_WS_BYTES if ws else 0
+    work = torch.zeros(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
+    status = torch.zeros(1, device=dev, dtype=torch.int32)
+    dmap, dmask = torch.from_numpy(row_map).to(dev), torch.from_numpy(mask).to(dev)
+
+    x_np, w_np = round_bf16(rng.standard_normal((m, k))), round_bf16(rng.standard_normal((n, k)) * 0.1)
+    want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
+    y = torch.full((out_rows, n), -3.0, device=dev, dtype=torch.bfloat16)
+    x, w = bf(x_np, dev), bf(w_np, dev)
+    nv.call("cgym_gemm_scatter", nv.ptr(y), nv.ptr(x), nv.ptr(w), nv.ptr(dmask), nv.ptr(dmap),
+            m, n, k, nv.dtype_code(torch.bfloat16), 0, nv.ptr(work) if ws else None, ws_bytes, nv.ptr(status), stream())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = f32(y)
+    untouched = np.ones(out_rows, dtype=bool)
+    untouched[row_map[written]] = False
+    assert np.all(got[untouched] == -3.0), "rows outside the map, masked rows and unmapped rows must stay as they were"
+    assert_gemm_close(got[row_map[written]], want[written], exact_fraction=0.97, what=f"scatter bf16 {shape}")
+
+    if k % 128 == 0:
+        xq, xs = ok.quantize_rows(round_bf16(rng.standard_normal((m, k))))
+        wq, wsc = ok.quantize_rows(round_bf16(rng.standard_normal((n, k)) * 0.05))
+        want8 = ok.fp8_matmul(xq, xs, wq, wsc)
+        args = [torch.from_numpy(a).to(dev) for a in (xq, xs, wq, wsc)]
+        y8 = torch.full((out_rows, n), -3.0, device=dev, dtype=torch.bfloat16)
+        nv.call("cgym_gemm_fp8_scatter", nv.ptr(y8), nv.ptr(args[0]), nv.ptr(args[1]), nv.ptr(args[2]), nv.ptr(args[3]),
+                nv.ptr(dmask), nv.ptr(dmap), m, n, k, 0, nv.ptr(work) if ws else None, ws_bytes, nv.ptr(status), stream())
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        got8 = f32(y8)
+        assert np.all(got8[untouched] == -3.0)
+        assert_gemm_close(got8[row_map[written]], want8[written], exact_fraction=0.97, what=f"scatter fp8 {shape}")
+
+
 # The decode step's own launches: the 1.2B model's projection shapes at the batch sizes that are benchmarked,
 # with the engine's workspace size (2 x 148 resident CTAs, one [token tile][128] fp32 partial tile each), so the
 # launcher takes the grids the step takes: cluster split-K up to 8 ways over an 8192-deep contraction, and two
 # 128-token tiles at 256 rows.
-DECODE_WS_BYTES = 2 * 148 * 128 * 128 * 4
 
 
 @pytest.mark.parametrize("shape", [(256, 2048, 8192), (256, 16384, 2048), (64, 2048, 8192), (128, 2048, 8192),
