@@ -529,17 +529,18 @@ class DeviceQueueDriver(QueueDriver):
     def live_generated(self) -> int:
         return int((self.session.lengths * self._occupied()).sum())
 
-    def _context_tokens(self) -> float:
-        occupied = self._occupied()
-        return float((self.session.entry.cache.seq_lens * occupied).sum()), float(occupied.sum())
-
     def window(self, host: bool, *, account_kv: bool = False):
+        # The decode steps are launched first; the host then parks the next prompts (metadata, copies and
+        # prefill launches queue behind the steps while they run) and only then waits for the poll's reads,
+        # which travel on a stream of their own. The queue holds a window's worth of parked prompts and more,
+        # so parking with the previous poll's free count never starves the slot turnover.
+        context, rows = self.session.last_context
+        before = context + rows
+        self.session.poll_begin(steps=self.poll_steps)
+        self._park(host)
+        results = self.session.poll_end()
         if account_kv:
-            context, rows = self._context_tokens()
-            before = context + rows
-        results = self.session.poll(steps=self.poll_steps)
-        if account_kv:
-            context, rows = self._context_tokens()
+            context, rows = self.session.last_context
             self.kv_token_steps += self.poll_steps * (before + context + rows) / 2.0
         for result in results:
             n = len(result.token_ids)
@@ -549,7 +550,6 @@ class DeviceQueueDriver(QueueDriver):
             self.delivered_requests += 1
             self.d2h_bytes += n * 12 + 4
         self.d2h_bytes += 4 + self.session.state.queue["result_capacity"]  # queue head + the result index
-        self._park(host)
         self.windows += 1
 
 
@@ -635,7 +635,8 @@ def run_queue(args) -> dict:
                            "deliver finished requests -> release -> admit the next queued requests into the freed slots "
                            f"({windows_per_step * poll_steps} decode steps + the admitted prompts' prefill)",
                    "scheduler": ("device: finished requests are evicted and parked prompts admitted inside the decode "
-                                 "graph; the host parks the next prompts and reads results once per window"
+                                 "graph; the host launches a window's steps, parks the next prompts behind them and reads results "
+                                 "once per window on a stream of its own"
                                  if on_device else "host: release and admit from Python at every window"),
                    "preroll": f"{preroll} untimed windows before the warm-up (age mix of a session in mid-queue)",
                    "options": options, "sampling": "temperature 1, full support", "replicas": world,

@@ -112,6 +112,9 @@ class LFM25GenerationSession:
         self._queued: dict[int, tuple] = {}
         self._next_request_id = 0
         self._queue_tail = self._queue_consumed = 0
+        self._poll_pending = None  # (event after the reads of poll_begin, whether steps were launched)
+        self._read_stream = None   # device-to-host reads of a poll (queue mode), created on first use
+        self.last_context = (0.0, 0.0)
         self.requests: list[_Request | None] = [None] * max_batch_size
         self.versions = [0] * max_batch_size
         self.closed = False
@@ -531,23 +534,75 @@ class LFM25GenerationSession:
         return max(0, min(self.queue_capacity - waiting, len(self._free_rows), results_free))
 
     def _poll_queue(self, steps: int) -> list[LFM25SessionResult]:
-        """``steps`` replays (slot turnover runs inside each), one more turnover so that the last step's
-        finishers are published and replaced, then one read of the result index."""
-        if not self._queued:
+        self.poll_begin(steps=steps)
+        return self.poll_end()
+
+    @torch.inference_mode()
+    def poll_begin(self, *, steps: int | None = None) -> None:
+        """First half of ``poll`` in queue mode: launch ``steps`` replays (slot turnover runs inside each) and one
+        more turnover, so that the last step's finishers are published and replaced, and start copying what the
+        host reads (queue head, result index, status word, live context) on a stream of its own. Returns at once:
+        whatever the caller launches next (``enqueue`` of the next prompts) queues behind the decode steps while
+        the host is still free to prepare it, and ``poll_end`` does not wait for it."""
+        self._check_open()
+        if not self.queue_capacity:
+            raise RuntimeError("poll_begin / poll_end need a session opened with queue_capacity > 0")
+        if self._poll_pending is not None:
+            raise RuntimeError("poll_end the previous poll first")
+        steps = self.decoder.finish_check_interval if steps is None else steps
+        if type(steps) is not int or steps <= 0:
+            raise ValueError("steps must be a positive integer")
+        queue, dev = self.state.queue, self.engine.device
+        launched = bool(self._queued)
+        if launched:
+            with self._timed("decode"):
+                for _ in range(steps):
+                    self.entry.graph.replay()
+                self.decoder._turnover(self.entry)
+            self.stats["decode_steps"] += steps
+            self.stats["decode_row_steps"] += self.batch_size * steps
+            self.stats["reserved_row_steps"] += self.batch_size * steps
+            batches = self.stats["decode_batches"]
+            batches[str(self.batch_size)] = batches.get(str(self.batch_size), 0) + steps
+        if self._read_stream is None:
+            self._read_stream = torch.cuda.Stream(device=dev)
+            ring = queue["result_capacity"]
+            self._host_head = torch.zeros(1, dtype=queue["head"].dtype).pin_memory()
+            self._host_reasons = torch.zeros(ring, dtype=torch.int8).pin_memory()
+            self._host_status = torch.zeros(1, dtype=torch.int32).pin_memory()
+            self._host_context = torch.zeros(2, dtype=torch.float64).pin_memory()
+        reads = self._read_stream
+        reads.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(reads):
+            self._host_head.copy_(queue["head"], non_blocking=True)
+            self._host_reasons.copy_(queue["result_reasons"], non_blocking=True)
+            self._host_status.copy_(self.cache.status, non_blocking=True)
+            occupied = queue["slot_requests"] >= 0
+            context = torch.stack([(self.cache.seq_lens[:self.batch_size] * occupied).sum(dtype=torch.float64),
+                                   occupied.sum(dtype=torch.float64)])
+            self._host_context.copy_(context, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(reads)
+        self._poll_pending = (done, launched)
+
+    @torch.inference_mode()
+    def poll_end(self) -> list[LFM25SessionResult]:
+        """Second half of ``poll`` in queue mode: wait for the reads of ``poll_begin`` (not for work launched since)
+        and deliver the requests that have finished."""
+        self._check_open()
+        if self._poll_pending is None:
+            raise RuntimeError("poll_begin first")
+        done_event, launched = self._poll_pending
+        self._poll_pending = None
+        done_event.synchronize()
+        if not launched:
             return []
         queue, dev = self.state.queue, self.engine.device
-        with self._timed("decode"):
-            for _ in range(steps):
-                self.entry.graph.replay()
-            self.decoder._turnover(self.entry)
-        self.stats["decode_steps"] += steps
-        self.stats["decode_row_steps"] += self.batch_size * steps
-        self.stats["reserved_row_steps"] += self.batch_size * steps
-        batches = self.stats["decode_batches"]
-        batches[str(self.batch_size)] = batches.get(str(self.batch_size), 0) + steps
-        head = int(queue["head"].item())
-        reasons = queue["result_reasons"].cpu().tolist()  # with the head above: the reads of this poll
-        self.cache.check_status()
+        head = int(self._host_head.item())
+        reasons = self._host_reasons.tolist()
+        self.last_context = tuple(self._host_context.tolist())  # (cached tokens of the live rows, live rows)
+        if int(self._host_status.item()):
+            self.cache.check_status()
         ring = queue["result_capacity"]
         # parked rows whose prompt a slot has adopted are free again
         # (request ids are handed out in queue order, so the ids below `head` are the entries consumed so far)
@@ -563,12 +618,15 @@ class LFM25GenerationSession:
         done = [rid for rid in sorted(self._queued) if self._queued[rid][2] is None and reasons[rid % ring]]
         if not done:
             return []
-        index = torch.tensor([rid % ring for rid in done], device=dev)
-        lengths = queue["result_lengths"][index].cpu().tolist()
-        longest = max(lengths)
-        tokens = self.state.tokens[:, :longest].index_select(0, index).cpu().tolist()
-        logprobs = self.state.logprobs[:, :longest].index_select(0, index).cpu().tolist()
-        queue["result_reasons"].index_fill_(0, index, 0)  # delivered: the result rows may be reused
+        # a finished request's result row is stable until the host marks it delivered, so it is read on the
+        # read stream while the caller's stream goes on with later work
+        with torch.cuda.stream(self._read_stream):
+            index = torch.tensor([rid % ring for rid in done], device=dev)
+            lengths = queue["result_lengths"][index].cpu().tolist()
+            longest = max(lengths)
+            tokens = self.state.tokens[:, :longest].index_select(0, index).cpu().tolist()
+            logprobs = self.state.logprobs[:, :longest].index_select(0, index).cpu().tolist()
+            queue["result_reasons"].index_fill_(0, index, 0)  # delivered: the result rows may be reused
         results = []
         for rid, length, ids, probs in zip(done, lengths, tokens, logprobs):
             prompt, sampling, _ = self._queued.pop(rid)
@@ -645,6 +703,9 @@ class LFM25GenerationSession:
     def close(self):
         if not self.closed:
             self.closed = True
+            self._poll_pending = None
+            if self._read_stream is not None:  # reads in flight finish before the state they read is reused
+                torch.cuda.current_stream(self.engine.device).wait_stream(self._read_stream)
             self.requests = [None] * self.batch_size
             self.state.alive.zero_()
             self.state.pending.zero_()

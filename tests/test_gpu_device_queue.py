@@ -118,6 +118,43 @@ def test_twelve_requests_over_three_slots_without_host_release_or_admit(dev):
             assert trace["argmax"][0].tolist() == list(done[i].token_ids)
 
 
+def test_parking_between_the_two_halves_of_a_poll_gives_the_same_requests(dev):
+    """poll_begin launches the steps, the host parks the next prompts behind them, poll_end reads the results on
+    a stream of its own: every request comes out as with plain polls (a request's stream depends on its prompt
+    and seed alone), and the calls refuse to be mixed up."""
+    engine = make_engine(dev, torch.float32)
+    prompts, samplings = requests()
+    plain, _, _ = run_device_queue(engine, prompts, samplings)
+    done, rounds = {}, 0
+    with engine.generation_session(max_batch_size=3, max_new_tokens=40, cache_len=128, queue_capacity=4) as session:
+        with pytest.raises(RuntimeError, match="poll_begin first"):
+            session.poll_end()
+        waiting = list(range(len(prompts)))
+
+        def park():
+            take = min(len(waiting), session.queue_space())
+            if take:
+                ids = [waiting.pop(0) for _ in range(take)]
+                session.enqueue([prompts[i] for i in ids], [samplings[i] for i in ids])
+
+        park()
+        while waiting or len(done) < len(prompts):
+            session.poll_begin(steps=8)
+            with pytest.raises(RuntimeError, match="poll_end the previous poll"):
+                session.poll_begin(steps=8)
+            park()  # with the free count of the previous poll_end
+            for result in session.poll_end():
+                done[result.request_id] = result
+            rounds += 1
+            assert rounds < 200
+        assert session.last_context[1] == 0.0, "no live row is left"
+        assert session.poll(steps=1) == []
+        assert session.cache.free_pages() == session.cache.n_pages
+    for i in range(12):
+        assert done[i].token_ids == plain[i].token_ids and done[i].finish_reason == plain[i].finish_reason
+        assert np.allclose(done[i].logprobs, plain[i].logprobs, atol=1e-6)
+
+
 def test_eos_finishes_are_evicted_and_the_queue_keeps_order(dev):
     """Requests that end on EOS (forced through the stop-token path) free their slot inside the graph; the
     next parked request takes the lowest free slot."""
