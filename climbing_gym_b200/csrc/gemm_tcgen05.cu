@@ -7,7 +7,11 @@
 // slice, TMA brings a [128 x 128B] weight tile and a [UN x 128B] activation tile into shared memory
 // with the 128-byte swizzle the UMMA descriptors expect; one elected thread issues tcgen05.mma
 // (fp32 accumulate in TMEM), tcgen05.commit releases the stage, and four epilogue warps read the
-// accumulator back with tcgen05.ld and write y (coalesced along N), applying scales / row mask.
+// accumulator back with tcgen05.ld, turn it (lane = feature) into token rows through shared memory and
+// write y in 16-byte row segments, applying scales / row mask / row map. While the MMAs run, the same
+// warps resolve where each token row of the tile goes (row mask, row map, M edge) and its activation
+// scale into shared memory and fetch the weight scales, so nothing between the accumulator and the
+// store depends on global memory.
 // Warp roles: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = epilogue.
 //
 // Split-K (grid.z <= 8) runs as a thread-block cluster: each CTA parks its fp32 partial tile - in the
