@@ -514,6 +514,251 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
   }
 }
 
+// ---- CTA-pair form (tcgen05.mma.cta_group::2) --------------------------------------------------
+// Two CTAs of a cluster (an SM pair) compute one [256 features x 256 tokens] tile: each stages its own 128
+// weight rows and HALF of the token tile (128 rows), the leader (cluster rank 0) issues one MMA of M = 256,
+// N = 256 per K step that reads both CTAs' shared memory and writes 128 accumulator lanes x 256 columns into
+// EACH CTA's TMEM, and every CTA runs the epilogue for its own 128 features. Per FLOP a CTA moves the bytes of
+// the single-CTA 256 x 256 tile, but it needs only 256 TMEM columns and a half-SM ring, so two pairs share an
+// SM pair and one CTA's epilogue runs under the other's main loop.
+// Protocol: both CTAs' copies complete on the LEADER's full barrier (the peer names it with mapa; the leader
+// expects both stages' bytes); the leader's
+// MMA thread commits every stage twice: to its own `done` barrier and, through the peer's mapped address, to
+// the peer's `empty` barrier (a relay by remote arrive from the leader's producer added a microsecond and
+// a half to the peer's refill loop and left the pair at 60 % of the tensor pipe); the accumulator barrier
+// likewise. Every copy is a plain per-CTA TMA load. TMEM is allocated and freed by
+// warp 1 of both CTAs with the cta_group::2 forms, the free after a cluster barrier.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local_addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(local_addr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t leader_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc, bool fp8) {
+  if (fp8)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+constexpr int PAIR_TOKENS = 256;  // token tile of a pair
+constexpr int PAIR_HALF = 128;    // token rows a CTA stages
+constexpr int PAIR_STAGES = 3;
+constexpr int PAIR_EPILOGUE_GROUP = 2;
+
+template <bool FP8>
+__global__ void __launch_bounds__(GEMM_THREADS, 2)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                 GemmEpilogue ep) {
+  constexpr int UN = PAIR_TOKENS, STAGES = PAIR_STAGES;
+  constexpr int W_BYTES = UM * SLICE_BYTES, STAGE_BYTES = W_BYTES + PAIR_HALF * SLICE_BYTES;
+  constexpr int ELEMS_PER_SLICE = FP8 ? 128 : 64;
+  constexpr int TMEM_COLS = UN;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[STAGES];   // leader: both CTAs' copies of a stage have landed
+  __shared__ __align__(8) uint64_t bar_done[STAGES];   // leader: the MMAs that read a stage have completed
+  __shared__ __align__(8) uint64_t bar_empty[STAGES];  // peer: the leader passed `done` on
+  __shared__ __align__(8) uint64_t bar_acc;            // the accumulator is complete (peer: passed on by the leader)
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  __shared__ int32_t row_out[UN];
+  __shared__ __align__(16) float row_scale[UN];
+
+  // No early griddepcontrol.launch_dependents here: a pair needs the SAME free TMEM columns on both of its SMs,
+  // and clusters can become resident late (the stragglers seen with split-K clusters). A successor GEMM of a
+  // dependent-launch chain that became resident early would allocate TMEM columns and then wait for this grid,
+  // while a late pair of this grid waits for those columns: a cycle of two unbounded waits. Without the trigger
+  // the successor starts when every CTA of this grid has exited. (w13 of a 256-row decode step routed through
+  // this kernel with the trigger hung exactly so.)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t tiles = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int n0 = blockIdx.x * UM, m0 = blockIdx.y * UN;
+  const int n_kb = (ep.K + ELEMS_PER_SLICE - 1) / ELEMS_PER_SLICE;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_done[s]), 1);
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bar_acc), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  // both CTAs' barriers exist before either touches the other's
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_acc = tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer (both CTAs) ----
+    const int x_row = m0 + static_cast<int>(rank) * PAIR_HALF;
+    const uint32_t full0 = leader ? smem_u32(&bar_full[0]) : map_to_cta(smem_u32(&bar_full[0]), 0);
+    auto load = [&](uint32_t dst, const CUtensorMap* map, uint32_t full, int x, int y) {
+      if (leader) tma_load_2d(dst, map, full, x, y);
+      else tma_load_2d_pair(dst, map, full, x, y);  // completes on the leader's barrier
+    };
+    // weights never depend on the previous kernel: the first ring of weight tiles goes out before the wait
+    const int prefetch = n_kb < STAGES ? n_kb : STAGES;
+    for (int i = 0; i < prefetch; ++i) {
+      const uint32_t full = full0 + static_cast<uint32_t>(i) * 8u;
+      if (leader) mbar_expect_tx(full, 2 * STAGE_BYTES);
+      load(tiles + i * STAGE_BYTES, &tmap_w, full, i * ELEMS_PER_SLICE, n0);
+    }
+    pdl_wait();
+    for (int i = 0; i < prefetch; ++i)
+      load(tiles + i * STAGE_BYTES + W_BYTES, &tmap_x, full0 + static_cast<uint32_t>(i) * 8u, i * ELEMS_PER_SLICE, x_row);
+    for (int i = prefetch; i < n_kb; ++i) {
+      const int s = i % STAGES;
+      // leader: the MMAs that read the stage have completed; peer: the leader's MMA thread said so
+      const uint32_t freed = smem_u32(leader ? &bar_done[s] : &bar_empty[s]);
+      if (!mbar_wait(freed, ((i / STAGES) & 1) ^ 1, &abort_flag)) break;
+      const uint32_t full = full0 + static_cast<uint32_t>(s) * 8u;
+      if (leader) mbar_expect_tx(full, 2 * STAGE_BYTES);
+      const uint32_t a_dst = tiles + s * STAGE_BYTES;
+      load(a_dst, &tmap_w, full, i * ELEMS_PER_SLICE, n0);
+      load(a_dst + W_BYTES, &tmap_x, full, i * ELEMS_PER_SLICE, x_row);
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---- MMA issuer (leader only): M = 256 (128 features per CTA), N = 256 tokens (128 staged per CTA) ----
+    uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(UN >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
+    if (!FP8) idesc |= (1u << 7) | (1u << 10);
+    const uint32_t peer_empty = map_to_cta(smem_u32(&bar_empty[0]), 1);
+    for (int i = 0; i < n_kb; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(smem_u32(&bar_full[s]), (i / STAGES) & 1, &abort_flag)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a_src = tiles + s * STAGE_BYTES, b_src = a_src + W_BYTES;
+      const uint64_t da = umma_smem_desc(a_src), db = umma_smem_desc(b_src);
+#pragma unroll
+      for (int k = 0; k < SLICE_BYTES / 32; ++k)
+        umma_pair(tmem_acc, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u, FP8);
+      umma_commit_pair(smem_u32(&bar_done[s]));
+      umma_commit_pair(peer_empty + static_cast<uint32_t>(s) * 8u);  // the peer may refill its half of the stage
+    }
+    umma_commit_pair(smem_u32(&bar_acc));
+    umma_commit_pair(map_to_cta(smem_u32(&bar_acc), 1));
+  } else if (warp >= 2) {
+    // ---- epilogue (both CTAs): TMEM lane = one of this CTA's 128 features, column = token of the pair's tile ----
+    const int quarter = warp & 3;
+    const int n_local = quarter * 32 + lane, n = n0 + n_local;
+    const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
+    pdl_wait();  // activation scales / row mask come from earlier kernels of the step
+    for (int ml = static_cast<int>(threadIdx.x) - 64; ml < UN; ml += 128) {
+      const int m = m0 + ml;
+      int out = -1;
+      float xs = 1.0f;
+      if (m < ep.M && (ep.row_mask == nullptr || ep.row_mask[m])) {
+        out = ep.row_map != nullptr ? ep.row_map[m] : m;
+        if (ep.x_scales != nullptr) xs = ep.x_scales[m];
+      }
+      row_out[ml] = out;
+      row_scale[ml] = xs;
+    }
+    if (n_kb > 0) mbar_wait(smem_u32(&bar_acc), 0, &abort_flag);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (abort_flag == 0) {
+      const bool wide = (ep.N & 7) == 0 && n0 + UM <= ep.N;
+      const bool scaled = ep.x_scales != nullptr;
+      const bool live = n_kb > 0;
+      __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem_raw + (tiles - smem_u32(smem_raw))) + quarter * 1024;
+      auto emit = [&](int c, const uint32_t (&v)[32]) {
+        if (wide) {
+#pragma unroll
+          for (int j0 = 0; j0 < 32; j0 += 8) {
+            float xs[8];
+            *reinterpret_cast<float4*>(&xs[0]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0]);
+            *reinterpret_cast<float4*>(&xs[4]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0 + 4]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float val = __uint_as_float(v[j0 + j]);
+              if (scaled) val = __fmul_rn(__fmul_rn(val, xs[j]), ws);
+              stage[(j0 + j) * 32 + lane] = __float2bfloat16_rn(val);
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int pass = 0; pass < 4; ++pass) {
+            const int row = pass * 8 + (lane >> 2);
+            const uint4 word = *reinterpret_cast<const uint4*>(stage + row * 32 + (lane & 3) * 8);
+            const int out_row = row_out[c * 32 + row];
+            if (out_row >= 0)
+              *reinterpret_cast<uint4*>(ep.y + static_cast<int64_t>(out_row) * ep.N + n0 + quarter * 32 + (lane & 3) * 8) = word;
+          }
+          __syncwarp();
+        } else if (n < ep.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int out_row = row_out[c * 32 + j];
+            if (out_row < 0) continue;
+            float val = __uint_as_float(v[j]);
+            if (scaled) val = __fmul_rn(__fmul_rn(val, row_scale[c * 32 + j]), ws);
+            ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
+          }
+        }
+      };
+      constexpr int GROUP = PAIR_EPILOGUE_GROUP;  // blocks of 32 columns fetched per TMEM wait
+#pragma unroll 1
+      for (int c0 = 0; c0 < UN / 32; c0 += GROUP) {
+        uint32_t v[GROUP][32];
+#pragma unroll
+        for (int g = 0; g < GROUP; ++g) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[g][j] = 0u;
+          if (live) tmem_issue32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>((c0 + g) * 32), v[g]);
+        }
+        if (live) {
+#pragma unroll
+          for (int g = 0; g < GROUP; ++g) tmem_wait32(v[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < GROUP; ++g) emit(c0 + g, v[g]);
+      }
+    }
+  }
+
+  // neither CTA frees its half of the pair's TMEM, or leaves, while the other may still use it
+  __syncwarp();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (threadIdx.x == 0 && abort_flag) atomicOr(ep.status, CGYM_STATUS_WAIT_TIMEOUT);
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_acc), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -583,6 +828,36 @@ static int launch_tile(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
 }
 
 
+template <bool FP8>
+static int launch_pair(const CUtensorMap& mw, const CUtensorMap& mx, const GemmEpilogue& ep, dim3 grid,
+                       cudaStream_t stream) {
+  constexpr int SMEM = PAIR_STAGES * (UM + PAIR_HALF) * SLICE_BYTES + 1024;
+  static SmemReservation reservation;
+  if (int rc = reserve_dynamic_smem(gemm_pair_kernel<FP8>, SMEM, reservation, "gemm(pair)")) return rc;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = dim3(GEMM_THREADS);
+  config.dynamicSmemBytes = SMEM;
+  config.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n_attrs = 0;
+  attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;  // consecutive feature tiles form the pair
+  attrs[n_attrs].val.clusterDim.x = 2;
+  attrs[n_attrs].val.clusterDim.y = 1;
+  attrs[n_attrs].val.clusterDim.z = 1;
+  ++n_attrs;
+  if (g_pdl_enabled) {
+    attrs[n_attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n_attrs].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attrs;
+  }
+  config.attrs = attrs;
+  config.numAttrs = n_attrs;
+  const cudaError_t rc = cudaLaunchKernelEx(&config, gemm_pair_kernel<FP8>, mw, mx, ep);
+  CGYM_REQUIRE(rc == cudaSuccess, "gemm(pair): launch failed: %s", cudaGetErrorString(rc));
+  return check_launch("gemm_pair");
+}
+
 bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const void* w) {
   const int elem = fp8 ? 1 : 2;
   if (M <= 0 || N <= 0 || K <= 0) return false;
@@ -598,6 +873,21 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
                "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
   CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
+  // CTA pairs (256 features x 256 tokens per pair, unsplit, two CTAs per SM) where they measured faster than
+  // the single-CTA tiles: prefill-sized token counts with a contraction of up to 4096 (w13, in-projection, qkv,
+  // out-projection: +3..7 %; at K = 8192 the single CTA's deeper stages win by 1 %), and the LM head of a full
+  // decode batch (+8 %).
+  const bool pair_auto = force_splits == 0 && N % (2 * UM) == 0 &&
+                         ((M > 256 && K <= 4096) || (M > 128 && M <= 256 && N / (2 * UM) >= 148));
+  if (force_splits == -2 || pair_auto) {
+    CGYM_REQUIRE(N % (2 * UM) == 0, "gemm(pair): the feature count must be a multiple of 256");
+    CUtensorMap mw, mx;
+    if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
+    if (int rc = make_map(&mx, x, M, K, PAIR_HALF, fp8)) return rc;
+    GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, row_map, status, M, N, K, 0, nullptr};
+    const dim3 grid(N / UM, (M + PAIR_TOKENS - 1) / PAIR_TOKENS, 1);
+    return fp8 ? launch_pair<true>(mw, mx, ep, grid, stream) : launch_pair<false>(mw, mx, ep, grid, stream);
+  }
   // Token tile: the smallest that covers M up to 128; up to 256 rows (a full decode batch) tiles of 128
   // or 64 keep the weight-streaming layout (half-SM rings, split-K) - the other tiles' weight loads hit
   // L2 - and only larger M (prefill) takes the 256-token tile that halves L2 -> SM traffic per FLOP.

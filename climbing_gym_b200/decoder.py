@@ -10,7 +10,9 @@ rows are masked inside the kernels instead of being compacted on the host.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
+import gc
 from collections import OrderedDict
 from dataclasses import dataclass, field
 
@@ -22,6 +24,23 @@ from .model import ForwardBuffers, LFM25Runner
 from .paged import PagedHybridCache
 from .text_stops import build_token_sequence_table, product_stop_table
 from .types import LFM25GenerationOutput
+
+
+@contextlib.contextmanager
+def _quiet_collector():
+    """Stream capture must not see the cyclic garbage collector at work: a decode graph that was evicted from
+    the cache (or belonged to an engine that is gone) and is only kept alive by a reference cycle would be
+    destroyed whenever the collector happens to run, and destroying a CUDA graph while another one is being
+    captured is an operation the capture does not permit (it is invalidated: "operation not permitted when
+    stream is capturing"). Collect what is garbage now, outside the capture, and hold the collector until it ends."""
+    gc.collect()
+    enabled = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if enabled:
+            gc.enable()
 
 
 class SlotState:
@@ -456,7 +475,7 @@ class B200Decoder:
             torch.cuda.synchronize(engine.device)
             graph = torch.cuda.CUDAGraph()
             before = lib.cgym_launch_count()
-            with torch.cuda.graph(graph, stream=stream):
+            with _quiet_collector(), torch.cuda.graph(graph, stream=stream):
                 self._step(entry)
             current.wait_stream(stream)
             entry.graph = _StepGraph(graph, int(lib.cgym_launch_count() - before))
@@ -529,7 +548,7 @@ class B200Decoder:
             torch.cuda.synchronize(dev)
             graph = torch.cuda.CUDAGraph()
             before = lib.cgym_launch_count()
-            with torch.cuda.graph(graph, stream=stream):
+            with _quiet_collector(), torch.cuda.graph(graph, stream=stream):
                 self._compact_step(entry, rows, slots, tokens, positions, active, kv_lens, bufs, sample=True)
             current.wait_stream(stream)
             step = _StepGraph(graph, int(lib.cgym_launch_count() - before))

@@ -493,6 +493,48 @@ def test_gemm_fp8_scaled_epilogue(dev, impl, shape):
 DECODE_WS_BYTES = 2 * 148 * 128 * 128 * 4  # the engine's GEMM workspace: one fp32 partial tile per resident CTA
 
 
+@pytest.mark.parametrize("shape", [(256, 256, 512), (200, 512, 256), (300, 1024, 2048), (1000, 2048, 448), (64, 768, 128)])
+def test_gemm_cta_pair_form(dev, shape):
+    """impl 4: two CTAs of a cluster share one 256 x 256 tile (tcgen05.mma.cta_group::2, each CTA stages half of the
+    token tile, both copies complete on the leader's barrier). Same contract as the single-CTA kernel: fp32
+    accumulation, row mask, row map, FP8 scales, ragged M and a K that is not a multiple of the ring."""
+    m, n, k = shape
+    rng = np.random.default_rng(m * 3 + n + k)
+    x_np, w_np = round_bf16(rng.standard_normal((m, k))), round_bf16(rng.standard_normal((n, k)) * 0.1)
+    want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
+    x, w = bf(x_np, dev), bf(w_np, dev)
+    y = gemm_call(dev, x, w, impl=4)
+    assert_gemm_close(f32(y), want, exact_fraction=0.97, what=f"pair {shape}")
+    out_rows = m + 7
+    row_map = rng.permutation(out_rows)[:m].astype(np.int32)
+    row_map[rng.random(m) < 0.2] = -1
+    mask = (rng.random(m) < 0.7).astype(np.uint8)
+    written = (row_map >= 0) & (mask == 1)
+    status = torch.zeros(1, device=dev, dtype=torch.int32)
+    dmap, dmask = torch.from_numpy(row_map).to(dev), torch.from_numpy(mask).to(dev)
+    ys = torch.full((out_rows, n), -3.0, device=dev, dtype=torch.bfloat16)
+    nv.call("cgym_gemm_scatter", nv.ptr(ys), nv.ptr(x), nv.ptr(w), nv.ptr(dmask), nv.ptr(dmap), m, n, k,
+            nv.dtype_code(torch.bfloat16), 4, None, 0, nv.ptr(status), stream())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = f32(ys)
+    untouched = np.ones(out_rows, dtype=bool)
+    untouched[row_map[written]] = False
+    assert np.all(got[untouched] == -3.0)
+    assert_gemm_close(got[row_map[written]], want[written], exact_fraction=0.97, what=f"pair scatter {shape}")
+    if k % 128 == 0:
+        xq, xs = ok.quantize_rows(round_bf16(rng.standard_normal((m, k))))
+        wq, wsc = ok.quantize_rows(round_bf16(rng.standard_normal((n, k)) * 0.05))
+        want8 = ok.fp8_matmul(xq, xs, wq, wsc)
+        args = [torch.from_numpy(a).to(dev) for a in (xq, xs, wq, wsc)]
+        y8 = torch.zeros((m, n), device=dev, dtype=torch.bfloat16)
+        nv.call("cgym_gemm_fp8", nv.ptr(y8), nv.ptr(args[0]), nv.ptr(args[1]), nv.ptr(args[2]), nv.ptr(args[3]), None,
+                m, n, k, 4, None, 0, nv.ptr(status), stream())
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert_gemm_close(f32(y8), want8, exact_fraction=0.97, what=f"pair fp8 {shape}")
+
+
 def test_gemm_bounded_wait_gives_up_and_the_context_survives(dev):
     """A wait that nothing satisfies (the producer arms its barriers but copies no tile: test hook) runs into the
     shortened limit; the kernel raises CGYM_STATUS_WAIT_TIMEOUT in the status word, frees its TMEM and returns.
