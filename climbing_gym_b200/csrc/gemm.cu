@@ -20,13 +20,13 @@ extern "C" int cgym_gemm_scatter(void* y, const void* x, const void* w, const ui
                                  int64_t workspace_bytes, int32_t* status, cgym_stream_t stream) {
   CGYM_REQUIRE(M >= 0 && N > 0 && K > 0, "gemm: bad shape (%d, %d, %d)", M, N, K);
   CGYM_REQUIRE(y && x && w, "gemm: null operand");
-  CGYM_REQUIRE(impl >= 0 && impl <= 4, "gemm: impl must be 0 (auto), 1 (simt), 2 (tcgen05), 3 (tcgen05, forced split-K) or 4 (tcgen05, CTA pairs)");
+  CGYM_REQUIRE(impl >= 0 && impl <= 5, "gemm: impl must be 0 (auto), 1 (simt), 2 (tcgen05), 3 (forced split-K), 4 (CTA pairs) or 5 (persistent CTA pairs)");
   if (M == 0) return 0;
   if (impl == 0) impl = (dtype == CGYM_BF16 && gemm_tcgen05_supports(M, N, K, false, x, w)) ? 2 : 1;
   if (impl >= 2) {
     CGYM_REQUIRE(dtype == CGYM_BF16, "gemm(tcgen05): bf16 operands only");
     return launch_gemm_tcgen05(y, x, w, nullptr, nullptr, row_mask, row_map, M, N, K, false, workspace,
-                               workspace_bytes, status, impl == 3 ? 4 : (impl == 4 ? -2 : 0), as_stream(stream));
+                               workspace_bytes, status, impl == 3 ? 4 : (impl == 4 ? -2 : (impl == 5 ? -3 : 0)), as_stream(stream));
   }
   return launch_gemm_simt(y, x, w, nullptr, nullptr, row_mask, row_map, M, N, K, dtype, as_stream(stream));
 }
@@ -44,12 +44,12 @@ extern "C" int cgym_gemm_fp8_scatter(void* y, const uint8_t* xq, const float* x_
                                      int32_t* status, cgym_stream_t stream) {
   CGYM_REQUIRE(M >= 0 && N > 0 && K > 0, "gemm_fp8: bad shape (%d, %d, %d)", M, N, K);
   CGYM_REQUIRE(y && xq && wq && x_scales && w_scales, "gemm_fp8: null operand");
-  CGYM_REQUIRE(impl >= 0 && impl <= 4, "gemm_fp8: impl must be 0..4");
+  CGYM_REQUIRE(impl >= 0 && impl <= 5, "gemm_fp8: impl must be 0..5");
   if (M == 0) return 0;
   if (impl == 0) impl = gemm_tcgen05_supports(M, N, K, true, xq, wq) ? 2 : 1;
   if (impl >= 2)
     return launch_gemm_tcgen05(y, xq, wq, x_scales, w_scales, row_mask, row_map, M, N, K, true, workspace,
-                               workspace_bytes, status, impl == 3 ? 4 : (impl == 4 ? -2 : 0), as_stream(stream));
+                               workspace_bytes, status, impl == 3 ? 4 : (impl == 4 ? -2 : (impl == 5 ? -3 : 0)), as_stream(stream));
   return launch_gemm_simt(y, xq, wq, x_scales, w_scales, row_mask, row_map, M, N, K, CGYM_E4M3, as_stream(stream));
 }
 

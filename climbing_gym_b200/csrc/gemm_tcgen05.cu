@@ -759,6 +759,206 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   }
 }
 
+// Persistent CTA-pair form for prefill-sized token counts: one pair per SM pair walks over the output tiles
+// (tile t, t + pairs, ...), a six-stage ring (192 KB) streams without a break from one tile into the next, and
+// the 512 TMEM columns hold TWO accumulators of 256 columns, so the epilogue of tile j (TMEM -> bf16 rows ->
+// global, through a staging block of its own) runs under the main loop of tile j + 1 in the same CTA. Barriers
+// beyond the one-tile form: acc_full[2] (leader commits to its own and to the peer's) and, in the leader,
+// acc_empty[2] with two arrivals per use: the leader's and the peer's epilogue have both read the buffer.
+constexpr int PP_STAGES = 6;
+
+template <bool FP8>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                            GemmEpilogue ep, int pairs_n, int n_tiles_total) {
+  constexpr int UN = PAIR_TOKENS, STAGES = PP_STAGES;
+  constexpr int W_BYTES = UM * SLICE_BYTES, STAGE_BYTES = W_BYTES + PAIR_HALF * SLICE_BYTES;
+  constexpr int ELEMS_PER_SLICE = FP8 ? 128 : 64;
+  constexpr int TMEM_COLS = 2 * UN;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[STAGES], bar_done[STAGES], bar_empty[STAGES];
+  __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  __shared__ int32_t row_out[UN];
+  __shared__ __align__(16) float row_scale[UN];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t tiles = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t stage_block = tiles + STAGES * STAGE_BYTES;  // 4 x 2 KB of epilogue staging behind the ring
+  const int n_kb = (ep.K + ELEMS_PER_SLICE - 1) / ELEMS_PER_SLICE;
+  const int pair_id = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int my_tiles = pair_id < n_tiles_total ? (n_tiles_total - pair_id + n_pairs - 1) / n_pairs : 0;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_done[s]), 1);
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&bar_acc_full[b]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[b]), 2);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_acc = tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer (both CTAs): one stream of K slices over all of the pair's tiles ----
+    const uint32_t full0 = leader ? smem_u32(&bar_full[0]) : map_to_cta(smem_u32(&bar_full[0]), 0);
+    pdl_wait();
+    int g = 0;
+    bool ok = true;
+    for (int j = 0; ok && j < my_tiles; ++j) {
+      const int t = pair_id + j * n_pairs;
+      const int n0 = ((t % pairs_n) * 2 + static_cast<int>(rank)) * UM;
+      const int x_row = (t / pairs_n) * UN + static_cast<int>(rank) * PAIR_HALF;
+      for (int i = 0; i < n_kb; ++i, ++g) {
+        const int s = g % STAGES;
+        if (g >= STAGES) {
+          const uint32_t freed = smem_u32(leader ? &bar_done[s] : &bar_empty[s]);
+          if (!mbar_wait(freed, ((g / STAGES) & 1) ^ 1, &abort_flag)) { ok = false; break; }
+        }
+        const uint32_t full = full0 + static_cast<uint32_t>(s) * 8u;
+        const uint32_t a_dst = tiles + s * STAGE_BYTES;
+        if (leader) {
+          mbar_expect_tx(full, 2 * STAGE_BYTES);
+          tma_load_2d(a_dst, &tmap_w, full, i * ELEMS_PER_SLICE, n0);
+          tma_load_2d(a_dst + W_BYTES, &tmap_x, full, i * ELEMS_PER_SLICE, x_row);
+        } else {
+          tma_load_2d_pair(a_dst, &tmap_w, full, i * ELEMS_PER_SLICE, n0);
+          tma_load_2d_pair(a_dst + W_BYTES, &tmap_x, full, i * ELEMS_PER_SLICE, x_row);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---- MMA issuer (leader only) ----
+    uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(UN >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
+    if (!FP8) idesc |= (1u << 7) | (1u << 10);
+    const uint32_t peer_empty = map_to_cta(smem_u32(&bar_empty[0]), 1);
+    const uint32_t peer_acc_full = map_to_cta(smem_u32(&bar_acc_full[0]), 1);
+    int g = 0;
+    bool ok = true;
+    for (int j = 0; ok && j < my_tiles; ++j) {
+      const int b = j & 1;
+      // both epilogues have read what tile j - 2 left in this buffer
+      if (j >= 2 && !mbar_wait(smem_u32(&bar_acc_empty[b]), ((j >> 1) & 1) ^ 1, &abort_flag)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      for (int i = 0; i < n_kb; ++i, ++g) {
+        const int s = g % STAGES;
+        if (!mbar_wait(smem_u32(&bar_full[s]), (g / STAGES) & 1, &abort_flag)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_src = tiles + s * STAGE_BYTES, b_src = a_src + W_BYTES;
+        const uint64_t da = umma_smem_desc(a_src), db = umma_smem_desc(b_src);
+#pragma unroll
+        for (int k = 0; k < SLICE_BYTES / 32; ++k)
+          umma_pair(tmem_acc + static_cast<uint32_t>(b * UN), da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u, FP8);
+        umma_commit_pair(smem_u32(&bar_done[s]));
+        umma_commit_pair(peer_empty + static_cast<uint32_t>(s) * 8u);
+      }
+      if (!ok) break;
+      umma_commit_pair(smem_u32(&bar_acc_full[b]));
+      umma_commit_pair(peer_acc_full + static_cast<uint32_t>(b) * 8u);
+    }
+  } else if (warp >= 2) {
+    // ---- epilogue (both CTAs), one tile behind the MMAs ----
+    const int quarter = warp & 3;
+    const uint32_t leader_acc_empty = map_to_cta(smem_u32(&bar_acc_empty[0]), 0);
+    pdl_wait();
+    const bool scaled = ep.x_scales != nullptr;
+    __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem_raw + (stage_block - smem_u32(smem_raw))) + quarter * 1024;
+    for (int j = 0; j < my_tiles; ++j) {
+      const int b = j & 1, t = pair_id + j * n_pairs;
+      const int n0 = ((t % pairs_n) * 2 + static_cast<int>(rank)) * UM, m0 = (t / pairs_n) * UN;
+      const int n = n0 + quarter * 32 + lane;
+      const float ws = (ep.w_scales != nullptr && n < ep.N) ? ep.w_scales[n] : 1.0f;
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous tile's rows are no longer read
+      for (int ml = static_cast<int>(threadIdx.x) - 64; ml < UN; ml += 128) {
+        const int m = m0 + ml;
+        int out = -1;
+        float xs = 1.0f;
+        if (m < ep.M && (ep.row_mask == nullptr || ep.row_mask[m])) {
+          out = ep.row_map != nullptr ? ep.row_map[m] : m;
+          if (scaled) xs = ep.x_scales[m];
+        }
+        row_out[ml] = out;
+        row_scale[ml] = xs;
+      }
+      const bool got = mbar_wait(smem_u32(&bar_acc_full[b]), (j >> 1) & 1, &abort_flag);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (!got || abort_flag) break;
+      const bool wide = (ep.N & 7) == 0 && n0 + UM <= ep.N;
+#pragma unroll 1
+      for (int c = 0; c < UN / 32; ++c) {
+        uint32_t v[32];
+        tmem_issue32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(b * UN + c * 32), v);
+        tmem_wait32(v);
+        if (wide) {
+#pragma unroll
+          for (int j0 = 0; j0 < 32; j0 += 8) {
+            float xs[8];
+            *reinterpret_cast<float4*>(&xs[0]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0]);
+            *reinterpret_cast<float4*>(&xs[4]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0 + 4]);
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              float val = __uint_as_float(v[j0 + jj]);
+              if (scaled) val = __fmul_rn(__fmul_rn(val, xs[jj]), ws);
+              stage[(j0 + jj) * 32 + lane] = __float2bfloat16_rn(val);
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int pass = 0; pass < 4; ++pass) {
+            const int row = pass * 8 + (lane >> 2);
+            const uint4 word = *reinterpret_cast<const uint4*>(stage + row * 32 + (lane & 3) * 8);
+            const int out_row = row_out[c * 32 + row];
+            if (out_row >= 0)
+              *reinterpret_cast<uint4*>(ep.y + static_cast<int64_t>(out_row) * ep.N + n0 + quarter * 32 + (lane & 3) * 8) = word;
+          }
+          __syncwarp();
+        } else if (n < ep.N) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int out_row = row_out[c * 32 + jj];
+            if (out_row < 0) continue;
+            float val = __uint_as_float(v[jj]);
+            if (scaled) val = __fmul_rn(__fmul_rn(val, row_scale[c * 32 + jj]), ws);
+            ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
+          }
+        }
+      }
+      // this CTA's four warps have read the buffer: one arrival per CTA on the leader's barrier
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64)
+        asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(leader_acc_empty + static_cast<uint32_t>(b) * 8u) : "memory");
+    }
+  }
+
+  __syncwarp();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (threadIdx.x == 0 && abort_flag) atomicOr(ep.status, CGYM_STATUS_WAIT_TIMEOUT);
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_acc), "r"(TMEM_COLS) : "memory");
+  }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -858,6 +1058,38 @@ static int launch_pair(const CUtensorMap& mw, const CUtensorMap& mx, const GemmE
   return check_launch("gemm_pair");
 }
 
+template <bool FP8>
+static int launch_pair_persistent(const CUtensorMap& mw, const CUtensorMap& mx, const GemmEpilogue& ep, int pairs_n,
+                                  int m_tiles, cudaStream_t stream) {
+  constexpr int SMEM = PP_STAGES * (UM + PAIR_HALF) * SLICE_BYTES + 4 * 2048 + 1024;
+  static SmemReservation reservation;
+  if (int rc = reserve_dynamic_smem(gemm_pair_persistent_kernel<FP8>, SMEM, reservation, "gemm(pair, persistent)")) return rc;
+  const int n_tiles_total = pairs_n * m_tiles;
+  const int pairs = n_tiles_total < 74 ? n_tiles_total : 74;  // one pair per SM pair
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(2 * pairs);
+  config.blockDim = dim3(GEMM_THREADS);
+  config.dynamicSmemBytes = SMEM;
+  config.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n_attrs = 0;
+  attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;
+  attrs[n_attrs].val.clusterDim.x = 2;
+  attrs[n_attrs].val.clusterDim.y = 1;
+  attrs[n_attrs].val.clusterDim.z = 1;
+  ++n_attrs;
+  if (g_pdl_enabled) {
+    attrs[n_attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n_attrs].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attrs;
+  }
+  config.attrs = attrs;
+  config.numAttrs = n_attrs;
+  const cudaError_t rc = cudaLaunchKernelEx(&config, gemm_pair_persistent_kernel<FP8>, mw, mx, ep, pairs_n, n_tiles_total);
+  CGYM_REQUIRE(rc == cudaSuccess, "gemm(pair, persistent): launch failed: %s", cudaGetErrorString(rc));
+  return check_launch("gemm_pair_persistent");
+}
+
 bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const void* w) {
   const int elem = fp8 ? 1 : 2;
   if (M <= 0 || N <= 0 || K <= 0) return false;
@@ -873,19 +1105,25 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
                "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
   CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
-  // CTA pairs (256 features x 256 tokens per pair, unsplit, two CTAs per SM) where they measured faster than
-  // the single-CTA tiles: prefill-sized token counts with a contraction of up to 4096 (w13, in-projection, qkv,
-  // out-projection: +3..7 %; at K = 8192 the single CTA's deeper stages win by 1 %), and the LM head of a full
-  // decode batch (+8 %).
+  // CTA pairs (256 features x 256 tokens per pair, unsplit) where they measured faster than the single-CTA
+  // tiles: prefill-sized token counts with a contraction of up to 4096 (w13, in-projection, qkv: +5..10 % in
+  // the persistent form; at K = 8192, 128 tiles, both forms lose to the single CTA by their last round), and
+  // the LM head of a full decode batch (+8 %, one-tile form).
   const bool pair_auto = force_splits == 0 && N % (2 * UM) == 0 &&
                          ((M > 256 && K <= 4096) || (M > 128 && M <= 256 && N / (2 * UM) >= 148));
-  if (force_splits == -2 || pair_auto) {
+  if (force_splits == -2 || force_splits == -3 || pair_auto) {
     CGYM_REQUIRE(N % (2 * UM) == 0, "gemm(pair): the feature count must be a multiple of 256");
     CUtensorMap mw, mx;
     if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
     if (int rc = make_map(&mx, x, M, K, PAIR_HALF, fp8)) return rc;
     GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, row_map, status, M, N, K, 0, nullptr};
     const dim3 grid(N / UM, (M + PAIR_TOKENS - 1) / PAIR_TOKENS, 1);
+    // two rounds or more of tiles over the 74 SM pairs: the persistent form (epilogue under the next tile's main
+    // loop); fewer tiles leave it idle in its last round and the one-tile form with two CTAs per SM is as fast
+    const bool persistent = pair_auto && M > 256 && static_cast<int>(grid.x / 2 * grid.y) >= 2 * 74;
+    if (force_splits == -3 || persistent)
+      return fp8 ? launch_pair_persistent<true>(mw, mx, ep, N / (2 * UM), grid.y, stream)
+                 : launch_pair_persistent<false>(mw, mx, ep, N / (2 * UM), grid.y, stream);
     return fp8 ? launch_pair<true>(mw, mx, ep, grid, stream) : launch_pair<false>(mw, mx, ep, grid, stream);
   }
   // Token tile: the smallest that covers M up to 128; up to 256 rows (a full decode batch) tiles of 128

@@ -176,8 +176,9 @@ int cgym_prefill_attention(void* out, const void* q, const int32_t* tile_row0,
  * lfm25_cuda.py:124-126,141,166,170-172,180,192): y[M,N] = x[M,K] . w[N,K]^T, fp32 accumulate.
  * row_mask (uint8[M], optional): rows with 0 are not written (replaces the saved-logits
  * where-merge, lfm25_cuda.py:237-245). impl: 0 = auto, 1 = SIMT tile kernel, 2 = tcgen05/TMEM.
- * impl 3 = tcgen05 with split-K forced (test hook). Split-K runs inside a thread-block cluster and
- * is deterministic. workspace/workspace_bytes (optional, 16-byte aligned, contents irrelevant): when
+ * impl 3 = tcgen05 with split-K forced, 4 = CTA pairs (tcgen05.mma.cta_group::2, one 256 x 256 tile per
+ * pair; N must be a multiple of 256), 5 = persistent CTA pairs (test hooks: auto picks among them by
+ * shape). Split-K runs inside a thread-block cluster and is deterministic. workspace/workspace_bytes (optional, 16-byte aligned, contents irrelevant): when
  * it holds tiles * splits * token_tile * 128 fp32 (2 * 148 * token_tile * 512 bytes always suffice;
  * token_tile = 32 / 64 / 128 / 256 >= M) the partial tiles are exchanged through it (L2), which is
  * faster; without it they go through distributed shared memory, same bits. Launches that share a

@@ -493,17 +493,22 @@ def test_gemm_fp8_scaled_epilogue(dev, impl, shape):
 DECODE_WS_BYTES = 2 * 148 * 128 * 128 * 4  # the engine's GEMM workspace: one fp32 partial tile per resident CTA
 
 
-@pytest.mark.parametrize("shape", [(256, 256, 512), (200, 512, 256), (300, 1024, 2048), (1000, 2048, 448), (64, 768, 128)])
-def test_gemm_cta_pair_form(dev, shape):
+@pytest.mark.parametrize("impl,shape", [(4, (256, 256, 512)), (4, (200, 512, 256)), (4, (300, 1024, 2048)),
+                                        (4, (1000, 2048, 448)), (4, (64, 768, 128)),
+                                        (5, (256, 256, 512)), (5, (1000, 2048, 448)), (5, (2000, 4096, 256)),
+                                        (5, (3000, 8192, 256)), (5, (300, 512, 1024))])
+def test_gemm_cta_pair_form(dev, impl, shape):
     """impl 4: two CTAs of a cluster share one 256 x 256 tile (tcgen05.mma.cta_group::2, each CTA stages half of the
-    token tile, both copies complete on the leader's barrier). Same contract as the single-CTA kernel: fp32
-    accumulation, row mask, row map, FP8 scales, ragged M and a K that is not a multiple of the ring."""
+    token tile, both copies complete on the leader's barrier). impl 5: the persistent form, one pair per SM pair
+    walking over the tiles with two accumulators in TMEM (shapes with one, two and five tiles per pair). Same
+    contract as the single-CTA kernel: fp32 accumulation, row mask, row map, FP8 scales, ragged M and a K that is
+    not a multiple of the ring."""
     m, n, k = shape
     rng = np.random.default_rng(m * 3 + n + k)
     x_np, w_np = round_bf16(rng.standard_normal((m, k))), round_bf16(rng.standard_normal((n, k)) * 0.1)
     want = round_bf16((x_np.astype(np.float64) @ w_np.astype(np.float64).T).astype(np.float32))
     x, w = bf(x_np, dev), bf(w_np, dev)
-    y = gemm_call(dev, x, w, impl=4)
+    y = gemm_call(dev, x, w, impl=impl)
     assert_gemm_close(f32(y), want, exact_fraction=0.97, what=f"pair {shape}")
     out_rows = m + 7
     row_map = rng.permutation(out_rows)[:m].astype(np.int32)
@@ -514,7 +519,7 @@ def test_gemm_cta_pair_form(dev, shape):
     dmap, dmask = torch.from_numpy(row_map).to(dev), torch.from_numpy(mask).to(dev)
     ys = torch.full((out_rows, n), -3.0, device=dev, dtype=torch.bfloat16)
     nv.call("cgym_gemm_scatter", nv.ptr(ys), nv.ptr(x), nv.ptr(w), nv.ptr(dmask), nv.ptr(dmap), m, n, k,
-            nv.dtype_code(torch.bfloat16), 4, None, 0, nv.ptr(status), stream())
+            nv.dtype_code(torch.bfloat16), impl, None, 0, nv.ptr(status), stream())
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     got = f32(ys)
@@ -529,7 +534,7 @@ def test_gemm_cta_pair_form(dev, shape):
         args = [torch.from_numpy(a).to(dev) for a in (xq, xs, wq, wsc)]
         y8 = torch.zeros((m, n), device=dev, dtype=torch.bfloat16)
         nv.call("cgym_gemm_fp8", nv.ptr(y8), nv.ptr(args[0]), nv.ptr(args[1]), nv.ptr(args[2]), nv.ptr(args[3]), None,
-                m, n, k, 4, None, 0, nv.ptr(status), stream())
+                m, n, k, impl, None, 0, nv.ptr(status), stream())
         torch.cuda.synchronize()
         assert int(status.item()) == 0
         assert_gemm_close(f32(y8), want8, exact_fraction=0.97, what=f"pair fp8 {shape}")
