@@ -1109,8 +1109,12 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   // tiles: prefill-sized token counts with a contraction of up to 4096 (w13, in-projection, qkv: +5..10 % in
   // the persistent form; at K = 8192, 128 tiles, both forms lose to the single CTA by their last round), and
   // the LM head of a full decode batch (+8 %, one-tile form).
+  // Inside a dependent-launch chain (a captured decode step) only the LM head of a 129..256-row batch takes
+  // pairs: a 512-row decode step whose projections ran as pairs stopped making progress (the step probe did
+  // not finish within its 100 s; the GPU stayed usable), and the cause was not found by reading, so that
+  // combination stays off. Prefill and scoring launch outside such chains.
   const bool pair_auto = force_splits == 0 && N % (2 * UM) == 0 &&
-                         ((M > 256 && K <= 4096) || (M > 128 && M <= 256 && N / (2 * UM) >= 148));
+                         ((M > 256 && K <= 4096 && !g_pdl_enabled) || (M > 128 && M <= 256 && N / (2 * UM) >= 148));
   if (force_splits == -2 || force_splits == -3 || pair_auto) {
     CGYM_REQUIRE(N % (2 * UM) == 0, "gemm(pair): the feature count must be a multiple of 256");
     CUtensorMap mw, mx;
