@@ -416,41 +416,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
         if (ep.partial) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) part[(c * 32 + j) * UM + n_local] = live ? __uint_as_float(v[j]) : 0.0f;
-        } else if (wide) {
-#pragma unroll
-          for (int j0 = 0; j0 < 32; j0 += 8) {
-            // the scales of eight rows are read before the first store of the group: the compiler cannot tell
-            // that the stores below leave row_scale alone, and would order every read behind the store before it
-            float xs[8];
-            *reinterpret_cast<float4*>(&xs[0]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0]);
-            *reinterpret_cast<float4*>(&xs[4]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0 + 4]);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float val = live ? __uint_as_float(v[j0 + j]) : 0.0f;
-              if (scaled) val = __fmul_rn(__fmul_rn(val, xs[j]), ws);
-              stage[(j0 + j) * 32 + lane] = __float2bfloat16_rn(val);
-            }
-          }
-          __syncwarp();
-          // four lanes per token row (8 features = 16 bytes each), eight rows per pass
-#pragma unroll
-          for (int pass = 0; pass < 4; ++pass) {
-            const int row = pass * 8 + (lane >> 2);
-            const uint4 word = *reinterpret_cast<const uint4*>(stage + row * 32 + (lane & 3) * 8);
-            const int out_row = row_out[c * 32 + row];
-            if (out_row >= 0)
-              *reinterpret_cast<uint4*>(ep.y + static_cast<int64_t>(out_row) * ep.N + n0 + f * UM + quarter * 32 + (lane & 3) * 8) = word;
-          }
-          __syncwarp();
-        } else if (n < ep.N) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int out_row = row_out[c * 32 + j];
-            if (out_row < 0) continue;
-            float val = live ? __uint_as_float(v[j]) : 0.0f;
-            if (scaled) val = __fmul_rn(__fmul_rn(val, row_scale[c * 32 + j]), ws);
-            ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
-          }
+        } else {
+          store_block(ep, v, c, n, n0 + f * UM + quarter * 32, lane, wide, scaled, ws, stage, row_out, row_scale);
         }
       };
       // A TMEM load and its wait cost about half a microsecond back to back, whatever the width. A CTA that
@@ -464,7 +431,12 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_con
         uint32_t v[GROUP][32];
 #pragma unroll
         for (int g = 0; g < GROUP; ++g) {
-          if (live) tmem_issue32(chunk_addr(i + g), v[g]);
+          if (live) {
+            tmem_issue32(chunk_addr(i + g), v[g]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[g][j] = 0u;
+          }
         }
         if (live) {
 #pragma unroll
@@ -560,6 +532,51 @@ __device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t da, uint64_t
 }
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// One block of 32 token columns of an accumulator (lane = feature n, v[j] = token row c * 32 + j of the tile) to y:
+// scaled, rounded to bf16, transposed through a [32 tokens][32 features] staging block of the warp and written as
+// 16-byte row segments when `wide` (the tile lies inside y and rows are 16-byte aligned), element by element
+// otherwise. row_out / row_scale are the tile's staged row metadata (shared memory).
+__device__ __forceinline__ void store_block(const GemmEpilogue& ep, const uint32_t (&v)[32], int c, int n, int n_base,
+                                            int lane, bool wide, bool scaled, float ws, __nv_bfloat16* stage,
+                                            const int32_t* row_out, const float* row_scale) {
+  if (wide) {
+#pragma unroll
+    for (int j0 = 0; j0 < 32; j0 += 8) {
+      // the scales of eight rows are read before the first store of the group: the compiler cannot tell that
+      // the stores below leave row_scale alone, and would order every read behind the store before it
+      float xs[8];
+      *reinterpret_cast<float4*>(&xs[0]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0]);
+      *reinterpret_cast<float4*>(&xs[4]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0 + 4]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float val = __uint_as_float(v[j0 + j]);
+        if (scaled) val = __fmul_rn(__fmul_rn(val, xs[j]), ws);
+        stage[(j0 + j) * 32 + lane] = __float2bfloat16_rn(val);
+      }
+    }
+    __syncwarp();
+    // four lanes per token row (8 features = 16 bytes each), eight rows per pass
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int row = pass * 8 + (lane >> 2);
+      const uint4 word = *reinterpret_cast<const uint4*>(stage + row * 32 + (lane & 3) * 8);
+      const int out_row = row_out[c * 32 + row];
+      if (out_row >= 0)
+        *reinterpret_cast<uint4*>(ep.y + static_cast<int64_t>(out_row) * ep.N + n_base + (lane & 3) * 8) = word;
+    }
+    __syncwarp();
+  } else if (n < ep.N) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int out_row = row_out[c * 32 + j];
+      if (out_row < 0) continue;
+      float val = __uint_as_float(v[j]);
+      if (scaled) val = __fmul_rn(__fmul_rn(val, row_scale[c * 32 + j]), ws);
+      ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
+    }
+  }
 }
 
 constexpr int PAIR_TOKENS = 256;  // token tile of a pair
@@ -694,39 +711,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       const bool live = n_kb > 0;
       __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem_raw + (tiles - smem_u32(smem_raw))) + quarter * 1024;
       auto emit = [&](int c, const uint32_t (&v)[32]) {
-        if (wide) {
-#pragma unroll
-          for (int j0 = 0; j0 < 32; j0 += 8) {
-            float xs[8];
-            *reinterpret_cast<float4*>(&xs[0]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0]);
-            *reinterpret_cast<float4*>(&xs[4]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0 + 4]);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float val = __uint_as_float(v[j0 + j]);
-              if (scaled) val = __fmul_rn(__fmul_rn(val, xs[j]), ws);
-              stage[(j0 + j) * 32 + lane] = __float2bfloat16_rn(val);
-            }
-          }
-          __syncwarp();
-#pragma unroll
-          for (int pass = 0; pass < 4; ++pass) {
-            const int row = pass * 8 + (lane >> 2);
-            const uint4 word = *reinterpret_cast<const uint4*>(stage + row * 32 + (lane & 3) * 8);
-            const int out_row = row_out[c * 32 + row];
-            if (out_row >= 0)
-              *reinterpret_cast<uint4*>(ep.y + static_cast<int64_t>(out_row) * ep.N + n0 + quarter * 32 + (lane & 3) * 8) = word;
-          }
-          __syncwarp();
-        } else if (n < ep.N) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int out_row = row_out[c * 32 + j];
-            if (out_row < 0) continue;
-            float val = __uint_as_float(v[j]);
-            if (scaled) val = __fmul_rn(__fmul_rn(val, row_scale[c * 32 + j]), ws);
-            ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
-          }
-        }
+        store_block(ep, v, c, n, n0 + quarter * 32, lane, wide, scaled, ws, stage, row_out, row_scale);
       };
       constexpr int GROUP = PAIR_EPILOGUE_GROUP;  // blocks of 32 columns fetched per TMEM wait
 #pragma unroll 1
@@ -907,39 +892,7 @@ gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __
         uint32_t v[32];
         tmem_issue32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(b * UN + c * 32), v);
         tmem_wait32(v);
-        if (wide) {
-#pragma unroll
-          for (int j0 = 0; j0 < 32; j0 += 8) {
-            float xs[8];
-            *reinterpret_cast<float4*>(&xs[0]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0]);
-            *reinterpret_cast<float4*>(&xs[4]) = *reinterpret_cast<const float4*>(&row_scale[c * 32 + j0 + 4]);
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-              float val = __uint_as_float(v[j0 + jj]);
-              if (scaled) val = __fmul_rn(__fmul_rn(val, xs[jj]), ws);
-              stage[(j0 + jj) * 32 + lane] = __float2bfloat16_rn(val);
-            }
-          }
-          __syncwarp();
-#pragma unroll
-          for (int pass = 0; pass < 4; ++pass) {
-            const int row = pass * 8 + (lane >> 2);
-            const uint4 word = *reinterpret_cast<const uint4*>(stage + row * 32 + (lane & 3) * 8);
-            const int out_row = row_out[c * 32 + row];
-            if (out_row >= 0)
-              *reinterpret_cast<uint4*>(ep.y + static_cast<int64_t>(out_row) * ep.N + n0 + quarter * 32 + (lane & 3) * 8) = word;
-          }
-          __syncwarp();
-        } else if (n < ep.N) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int out_row = row_out[c * 32 + jj];
-            if (out_row < 0) continue;
-            float val = __uint_as_float(v[jj]);
-            if (scaled) val = __fmul_rn(__fmul_rn(val, row_scale[c * 32 + jj]), ws);
-            ep.y[static_cast<int64_t>(out_row) * ep.N + n] = __float2bfloat16_rn(val);
-          }
-        }
+        store_block(ep, v, c, n, n0 + quarter * 32, lane, wide, scaled, ws, stage, row_out, row_scale);
       }
       // this CTA's four warps have read the buffer: one arrival per CTA on the leader's barrier
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
