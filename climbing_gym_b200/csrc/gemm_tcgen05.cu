@@ -607,7 +607,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   // dependent-launch chain that became resident early would allocate TMEM columns and then wait for this grid,
   // while a late pair of this grid waits for those columns: a cycle of two unbounded waits. Without the trigger
   // the successor starts when every CTA of this grid has exited. (w13 of a 256-row decode step routed through
-  // this kernel with the trigger hung exactly so.)
+  // this kernel with the trigger hung; this cycle is the explanation that fits.)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
