@@ -775,7 +775,7 @@ def host_threads() -> int:
     return torch.get_num_threads()
 
 
-def cpu_baseline(workload: str, *, seconds_budget: float = 25.0, steps: int = 1, warmup: int = 0) -> dict:
+def cpu_baseline(workload: str, *, seconds_budget: float = 25.0, steps: int = 4, warmup: int = 0) -> dict:
     """The reference's own eager CPU engine (fp32, its CPU default) on a bounded sample of the workload;
     the numpy port of it when the reference is not staged. `warmup` untimed passes, then exactly `steps`
     timed passes; the number of sampled tokens per pass is cut down after the first pass if `steps` passes
