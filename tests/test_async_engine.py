@@ -330,3 +330,37 @@ def test_product_of_two_stop_automata_matches_when_either_does():
             assert (value >= 65536) == (va >= 65536 or vb >= 65536)
     with pytest.raises(ValueError, match="same vocabulary"):
         product_stop_table(first, build_token_sequence_table([(1,)], 9))
+
+
+def test_graph_capture_holds_the_cyclic_collector():
+    """decoder._quiet_collector: what is garbage is collected before a stream capture starts, the cyclic collector
+    stays off while the capture runs (a CUDA graph destroyed by it in the middle of a capture invalidates the
+    capture) and comes back afterwards, also when the capture raises."""
+    import gc
+    import weakref
+
+    from climbing_gym_b200.decoder import _quiet_collector
+
+    class Node:
+        pass
+
+    a, b = Node(), Node()
+    a.other, b.other = b, a  # a cycle: only the cyclic collector frees it
+    probe = weakref.ref(a)
+    del a, b
+    assert gc.isenabled()
+    with _quiet_collector():
+        assert probe() is None, "garbage is collected before the capture begins"
+        assert not gc.isenabled()
+    assert gc.isenabled()
+    with pytest.raises(RuntimeError):
+        with _quiet_collector():
+            raise RuntimeError("capture failed")
+    assert gc.isenabled()
+    gc.disable()
+    try:
+        with _quiet_collector():
+            pass
+        assert not gc.isenabled(), "a collector that was off stays off"
+    finally:
+        gc.enable()
