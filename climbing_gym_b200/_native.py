@@ -81,6 +81,7 @@ SIGNATURES = {
     "cgym_gemm": [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_fp8": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_gemm_scatter": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _L, _P, _P],
+    "cgym_gemm_plan": [_I, _I, _I, _I, _I, _I, _P],
     "cgym_gemm_fp8_scatter": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _L, _P, _P],
     "cgym_bf16_stream_pack": [_P, _P, _P, _L, _I, _P],
     "cgym_bf16_stream_unpack": [_P, _P, _P, _P, _L, _I, _P],

@@ -1051,13 +1051,17 @@ bool gemm_tcgen05_supports(int M, int N, int K, bool fp8, const void* x, const v
   return true;
 }
 
-int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_scales, const float* w_scales,
-                        const uint8_t* row_mask, const int32_t* row_map, int M, int N, int K, bool fp8,
-                        void* workspace, int64_t workspace_bytes, int32_t* status, int force_splits,
-                        cudaStream_t stream) {
-  CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
-               "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
-  CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
+// Which kernel, tile and grid a GEMM takes: a pure function of the shape, the operand type, the caller's
+// forcing code and whether the launch is part of a dependent-launch chain (a captured decode step).
+struct GemmPlan {
+  int kind;    // 0 = single-CTA tiles, 1 = CTA pairs (one tile per pair), 2 = persistent CTA pairs
+  int un;      // token tile (MMA N)
+  int fm;      // 128-feature sub-tiles per CTA (single-CTA tiles only)
+  int splits;  // K splits = cluster size along z (single-CTA tiles only)
+  int grid_x, grid_y;
+};
+
+static GemmPlan plan_gemm(int M, int N, int K, bool fp8, int force_splits, bool pdl) {
   // CTA pairs (256 features x 256 tokens per pair, unsplit) where they measured faster than the single-CTA
   // tiles: prefill-sized token counts with a contraction of up to 4096 (w13, in-projection, qkv: +5..10 % in
   // the persistent form; at K = 8192, 128 tiles, both forms lose to the single CTA by their last round), and
@@ -1067,21 +1071,13 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   // not finish within its 100 s; the GPU stayed usable), and the cause was not found by reading, so that
   // combination stays off. Prefill and scoring launch outside such chains.
   const bool pair_auto = force_splits == 0 && N % (2 * UM) == 0 &&
-                         ((M > 256 && K <= 4096 && !g_pdl_enabled) || (M > 128 && M <= 256 && N / (2 * UM) >= 148));
+                         ((M > 256 && K <= 4096 && !pdl) || (M > 128 && M <= 256 && N / (2 * UM) >= 148));
   if (force_splits == -2 || force_splits == -3 || pair_auto) {
-    CGYM_REQUIRE(N % (2 * UM) == 0, "gemm(pair): the feature count must be a multiple of 256");
-    CUtensorMap mw, mx;
-    if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
-    if (int rc = make_map(&mx, x, M, K, PAIR_HALF, fp8)) return rc;
-    GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, row_map, status, M, N, K, 0, nullptr};
-    const dim3 grid(N / UM, (M + PAIR_TOKENS - 1) / PAIR_TOKENS, 1);
+    const int grid_x = N / UM, grid_y = (M + PAIR_TOKENS - 1) / PAIR_TOKENS;
     // two rounds or more of tiles over the 74 SM pairs: the persistent form (epilogue under the next tile's main
     // loop); fewer tiles leave it idle in its last round and the one-tile form with two CTAs per SM is as fast
-    const bool persistent = pair_auto && M > 256 && static_cast<int>(grid.x / 2 * grid.y) >= 2 * 74;
-    if (force_splits == -3 || persistent)
-      return fp8 ? launch_pair_persistent<true>(mw, mx, ep, N / (2 * UM), grid.y, stream)
-                 : launch_pair_persistent<false>(mw, mx, ep, N / (2 * UM), grid.y, stream);
-    return fp8 ? launch_pair<true>(mw, mx, ep, grid, stream) : launch_pair<false>(mw, mx, ep, grid, stream);
+    const bool persistent = force_splits == -3 || (pair_auto && M > 256 && grid_x / 2 * grid_y >= 2 * 74);
+    return GemmPlan{persistent ? 2 : 1, PAIR_TOKENS, 1, 1, grid_x, grid_y};
   }
   // Token tile: the smallest that covers M up to 128; up to 256 rows (a full decode batch) tiles of 128
   // or 64 keep the weight-streaming layout (half-SM rings, split-K) - the other tiles' weight loads hit
@@ -1131,6 +1127,32 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   splits = splits >= 8 ? 8 : (splits >= 4 ? 4 : (splits >= 2 ? 2 : 1));  // cluster sizes the reduction is built for
   // every split must own at least one K slice
   while (splits > 1 && (splits - 1) * ((total_kb + splits - 1) / splits) >= total_kb) splits /= 2;
+  return GemmPlan{0, un, dual ? 2 : 1, splits, dual ? n_tiles / 2 : n_tiles, m_tiles};
+}
+
+int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_scales, const float* w_scales,
+                        const uint8_t* row_mask, const int32_t* row_map, int M, int N, int K, bool fp8,
+                        void* workspace, int64_t workspace_bytes, int32_t* status, int force_splits,
+                        cudaStream_t stream) {
+  CGYM_REQUIRE(gemm_tcgen05_supports(M, N, K, fp8, x, w),
+               "gemm(tcgen05): needs 16-byte aligned operands and a K row pitch that is a multiple of 16 bytes");
+  CGYM_REQUIRE(status != nullptr, "gemm(tcgen05): a status word is required");
+  const GemmPlan plan = plan_gemm(M, N, K, fp8, force_splits, g_pdl_enabled != 0);
+  if (plan.kind != 0) {
+    CGYM_REQUIRE(N % (2 * UM) == 0, "gemm(pair): the feature count must be a multiple of 256");
+    CUtensorMap mw, mx;
+    if (int rc = make_map(&mw, w, N, K, UM, fp8)) return rc;
+    if (int rc = make_map(&mx, x, M, K, PAIR_HALF, fp8)) return rc;
+    GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, row_map, status, M, N, K, 0, nullptr};
+    if (plan.kind == 2)
+      return fp8 ? launch_pair_persistent<true>(mw, mx, ep, N / (2 * UM), plan.grid_y, stream)
+                 : launch_pair_persistent<false>(mw, mx, ep, N / (2 * UM), plan.grid_y, stream);
+    const dim3 grid(plan.grid_x, plan.grid_y, 1);
+    return fp8 ? launch_pair<true>(mw, mx, ep, grid, stream) : launch_pair<false>(mw, mx, ep, grid, stream);
+  }
+  const int un = plan.un, splits = plan.splits;
+  const bool dual = plan.fm == 2, half_ring = un <= 128;
+  const int n_tiles = (N + UM - 1) / UM, m_tiles = plan.grid_y;
   // partial tiles go through the caller's workspace (L2) when it is large enough, else through DSMEM
   const int64_t split_bytes = static_cast<int64_t>(n_tiles) * m_tiles * splits * un * UM * 4;
   float* split_ws = nullptr;
@@ -1143,7 +1165,7 @@ int launch_gemm_tcgen05(void* y, const void* x, const void* w, const float* x_sc
   if (int rc = make_map(&mx, x, M, K, un, fp8)) return rc;
   GemmEpilogue ep{static_cast<__nv_bfloat16*>(y), x_scales, w_scales, row_mask, row_map, status, M, N, K,
                   splits > 1 ? 1 : 0, split_ws};
-  dim3 grid(dual ? n_tiles / 2 : n_tiles, m_tiles, splits);
+  dim3 grid(plan.grid_x, m_tiles, splits);
   int rc = 0;
 #define LAUNCH_UN(U, R)                                                                 \
   rc = fp8 ? launch_tile<U, true, R>(mw, mx, ep, grid, stream) : launch_tile<U, false, R>(mw, mx, ep, grid, stream)
@@ -1169,5 +1191,17 @@ extern "C" int cgym_test_gemm_wait(unsigned long long limit_ns, int drop_loads) 
   cudaError_t rc = cudaMemcpyToSymbol(g_wait_limit_ns, &limit, sizeof(limit));
   if (rc == cudaSuccess) rc = cudaMemcpyToSymbol(g_drop_loads, &drop, sizeof(drop));
   CGYM_REQUIRE(rc == cudaSuccess, "test_gemm_wait: %s", cudaGetErrorString(rc));
+  return 0;
+}
+
+extern "C" int cgym_gemm_plan(int M, int N, int K, int fp8, int impl, int in_dependent_chain, int* plan6) {
+  using namespace cgym;
+  CGYM_REQUIRE(M > 0 && N > 0 && K > 0 && plan6 != nullptr, "gemm_plan: bad arguments");
+  CGYM_REQUIRE(impl == 0 || (impl >= 2 && impl <= 5), "gemm_plan: impl must be 0 or 2..5 (the tcgen05 forms)");
+  const int force = impl == 3 ? 4 : (impl == 4 ? -2 : (impl == 5 ? -3 : 0));
+  CGYM_REQUIRE(force == 0 || force == 4 || N % (2 * UM) == 0, "gemm_plan: pairs need a feature count that is a multiple of 256");
+  const GemmPlan plan = plan_gemm(M, N, K, fp8 != 0, force, in_dependent_chain != 0);
+  plan6[0] = plan.kind, plan6[1] = plan.un, plan6[2] = plan.fm;
+  plan6[3] = plan.splits, plan6[4] = plan.grid_x, plan6[5] = plan.grid_y;
   return 0;
 }

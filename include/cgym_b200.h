@@ -188,6 +188,13 @@ int cgym_gemm(void* y, const void* x, const void* w, const uint8_t* row_mask, in
               int dtype, int impl, void* workspace, int64_t workspace_bytes, int32_t* status,
               cgym_stream_t stream);
 
+/* Which kernel and grid cgym_gemm / cgym_gemm_fp8 take for a shape, without launching anything
+ * (no reference counterpart; callable without a device). impl as in cgym_gemm (0 = auto, 2..5 = the tcgen05 forms);
+ * in_dependent_chain != 0 plans as inside a captured decode step (cgym_set_pdl(1)). plan6 receives
+ * {kind, token tile, feature sub-tiles per CTA, K splits, grid x, grid y}; kind 0 = single-CTA tiles,
+ * 1 = CTA pairs with one tile per pair, 2 = persistent CTA pairs. */
+int cgym_gemm_plan(int M, int N, int K, int fp8, int impl, int in_dependent_chain, int* plan6);
+
 /* cgym_gemm whose output rows are scattered: token row m is written to y row row_map[m] (int32[M]; negative =
  * not written; NULL = cgym_gemm). Replaces the compact decode graphs' _scatter_logits copy
  * (lfm25_batching.py:25-33, 96-101): the LM head of a step over a compacted set of rows writes each row's
