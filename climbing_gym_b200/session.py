@@ -627,6 +627,9 @@ class LFM25GenerationSession:
             tokens = self.state.tokens[:, :longest].index_select(0, index).cpu().tolist()
             logprobs = self.state.logprobs[:, :longest].index_select(0, index).cpu().tolist()
             queue["result_reasons"].index_fill_(0, index, 0)  # delivered: the result rows may be reused
+        # work launched from here on (a later request that lands in one of these result rows) is ordered
+        # behind that clearing; the read stream holds nothing else, so the caller's stream does not stall
+        torch.cuda.current_stream(dev).wait_stream(self._read_stream)
         results = []
         for rid, length, ids, probs in zip(done, lengths, tokens, logprobs):
             prompt, sampling, _ = self._queued.pop(rid)
